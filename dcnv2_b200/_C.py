@@ -1,0 +1,146 @@
+"""Drop-in for the reference's ``Conv2d._C`` extension module (ext.cpp:15-18).
+
+``dcn_v2_forward`` and ``dcn_v2_backward`` keep the reference's positional
+signatures (name.h:15-36) and add optional trailing ``dilation_h, dilation_w,
+deformable_groups`` (default 1).  Tensors are handed to ``libdcn_b200.so``
+through its C ABI; outputs and the workspace come from PyTorch's caching
+allocator on the tensors' device, and the work is queued on the current CUDA
+stream, as the reference does (com.cu:215, 748).
+
+Errors follow the reference: a CPU tensor raises ``RuntimeError("<name> must be a
+CUDA tensor")`` (com.cu:209-213), a channel mismatch raises ``RuntimeError``
+(com.cu:760-761), and a failing library call raises ``RuntimeError`` with the
+library's message (com.cu:266-270).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import List, Optional
+
+import torch
+
+from . import _lib
+
+# DCN_CHECK=1: synchronise after every call and raise on device-side error bits
+_CHECK = os.environ.get("DCN_CHECK", "0") not in ("", "0")
+
+_DTYPES = {torch.float32: _lib.DCN_F32, torch.float16: _lib.DCN_F16, torch.bfloat16: _lib.DCN_BF16}
+
+
+def _check_cuda(**tensors):
+    for name, t in tensors.items():
+        if t is not None and not t.is_cuda:
+            raise RuntimeError(f"{name} must be a CUDA tensor")
+
+
+def _desc(input, weight, stride_h, stride_w, pad_h, pad_w, dil_h, dil_w, dg, has_bias):
+    if input.dim() != 4 or weight.dim() != 4:
+        raise RuntimeError("input and weight must be 4-D (NCHW / [Co, C, kh, kw])")
+    B, C, H, W = input.shape
+    Co, Cw, kh, kw = weight.shape
+    if C != Cw:
+        raise RuntimeError(f"Input shape and kernel channels wont match: ({C} vs {Cw}).")
+    if input.dtype not in _DTYPES:
+        raise RuntimeError(f"unsupported dtype {input.dtype}")
+    d = _lib.DcnDesc(B, C, H, W, Co, kh, kw, int(stride_h), int(stride_w), int(pad_h), int(pad_w),
+                     int(dil_h), int(dil_w), int(dg), _DTYPES[input.dtype], 1 if has_bias else 0)
+    Ho, Wo = ctypes.c_int32(), ctypes.c_int32()
+    rc = _lib.lib.dcn_output_size(ctypes.byref(d), ctypes.byref(Ho), ctypes.byref(Wo))
+    if rc != _lib.DCN_OK:
+        raise RuntimeError(f"dcn: {_lib.strerror(rc)}")
+    return d, Ho.value, Wo.value
+
+
+def _prep(t, dtype, name, shape=None):
+    if t.dtype != dtype:
+        raise RuntimeError(f"{name} must have dtype {dtype}, got {t.dtype}")
+    if shape is not None and tuple(t.shape) != tuple(shape):
+        raise RuntimeError(f"{name} has shape {tuple(t.shape)}, expected {tuple(shape)}")
+    return t.contiguous()
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr() if t is not None and t.numel() > 0 else 0)
+
+
+def _check_device(ws):
+    st = read_device_status(ws)
+    if st != 0:
+        raise RuntimeError(f"dcn: kernel reported device error bits {st:#x} (pipeline wait timed out)")
+
+
+def _check(rc):
+    if rc != _lib.DCN_OK:
+        raise RuntimeError(f"dcn: {_lib.strerror(rc)}")
+
+
+def dcn_v2_forward(input: torch.Tensor, weight: torch.Tensor, mask: torch.Tensor,
+                   offset: torch.Tensor, bias: Optional[torch.Tensor], stride_h: int, stride_w: int,
+                   pad_h: int, pad_w: int, dilation_h: int = 1, dilation_w: int = 1,
+                   deformable_groups: int = 1) -> torch.Tensor:
+    """Output [B, Co, Ho, Wo] of modulated deformable convolution (MyDCN_forward)."""
+    _check_cuda(input=input, weight=weight, bias=bias, offset=offset, mask=mask)
+    d, Ho, Wo = _desc(input, weight, stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w,
+                      deformable_groups, bias is not None)
+    B, dg, K2 = input.shape[0], deformable_groups, weight.shape[2] * weight.shape[3]
+    dt = input.dtype
+    input = input.contiguous()
+    weight = _prep(weight, dt, "weight")
+    offset = _prep(offset, dt, "offset", (B, 2 * dg * K2, Ho, Wo))
+    mask = _prep(mask, dt, "mask", (B, dg * K2, Ho, Wo))
+    if bias is not None:
+        bias = _prep(bias, dt, "bias", (weight.shape[0],))
+    with torch.cuda.device(input.device):
+        out = torch.empty((B, weight.shape[0], Ho, Wo), dtype=dt, device=input.device)
+        nbytes = _lib.lib.dcn_forward_workspace_size(ctypes.byref(d))
+        ws = torch.empty((max(nbytes, 256),), dtype=torch.uint8, device=input.device)
+        stream = torch.cuda.current_stream(input.device).cuda_stream
+        _check(_lib.lib.dcn_forward(ctypes.byref(d), _ptr(input), _ptr(weight), _ptr(mask),
+                                    _ptr(offset), _ptr(bias), _ptr(out), _ptr(ws), ws.numel(),
+                                    ctypes.c_void_p(stream)))
+        if _CHECK:
+            _check_device(ws)
+    return out
+
+
+def dcn_v2_backward(input: torch.Tensor, weight: torch.Tensor, mask: torch.Tensor,
+                    offset: torch.Tensor, bias: Optional[torch.Tensor], grad_output: torch.Tensor,
+                    stride_h: int, stride_w: int, pad_h: int, pad_w: int, dilation_h: int = 1,
+                    dilation_w: int = 1, deformable_groups: int = 1) -> List[torch.Tensor]:
+    """[grad_input, grad_offset, grad_mask, grad_weight, grad_bias] (MyDCN_backward order)."""
+    _check_cuda(input=input, weight=weight, bias=bias, offset=offset, mask=mask,
+                grad_output=grad_output)
+    has_bias = bias is not None
+    d, Ho, Wo = _desc(input, weight, stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w,
+                      deformable_groups, True)
+    B, dg, K2 = input.shape[0], deformable_groups, weight.shape[2] * weight.shape[3]
+    Co = weight.shape[0]
+    dt = input.dtype
+    input = input.contiguous()
+    weight = _prep(weight, dt, "weight")
+    offset = _prep(offset, dt, "offset", (B, 2 * dg * K2, Ho, Wo))
+    mask = _prep(mask, dt, "mask", (B, dg * K2, Ho, Wo))
+    grad_output = _prep(grad_output, dt, "grad_output", (B, Co, Ho, Wo))
+    with torch.cuda.device(input.device):
+        gi = torch.empty_like(input)
+        goff = torch.empty_like(offset)
+        gm = torch.empty_like(mask)
+        gw = torch.empty_like(weight)
+        gb = torch.empty((Co,), dtype=dt, device=input.device)
+        nbytes = _lib.lib.dcn_backward_workspace_size(ctypes.byref(d))
+        ws = torch.empty((max(nbytes, 256),), dtype=torch.uint8, device=input.device)
+        stream = torch.cuda.current_stream(input.device).cuda_stream
+        _check(_lib.lib.dcn_backward(ctypes.byref(d), _ptr(input), _ptr(weight), _ptr(mask),
+                                     _ptr(offset), _ptr(bias), _ptr(grad_output), _ptr(gi),
+                                     _ptr(goff), _ptr(gm), _ptr(gw), _ptr(gb), _ptr(ws),
+                                     ws.numel(), ctypes.c_void_p(stream)))
+        if _CHECK:
+            _check_device(ws)
+    return [gi, goff, gm, gw, gb if has_bias else None]
+
+
+def read_device_status(workspace: torch.Tensor) -> int:
+    """Synchronises the current stream and returns (and clears) the device error bits."""
+    stream = torch.cuda.current_stream(workspace.device).cuda_stream
+    return int(_lib.lib.dcn_read_device_status(_ptr(workspace), ctypes.c_void_p(stream)))

@@ -1,0 +1,278 @@
+// C ABI of libdcn_b200 (declared in include/dcn_b200.h): problem planning,
+// workspace layout and the launch sequences of forward and backward.
+#include <cuda_runtime.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "dcn_b200.h"
+#include "dcn_kernels.h"
+#include "dcn_plan.h"
+
+namespace dcn {
+
+namespace {
+
+int device_sms() {
+  static int cached[64];
+  static std::once_flag flags[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  std::call_once(flags[dev], [dev] {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    cached[dev] = n;
+  });
+  return cached[dev];
+}
+
+// Backward-weight work split: M tiles per CTA and units per CTA, chosen to
+// reuse each gathered column across as many Co rows as TMEM holds, with at
+// least two pipeline stages in shared memory.
+void plan_weight_grad(Plan* p, int num_sms) {
+  const size_t aTile = 128 * 128;
+  int best_m = 1, best_u = 1;
+  for (int m = p->nMT; m >= 1; --m) {
+    int u = 512 / (m * p->NC);
+    if (u < 1) continue;
+    if (u > p->nU) u = p->nU;
+    // balance the unit sets
+    const int nsets = ceil_div(p->nU, u);
+    u = ceil_div(p->nU, nsets);
+    while (u >= 1) {
+      const size_t stage = (size_t)p->nsplit * (m * aTile + (size_t)u * p->NC * 128);
+      if (2 * stage + 1024 <= kBwdSmemBudget) break;
+      --u;
+    }
+    if (u >= 1) {
+      best_m = m;
+      best_u = u;
+      break;
+    }
+  }
+  p->wg_mt_per_cta = best_m;
+  p->wg_ncg = ceil_div(p->nMT, best_m);
+  p->wg_units_per_set = best_u;
+  p->wg_nsets = ceil_div(p->nU, best_u);
+  p->wg_ksteps = (int)((p->totalP + 63) / 64);
+  const int base = p->wg_ncg * p->wg_nsets;
+  int ns = num_sms / base;
+  if (ns < 1) ns = 1;
+  if (ns > p->wg_ksteps) ns = p->wg_ksteps;
+  if (ns < 1) ns = 1;
+  p->wg_nsplit_px = ns;
+}
+
+}  // namespace
+
+int make_plan(const dcn_desc* d, Plan* p, int num_sms) {
+  if (d == nullptr || p == nullptr) return DCN_E_NULLPTR;
+  memset(p, 0, sizeof(*p));
+  if (d->B < 0 || d->C <= 0 || d->H <= 0 || d->W <= 0 || d->Co <= 0 || d->kh <= 0 ||
+      d->kw <= 0 || d->sh <= 0 || d->sw <= 0 || d->ph < 0 || d->pw < 0 || d->dh <= 0 ||
+      d->dw <= 0 || d->dg <= 0 || d->C % d->dg != 0)
+    return DCN_E_INVALID;
+  if (d->dtype != DCN_F32 && d->dtype != DCN_F16 && d->dtype != DCN_BF16) return DCN_E_INVALID;
+  p->B = d->B; p->C = d->C; p->H = d->H; p->W = d->W; p->Co = d->Co;
+  p->kh = d->kh; p->kw = d->kw; p->sh = d->sh; p->sw = d->sw; p->ph = d->ph; p->pw = d->pw;
+  p->dh = d->dh; p->dw = d->dw; p->dg = d->dg; p->dtype = d->dtype; p->has_bias = d->has_bias;
+  const long long ho = ((long long)d->H + 2LL * d->ph - ((long long)d->dh * (d->kh - 1) + 1)) / d->sh + 1;
+  const long long wo = ((long long)d->W + 2LL * d->pw - ((long long)d->dw * (d->kw - 1) + 1)) / d->sw + 1;
+  if (ho <= 0 || wo <= 0) return DCN_E_INVALID;
+  if (ho * wo > (1LL << 30) || (long long)d->H * d->W > (1LL << 30)) return DCN_E_UNSUPPORTED;
+  p->Ho = (int)ho; p->Wo = (int)wo; p->HoWo = (int)(ho * wo);
+  p->K2 = d->kh * d->kw;
+  p->totalP = (long long)d->B * p->HoWo;
+  p->Cg = d->C / d->dg;
+  p->Cgp = ceil_div(p->Cg, kChunk) * kChunk;
+  p->nCB = p->Cgp / kChunk;
+  p->CS = d->dg * p->Cgp;
+  p->esz = d->dtype == DCN_F32 ? 4 : 2;
+  p->xesz = p->esz;
+  p->nsplit = d->dtype == DCN_F32 ? 2 : 1;
+  // forward
+  p->nK = p->K2 * d->dg * p->nCB;
+  p->nCoT = ceil_div(d->Co, 256);
+  p->NT = ceil_div(ceil_div(d->Co, p->nCoT), 16) * 16;
+  p->nPT = (int)((p->totalP + kTileM - 1) / kTileM);
+  // backward data
+  p->Cop = ceil_div(d->Co, kChunk) * kChunk;
+  p->nKo = p->Cop / kChunk;
+  p->NC = p->Cgp < 256 ? p->Cgp : 256;
+  p->nCC = ceil_div(p->Cgp, p->NC);
+  p->nU = p->K2 * d->dg * p->nCC;
+  // backward weight
+  p->nMT = ceil_div(d->Co, 128);
+  plan_weight_grad(p, num_sms);
+  // packed tiles
+  p->wf_tile_bytes = (size_t)p->nsplit * p->NT * 128;
+  p->wd_tile_bytes = (size_t)p->nsplit * p->NC * 128;
+  // workspace layout
+  size_t off = 0;
+  p->off_status = off; off += kWsAlign;
+  p->off_x = off; off = align_up(off + (size_t)d->B * d->H * d->W * p->CS * p->xesz, kWsAlign);
+  const size_t common = off;
+  p->off_wf = off; off = align_up(off + (size_t)p->nCoT * p->nK * p->wf_tile_bytes, kWsAlign);
+  p->fwd_bytes = off;
+  off = common;
+  p->off_wd = off; off = align_up(off + (size_t)p->nU * p->nKo * p->wd_tile_bytes, kWsAlign);
+  p->off_gx = off; off = align_up(off + (size_t)d->B * d->H * d->W * p->CS * 4, kWsAlign);
+  p->off_gw = off; off = align_up(off + (size_t)d->Co * p->K2 * p->CS * 4, kWsAlign);
+  p->off_gb = off; off = align_up(off + (size_t)d->Co * 4, kWsAlign);
+  p->bwd_bytes = off;
+  return DCN_OK;
+}
+
+}  // namespace dcn
+
+using namespace dcn;
+
+namespace {
+
+bool aligned16(const void* ptr) { return ((uintptr_t)ptr & 15u) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+int dcn_output_size(const dcn_desc* d, int32_t* Ho, int32_t* Wo) {
+  Plan p;
+  const int rc = make_plan(d, &p, 148);
+  if (rc != DCN_OK) return rc;
+  if (Ho) *Ho = p.Ho;
+  if (Wo) *Wo = p.Wo;
+  return DCN_OK;
+}
+
+size_t dcn_forward_workspace_size(const dcn_desc* d) {
+  Plan p;
+  return make_plan(d, &p, 148) == DCN_OK ? p.fwd_bytes : 0;
+}
+
+size_t dcn_backward_workspace_size(const dcn_desc* d) {
+  Plan p;
+  return make_plan(d, &p, 148) == DCN_OK ? p.bwd_bytes : 0;
+}
+
+int dcn_forward(const dcn_desc* d, const void* input, const void* weight, const void* mask,
+                const void* offset, const void* bias, void* output, void* workspace,
+                size_t workspace_bytes, void* stream) {
+  Plan P;
+  int rc = make_plan(d, &P, device_sms());
+  if (rc != DCN_OK) return rc;
+  if (!workspace) return DCN_E_NULLPTR;
+  if (workspace_bytes < P.fwd_bytes || ((uintptr_t)workspace & (kWsAlign - 1)) != 0)
+    return DCN_E_WORKSPACE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (cudaMemsetAsync(ws + P.off_status, 0, sizeof(int), s) != cudaSuccess) return DCN_E_CUDA;
+  if (P.totalP == 0) return DCN_OK;
+  if (!input || !weight || !mask || !offset || !output) return DCN_E_NULLPTR;
+  if (d->has_bias && !bias) return DCN_E_NULLPTR;
+  if ((rc = launch_pack_input(P, input, ws + P.off_x, s)) != DCN_OK) return rc;
+  if ((rc = launch_pack_weight_fwd(P, weight, ws + P.off_wf, s)) != DCN_OK) return rc;
+  FwdArgs a;
+  memset(&a, 0, sizeof(a));
+  a.plan = P;
+  a.xt = ws + P.off_x;
+  a.offset = offset;
+  a.mask = mask;
+  a.wpk = ws + P.off_wf;
+  a.bias = d->has_bias ? bias : nullptr;
+  a.out = output;
+  a.err = reinterpret_cast<int*>(ws + P.off_status);
+  a.num_sms = device_sms();
+  return launch_forward(a, s);
+}
+
+int dcn_backward(const dcn_desc* d, const void* input, const void* weight, const void* mask,
+                 const void* offset, const void* bias, const void* grad_output, void* grad_input,
+                 void* grad_offset, void* grad_mask, void* grad_weight, void* grad_bias,
+                 void* workspace, size_t workspace_bytes, void* stream) {
+  (void)bias;
+  Plan P;
+  int rc = make_plan(d, &P, device_sms());
+  if (rc != DCN_OK) return rc;
+  if (!input || !weight || !mask || !offset || !grad_output || !grad_input || !grad_offset ||
+      !grad_mask || !grad_weight || !workspace)
+    return DCN_E_NULLPTR;
+  if (d->has_bias && !grad_bias) return DCN_E_NULLPTR;
+  if (workspace_bytes < P.bwd_bytes || ((uintptr_t)workspace & (kWsAlign - 1)) != 0)
+    return DCN_E_WORKSPACE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  float* gxn = reinterpret_cast<float*>(ws + P.off_gx);
+  float* gw = reinterpret_cast<float*>(ws + P.off_gw);
+  float* gb = reinterpret_cast<float*>(ws + P.off_gb);
+  if (cudaMemsetAsync(ws + P.off_status, 0, sizeof(int), s) != cudaSuccess) return DCN_E_CUDA;
+  // gx, gw and gb accumulators are contiguous: one memset
+  if (cudaMemsetAsync(ws + P.off_gx, 0, P.bwd_bytes - P.off_gx, s) != cudaSuccess) return DCN_E_CUDA;
+  if (P.totalP == 0) {
+    if ((rc = launch_finish_grad_weight(P, gw, gb, grad_weight, d->has_bias ? grad_bias : nullptr, s)) != DCN_OK)
+      return rc;
+    if (P.B > 0) return launch_finish_grad_input(P, gxn, grad_input, s);
+    return DCN_OK;
+  }
+  if ((rc = launch_pack_input(P, input, ws + P.off_x, s)) != DCN_OK) return rc;
+  if ((rc = launch_pack_weight_bwd(P, weight, ws + P.off_wd, s)) != DCN_OK) return rc;
+  BwdDataArgs a;
+  memset(&a, 0, sizeof(a));
+  a.plan = P;
+  a.xt = ws + P.off_x;
+  a.offset = offset;
+  a.mask = mask;
+  a.gout = grad_output;
+  a.wpk = ws + P.off_wd;
+  a.gx_nhwc = gxn;
+  a.goffset = grad_offset;
+  a.gmask = grad_mask;
+  a.err = reinterpret_cast<int*>(ws + P.off_status);
+  a.num_sms = device_sms();
+  a.vec_gout = aligned16(grad_output);
+  if ((rc = launch_backward_data(a, s)) != DCN_OK) return rc;
+  BwdWeightArgs w;
+  memset(&w, 0, sizeof(w));
+  w.plan = P;
+  w.xt = ws + P.off_x;
+  w.offset = offset;
+  w.mask = mask;
+  w.gout = grad_output;
+  w.gw = gw;
+  w.gb = d->has_bias ? gb : nullptr;
+  w.err = a.err;
+  w.num_sms = a.num_sms;
+  w.vec_gout = aligned16(grad_output);
+  if ((rc = launch_backward_weight(w, s)) != DCN_OK) return rc;
+  if ((rc = launch_finish_grad_input(P, gxn, grad_input, s)) != DCN_OK) return rc;
+  return launch_finish_grad_weight(P, gw, gb, grad_weight, d->has_bias ? grad_bias : nullptr, s);
+}
+
+int dcn_read_device_status(void* workspace, void* stream) {
+  if (!workspace) return DCN_E_NULLPTR;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int h = 0;
+  if (cudaMemcpyAsync(&h, workspace, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess)
+    return DCN_E_CUDA;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return DCN_E_CUDA;
+  if (cudaMemsetAsync(workspace, 0, sizeof(int), s) != cudaSuccess) return DCN_E_CUDA;
+  return h;
+}
+
+const char* dcn_strerror(int code) {
+  switch (code) {
+    case DCN_OK: return "ok";
+    case DCN_E_INVALID: return "invalid shape or parameter";
+    case DCN_E_NULLPTR: return "required pointer is NULL";
+    case DCN_E_WORKSPACE: return "workspace too small or not 256-byte aligned";
+    case DCN_E_CUDA: return "CUDA runtime error";
+    case DCN_E_UNSUPPORTED: return "unsupported configuration";
+    case DCN_E_DEVICE: return "error recorded by a kernel";
+    default: return "unknown error";
+  }
+}
+
+const char* dcn_version(void) { return "dcn_b200 0.1.0 sm_100a"; }
+
+}  // extern "C"

@@ -1,0 +1,356 @@
+// Shared device helpers for the sm_100a DCNv2 kernels: mbarriers with bounded
+// waits, bulk (TMA) copies, tcgen05 (UMMA) descriptors / MMA / TMEM access, and
+// element conversions.  Every wait on an mbarrier gives up after
+// DCN_WAIT_TIMEOUT_NS, records DCN_DEVERR_TIMEOUT in the caller's error word and
+// raises a CTA-wide abort flag, so a broken pipeline ends the kernel instead of
+// hanging the GPU.
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "dcn_b200.h"
+
+#ifndef DCN_WAIT_TIMEOUT_NS
+#define DCN_WAIT_TIMEOUT_NS 4000000000ull  // 4 s: far above any legitimate wait
+#endif
+
+namespace dcn {
+
+// ---------------------------------------------------------------- basics
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void raise_error(int* err, int code) {
+  if (err) atomicOr(err, code);
+}
+
+// ---------------------------------------------------------------- mbarrier
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Waits for the phase of parity `parity` to complete.  Returns false (and
+// records a timeout) when the wait exceeds DCN_WAIT_TIMEOUT_NS or when another
+// warp of the CTA has already aborted.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err,
+                                          volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > DCN_WAIT_TIMEOUT_NS) {
+      raise_error(err, DCN_DEVERR_TIMEOUT);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+
+// Bounded wait used during teardown: ignores the abort flag (the barrier is
+// still expected to complete) but never spins longer than the timeout.
+__device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity, int* err) {
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer() - t0 > DCN_WAIT_TIMEOUT_NS) {
+      raise_error(err, DCN_DEVERR_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+
+// Orders this thread's generic-proxy shared-memory writes before later
+// async-proxy (tensor core / TMA) reads of the same bytes.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---------------------------------------------------------------- bulk copy (TMA engine)
+// Untiled bulk copy global -> shared; completion is signalled as tx bytes on `bar`.
+// Source and destination 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
+                                         uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+// ---------------------------------------------------------------- tcgen05 / TMEM
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, one CTA, kind::f16 (f16 or bf16 operands, f32 accumulate).
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives once on `bar` when every tcgen05.mma issued so far by this thread has completed.
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+      : "memory");
+}
+
+// 32 lanes x 32 bit, 16 consecutive columns per thread.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 32 lanes x 32 bit, 8 consecutive columns per thread.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor, 128-byte swizzle (Swizzle<3,4,3>), sm_100 format:
+// start address [0,14), leading byte offset [16,30), stride byte offset [32,46),
+// version 1 at [46,48), layout type 2 (SWIZZLE_128B) at [61,64).  All >> 4.
+//   K-major : rows of 128 B (64 16-bit elements of K); SBO = 1024 B between
+//             8-row groups; LBO unused.
+//   MN-major: rows of 128 B (64 16-bit elements of M or N) per K index;
+//             SBO = byte stride between groups of 8 K rows, LBO = byte stride
+//             between 64-element M/N atoms.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo_bytes,
+                                               uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// Instruction descriptor for kind::f16: f32 accumulator, A/B format (0 f16, 1 bf16),
+// major-ness of A and B (0 K-major, 1 MN-major), M and N.
+__host__ __device__ constexpr uint32_t make_idesc(int bf16, int a_mn, int b_mn, int M, int N) {
+  return (1u << 4) | ((uint32_t)bf16 << 7) | ((uint32_t)bf16 << 10) | ((uint32_t)a_mn << 15) |
+         ((uint32_t)b_mn << 16) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// Byte offset of 16-byte chunk `c` (0..7) of row `r` inside a 1024-byte aligned
+// SW128 tile whose rows are 128 B apart.
+__device__ __forceinline__ uint32_t sw128_off(uint32_t r, uint32_t c) {
+  return r * 128u + ((c ^ (r & 7u)) << 4);
+}
+
+// ---------------------------------------------------------------- element types
+template <typename T>
+struct Elem;
+template <>
+struct Elem<float> {
+  static __device__ __forceinline__ float to_f(float v) { return v; }
+  static __device__ __forceinline__ float from_f(float v) { return v; }
+};
+template <>
+struct Elem<__half> {
+  static __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+  static __device__ __forceinline__ __half from_f(float v) { return __float2half_rn(v); }
+};
+template <>
+struct Elem<__nv_bfloat16> {
+  static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  static __device__ __forceinline__ __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+};
+
+template <typename T>
+__device__ __forceinline__ float ldf(const T* p) {
+  return Elem<T>::to_f(*p);
+}
+
+// Operand type fed to the tensor core for an input type: f16 stays f16; bf16 and
+// f32 (as a bf16 hi/lo pair) run on bf16.
+template <typename T>
+struct OpOf {
+  static constexpr int kBF16 = 1;
+  static constexpr bool kSplit = false;
+};
+template <>
+struct OpOf<float> {
+  static constexpr int kBF16 = 1;
+  static constexpr bool kSplit = true;
+};
+template <>
+struct OpOf<__half> {
+  static constexpr int kBF16 = 0;
+  static constexpr bool kSplit = false;
+};
+
+// Packs two floats into the 16-bit operand type (bf16 when kBF16, else f16).
+template <int kBF16>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  if constexpr (kBF16) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  } else {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+}
+
+// bf16 hi/lo split of two floats: a ~= hi + lo with |a - hi - lo| <= 2^-17 |a|.
+__device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  float2 hf = __bfloat1622float2(h);
+  __nv_bfloat162 l = __floats2bfloat162_rn(a - hf.x, b - hf.y);
+  hi = *reinterpret_cast<uint32_t*>(&h);
+  lo = *reinterpret_cast<uint32_t*>(&l);
+}
+
+// Unpacks 8 packed 16-bit values (one uint4) into floats.
+template <typename T>
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if constexpr (std::is_same<T, __half>::value) {
+      __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+      float2 x = __half22float2(h);
+      f[2 * i] = x.x;
+      f[2 * i + 1] = x.y;
+    } else {
+      __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[i]);
+      float2 x = __bfloat1622float2(h);
+      f[2 * i] = x.x;
+      f[2 * i + 1] = x.y;
+    }
+  }
+}
+
+__device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ void sts_v4(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+
+// Vector fp32 reduction into global memory (sm_90+).
+__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
+               "f"(d)
+               : "memory");
+}
+
+// ---------------------------------------------------------------- sampling geometry
+// Bilinear sampling geometry of one (pixel, tap, group): the four corner
+// weights (already multiplied by the modulation mask; zero for corners outside
+// the image) and the corner pixel indices.  Follows the reference's validity
+// rule -1 < h < H, -1 < w < W and per-corner zero padding (com.cu:119-148, 187).
+struct Sample {
+  float h, w;        // sample position
+  float lh, lw;      // fractional parts
+  float m;           // modulation mask
+  float cw[4];       // corner weights * mask (0 for corners outside the image)
+  int cidx[4];       // corner pixel index h*W + w (valid only when cw != 0 or flag set)
+  uint32_t cvalid;   // bit i: corner i inside the image
+  bool inside;       // -1 < h < H and -1 < w < W
+};
+
+__device__ __forceinline__ Sample make_sample(float h, float w, float m, int H, int W) {
+  Sample s;
+  s.h = h;
+  s.w = w;
+  s.m = m;
+  s.inside = (h > -1.f) && (w > -1.f) && (h < (float)H) && (w < (float)W);
+  const float hf = floorf(h), wf = floorf(w);
+  const int hl = (int)hf, wl = (int)wf;
+  s.lh = h - hf;
+  s.lw = w - wf;
+  const float hh = 1.f - s.lh, hw = 1.f - s.lw;
+  const bool r0 = hl >= 0, r1 = hl + 1 <= H - 1, c0 = wl >= 0, c1 = wl + 1 <= W - 1;
+  s.cvalid = 0;
+  if (s.inside) {
+    s.cvalid = (r0 && c0 ? 1u : 0u) | (r0 && c1 ? 2u : 0u) | (r1 && c0 ? 4u : 0u) |
+               (r1 && c1 ? 8u : 0u);
+  }
+  s.cw[0] = (s.cvalid & 1u) ? hh * hw * m : 0.f;
+  s.cw[1] = (s.cvalid & 2u) ? hh * s.lw * m : 0.f;
+  s.cw[2] = (s.cvalid & 4u) ? s.lh * hw * m : 0.f;
+  s.cw[3] = (s.cvalid & 8u) ? s.lh * s.lw * m : 0.f;
+  s.cidx[0] = hl * W + wl;
+  s.cidx[1] = hl * W + wl + 1;
+  s.cidx[2] = (hl + 1) * W + wl;
+  s.cidx[3] = (hl + 1) * W + wl + 1;
+  return s;
+}
+
+}  // namespace dcn

@@ -1,0 +1,70 @@
+// grad_output tile loads shared by the two backward kernels.
+#pragma once
+#include "dcn_common.cuh"
+#include "dcn_plan.h"
+
+namespace dcn {
+
+// Loads grad_output[b, co, p] for the 8 consecutive flat pixels pix0..pix0+7
+// (flat pixel = b*HoWo + p) as floats; zero outside the tensor.  `vec` allows one
+// 16-byte load (two for f32): valid when HoWo % 8 == 0, pix0 % 8 == 0 and the
+// tensor is 16-byte aligned, so the 8 pixels lie in one image and one line.
+template <typename T>
+__device__ __forceinline__ void load8_gout(const T* __restrict__ gout, const Plan& P,
+                                           long long pix0, int co, bool vec, float (&v)[8]) {
+  if (co >= P.Co || pix0 >= P.totalP) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = 0.f;
+    return;
+  }
+  if (vec) {
+    const int b = (int)(pix0 / P.HoWo);
+    const int p = (int)(pix0 - (long long)b * P.HoWo);
+    const T* src = gout + ((size_t)b * P.Co + co) * P.HoWo + p;
+    if constexpr (std::is_same<T, float>::value) {
+      const uint4 a = ldg_nc_v4(src), c = ldg_nc_v4(src + 4);
+      v[0] = __uint_as_float(a.x); v[1] = __uint_as_float(a.y);
+      v[2] = __uint_as_float(a.z); v[3] = __uint_as_float(a.w);
+      v[4] = __uint_as_float(c.x); v[5] = __uint_as_float(c.y);
+      v[6] = __uint_as_float(c.z); v[7] = __uint_as_float(c.w);
+    } else {
+      unpack8<T>(ldg_nc_v4(src), v);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const long long pix = pix0 + e;
+      v[e] = 0.f;
+      if (pix < P.totalP) {
+        const int b = (int)(pix / P.HoWo);
+        const int p = (int)(pix - (long long)b * P.HoWo);
+        v[e] = ldf(gout + ((size_t)b * P.Co + co) * P.HoWo + p);
+      }
+    }
+  }
+}
+
+// Stores 8 floats as one 16-byte operand chunk at shared address `addr`
+// (and the bf16 lo part at addr + lo_ofs for the f32 split).
+template <typename T>
+__device__ __forceinline__ void store8_op(uint32_t addr, uint32_t lo_ofs, const float (&v)[8]) {
+  if constexpr (OpOf<T>::kSplit) {
+    uint4 hi, lo;
+    split2(v[0], v[1], hi.x, lo.x);
+    split2(v[2], v[3], hi.y, lo.y);
+    split2(v[4], v[5], hi.z, lo.z);
+    split2(v[6], v[7], hi.w, lo.w);
+    sts_v4(addr, hi);
+    sts_v4(addr + lo_ofs, lo);
+  } else {
+    constexpr int kBF = OpOf<T>::kBF16;
+    uint4 u;
+    u.x = pack2<kBF>(v[0], v[1]);
+    u.y = pack2<kBF>(v[2], v[3]);
+    u.z = pack2<kBF>(v[4], v[5]);
+    u.w = pack2<kBF>(v[6], v[7]);
+    sts_v4(addr, u);
+  }
+}
+
+}  // namespace dcn

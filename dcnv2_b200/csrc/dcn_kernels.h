@@ -1,0 +1,69 @@
+// Kernel argument blocks and launchers shared between the API layer and the kernels.
+#pragma once
+#include <cuda_runtime.h>
+
+#include "dcn_plan.h"
+
+namespace dcn {
+
+constexpr int kMaxStages = 6;
+constexpr size_t kFwdSmemBudget = 200 * 1024;  // dynamic smem for the forward ring
+constexpr size_t kBwdSmemBudget = 200 * 1024;
+
+struct FwdArgs {
+  Plan plan;
+  const void* xt;       // packed NHWC input [B][H][W][dg][Cgp]
+  const void* offset;   // [B][dg*2*K2][Ho][Wo]
+  const void* mask;     // [B][dg*K2][Ho][Wo]
+  const uint8_t* wpk;   // packed weight tiles [nCoT][nK][NT x 128 B x nsplit]
+  const void* bias;     // [Co] or nullptr
+  void* out;            // [B][Co][Ho][Wo]
+  int* err;             // device error word
+  int stages;
+  int num_sms;
+};
+
+struct BwdDataArgs {
+  Plan plan;
+  const void* xt;       // packed NHWC input
+  const void* offset;
+  const void* mask;
+  const void* gout;     // grad_output [B][Co][Ho][Wo]
+  const uint8_t* wpk;   // packed W^T tiles [nU][nKo][NC x 128 B x nsplit]
+  float* gx_nhwc;       // fp32 [B][H][W][dg][Cgp], zero-initialised, accumulated by red.add
+  void* goffset;        // [B][dg*2*K2][Ho][Wo]
+  void* gmask;          // [B][dg*K2][Ho][Wo]
+  int* err;
+  int stages;
+  int num_sms;
+  int vec_gout;         // grad_output 16-byte aligned (vector loads allowed when HoWo % 8 == 0)
+};
+
+struct BwdWeightArgs {
+  Plan plan;
+  const void* xt;
+  const void* offset;
+  const void* mask;
+  const void* gout;
+  float* gw;            // fp32 [Co][K2][dg][Cgp], zero-initialised, accumulated
+  float* gb;            // fp32 [Co] or nullptr, zero-initialised, accumulated
+  int* err;
+  int stages;
+  int num_sms;
+  int vec_gout;
+};
+
+// Packing / finishing kernels (dcn_pack.cu)
+int launch_pack_input(const Plan& p, const void* x, void* xt, cudaStream_t s);
+int launch_pack_weight_fwd(const Plan& p, const void* w, uint8_t* wpk, cudaStream_t s);
+int launch_pack_weight_bwd(const Plan& p, const void* w, uint8_t* wpk, cudaStream_t s);
+int launch_finish_grad_input(const Plan& p, const float* gx_nhwc, void* gx, cudaStream_t s);
+int launch_finish_grad_weight(const Plan& p, const float* gw, const float* gb, void* gw_out,
+                              void* gb_out, cudaStream_t s);
+
+// Main kernels
+int launch_forward(const FwdArgs& a, cudaStream_t s);
+int launch_backward_data(const BwdDataArgs& a, cudaStream_t s);
+int launch_backward_weight(const BwdWeightArgs& a, cudaStream_t s);
+
+}  // namespace dcn

@@ -1,0 +1,234 @@
+// Layout kernels around the tensor-core kernels:
+//  * input NCHW -> channels-last, group-padded [B][H][W][dg][Cgp] so one
+//    bilinear corner of 64 channels is one 128-byte (bf16) line;
+//  * weight -> pre-swizzled UMMA operand tiles, so one bulk copy per pipeline
+//    stage lands a ready-to-use 128B-swizzled tile in shared memory;
+//  * fp32 gradient accumulators -> the caller's layouts and element type.
+#include "dcn_common.cuh"
+#include "dcn_kernels.h"
+
+namespace dcn {
+
+namespace {
+
+// [B][C][H*W] -> [B][H*W][dg][Cgp]; padded channels are written as zero.
+template <typename T>
+__global__ void pack_input_kernel(const T* __restrict__ x, T* __restrict__ xt, int C, int HW,
+                                  int Cg, int Cgp, int CS) {
+  __shared__ float tile[32][33];
+  const int b = blockIdx.z;
+  const int d0 = blockIdx.y * 32;  // destination channel (in [0, CS))
+  const int p0 = blockIdx.x * 32;  // pixel
+  const T* xb = x + (size_t)b * C * HW;
+  for (int k = threadIdx.y; k < 32; k += 8) {
+    const int d = d0 + k, p = p0 + threadIdx.x;
+    float v = 0.f;
+    if (d < CS && p < HW) {
+      const int g = d / Cgp, cc = d - g * Cgp;
+      if (cc < Cg) v = ldf(xb + (size_t)(g * Cg + cc) * HW + p);
+    }
+    tile[k][threadIdx.x] = v;
+  }
+  __syncthreads();
+  T* xo = xt + (size_t)b * HW * CS;
+  for (int k = threadIdx.y; k < 32; k += 8) {
+    const int p = p0 + k, d = d0 + threadIdx.x;
+    if (d < CS && p < HW) xo[(size_t)p * CS + d] = Elem<T>::from_f(tile[threadIdx.x][k]);
+  }
+}
+
+// Writes 8 consecutive K elements (one 16-byte chunk) of a UMMA operand row.
+// hi/lo pair for the f32 split, else the 16-bit operand type.
+template <typename T>
+__device__ __forceinline__ void write_chunk(uint8_t* tile, size_t lo_ofs, int row, int chunk,
+                                            const float (&v)[8]) {
+  const uint32_t off = sw128_off(row, chunk);
+  if constexpr (OpOf<T>::kSplit) {
+    uint4 hi, lo;
+    split2(v[0], v[1], hi.x, lo.x);
+    split2(v[2], v[3], hi.y, lo.y);
+    split2(v[4], v[5], hi.z, lo.z);
+    split2(v[6], v[7], hi.w, lo.w);
+    *reinterpret_cast<uint4*>(tile + off) = hi;
+    *reinterpret_cast<uint4*>(tile + lo_ofs + off) = lo;
+  } else {
+    constexpr int kBF = OpOf<T>::kBF16;
+    uint4 u;
+    u.x = pack2<kBF>(v[0], v[1]);
+    u.y = pack2<kBF>(v[2], v[3]);
+    u.z = pack2<kBF>(v[4], v[5]);
+    u.w = pack2<kBF>(v[6], v[7]);
+    *reinterpret_cast<uint4*>(tile + off) = u;
+  }
+}
+
+// Forward B operand: tile (ct, kc) holds rows co = ct*NT + r, K elements
+// (t, g, cb*64 + e) of W[co][g*Cg + cb*64 + e][t].  One thread per 16-byte chunk.
+template <typename T>
+__global__ void pack_weight_fwd_kernel(const T* __restrict__ w, uint8_t* __restrict__ wpk,
+                                       const Plan P) {
+  const long long nchunks = (long long)P.nCoT * P.nK * P.NT * 8;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < nchunks;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int chunk = (int)(idx & 7);
+    const long long rt = idx >> 3;
+    const int r = (int)(rt % P.NT);
+    const long long tk = rt / P.NT;
+    const int kc = (int)(tk % P.nK);
+    const int ct = (int)(tk / P.nK);
+    const int t = kc / (P.dg * P.nCB);
+    const int rem = kc - t * (P.dg * P.nCB);
+    const int g = rem / P.nCB, cb = rem - g * P.nCB;
+    const int co = ct * P.NT + r;
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int cc = cb * kChunk + chunk * 8 + e;
+      v[e] = (co < P.Co && cc < P.Cg)
+                 ? ldf(w + ((size_t)co * P.C + g * P.Cg + cc) * P.K2 + t)
+                 : 0.f;
+    }
+    uint8_t* tile = wpk + (size_t)(ct * P.nK + kc) * P.wf_tile_bytes;
+    write_chunk<T>(tile, (size_t)P.NT * 128, r, chunk, v);
+  }
+}
+
+// Backward-data B operand (W transposed): tile (u, ko) holds rows n = channel
+// cc = chunk*NC + n of group g at tap t, K elements co = ko*64 + e.
+template <typename T>
+__global__ void pack_weight_bwd_kernel(const T* __restrict__ w, uint8_t* __restrict__ wpk,
+                                       const Plan P) {
+  const long long nchunks = (long long)P.nU * P.nKo * P.NC * 8;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < nchunks;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int chunk = (int)(idx & 7);
+    const long long rt = idx >> 3;
+    const int n = (int)(rt % P.NC);
+    const long long uk = rt / P.NC;
+    const int ko = (int)(uk % P.nKo);
+    const int u = (int)(uk / P.nKo);
+    const int t = u / (P.dg * P.nCC);
+    const int rem = u - t * (P.dg * P.nCC);
+    const int g = rem / P.nCC, cch = rem - g * P.nCC;
+    const int cc = cch * P.NC + n;
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int co = ko * kChunk + chunk * 8 + e;
+      v[e] = (co < P.Co && cc < P.Cg)
+                 ? ldf(w + ((size_t)co * P.C + g * P.Cg + cc) * P.K2 + t)
+                 : 0.f;
+    }
+    uint8_t* tile = wpk + (size_t)(u * P.nKo + ko) * P.wd_tile_bytes;
+    write_chunk<T>(tile, (size_t)P.NC * 128, n, chunk, v);
+  }
+}
+
+// fp32 [B][H*W][dg][Cgp] -> T [B][C][H*W]
+template <typename T>
+__global__ void finish_grad_input_kernel(const float* __restrict__ gxn, T* __restrict__ gx,
+                                         int C, int HW, int Cg, int Cgp, int CS) {
+  __shared__ float tile[32][33];
+  const int b = blockIdx.z;
+  const int c0 = blockIdx.y * 32;
+  const int p0 = blockIdx.x * 32;
+  const float* src = gxn + (size_t)b * HW * CS;
+  for (int k = threadIdx.y; k < 32; k += 8) {
+    const int p = p0 + k, c = c0 + threadIdx.x;
+    float v = 0.f;
+    if (c < C && p < HW) {
+      const int g = c / Cg, cc = c - g * Cg;
+      v = src[(size_t)p * CS + g * Cgp + cc];
+    }
+    tile[k][threadIdx.x] = v;
+  }
+  __syncthreads();
+  T* dst = gx + (size_t)b * C * HW;
+  for (int k = threadIdx.y; k < 32; k += 8) {
+    const int c = c0 + k, p = p0 + threadIdx.x;
+    if (c < C && p < HW) dst[(size_t)c * HW + p] = Elem<T>::from_f(tile[threadIdx.x][k]);
+  }
+}
+
+// fp32 [Co][K2][dg][Cgp] -> T [Co][C][K2]; fp32 [Co] -> T [Co]
+template <typename T>
+__global__ void finish_grad_weight_kernel(const float* __restrict__ gw, const float* __restrict__ gb,
+                                          T* __restrict__ gwo, T* __restrict__ gbo, const Plan P) {
+  const long long n = (long long)P.Co * P.C * P.K2;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < n;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int t = (int)(idx % P.K2);
+    const long long r = idx / P.K2;
+    const int c = (int)(r % P.C);
+    const int co = (int)(r / P.C);
+    const int g = c / P.Cg, cc = c - g * P.Cg;
+    gwo[idx] = Elem<T>::from_f(gw[((size_t)co * P.K2 + t) * P.CS + g * P.Cgp + cc]);
+    if (gbo != nullptr && idx < P.Co) gbo[idx] = Elem<T>::from_f(gb[idx]);
+  }
+}
+
+template <typename F>
+int dispatch(int dtype, F&& f) {
+  switch (dtype) {
+    case DCN_F32: f(float{}); break;
+    case DCN_F16: f(__half{}); break;
+    default: f(__nv_bfloat16{}); break;
+  }
+  return cudaGetLastError() == cudaSuccess ? DCN_OK : DCN_E_CUDA;
+}
+
+int grid_for(long long n, int threads) {
+  long long g = (n + threads - 1) / threads;
+  if (g > 148LL * 16) g = 148LL * 16;
+  return (int)(g < 1 ? 1 : g);
+}
+
+}  // namespace
+
+int launch_pack_input(const Plan& P, const void* x, void* xt, cudaStream_t s) {
+  const int HW = P.H * P.W;
+  dim3 grid(ceil_div(HW, 32), ceil_div(P.CS, 32), P.B), block(32, 8);
+  return dispatch(P.dtype, [&](auto tag) {
+    using T = decltype(tag);
+    pack_input_kernel<T><<<grid, block, 0, s>>>(static_cast<const T*>(x), static_cast<T*>(xt),
+                                                P.C, HW, P.Cg, P.Cgp, P.CS);
+  });
+}
+
+int launch_pack_weight_fwd(const Plan& P, const void* w, uint8_t* wpk, cudaStream_t s) {
+  const long long n = (long long)P.nCoT * P.nK * P.NT * 8;
+  return dispatch(P.dtype, [&](auto tag) {
+    using T = decltype(tag);
+    pack_weight_fwd_kernel<T><<<grid_for(n, 256), 256, 0, s>>>(static_cast<const T*>(w), wpk, P);
+  });
+}
+
+int launch_pack_weight_bwd(const Plan& P, const void* w, uint8_t* wpk, cudaStream_t s) {
+  const long long n = (long long)P.nU * P.nKo * P.NC * 8;
+  return dispatch(P.dtype, [&](auto tag) {
+    using T = decltype(tag);
+    pack_weight_bwd_kernel<T><<<grid_for(n, 256), 256, 0, s>>>(static_cast<const T*>(w), wpk, P);
+  });
+}
+
+int launch_finish_grad_input(const Plan& P, const float* gxn, void* gx, cudaStream_t s) {
+  const int HW = P.H * P.W;
+  dim3 grid(ceil_div(HW, 32), ceil_div(P.C, 32), P.B), block(32, 8);
+  return dispatch(P.dtype, [&](auto tag) {
+    using T = decltype(tag);
+    finish_grad_input_kernel<T><<<grid, block, 0, s>>>(gxn, static_cast<T*>(gx), P.C, HW, P.Cg,
+                                                       P.Cgp, P.CS);
+  });
+}
+
+int launch_finish_grad_weight(const Plan& P, const float* gw, const float* gb, void* gwo,
+                              void* gbo, cudaStream_t s) {
+  const long long n = (long long)P.Co * P.C * P.K2;
+  return dispatch(P.dtype, [&](auto tag) {
+    using T = decltype(tag);
+    finish_grad_weight_kernel<T><<<grid_for(n, 256), 256, 0, s>>>(
+        gw, gb, static_cast<T*>(gwo), static_cast<T*>(gbo), P);
+  });
+}
+
+}  // namespace dcn

@@ -1,0 +1,52 @@
+// Host/device shared problem plan: derived sizes, tiling and workspace layout.
+#pragma once
+#include <stddef.h>
+#include <stdint.h>
+
+#include "dcn_b200.h"
+
+namespace dcn {
+
+constexpr int kTileM = 128;   // pixels per output tile (UMMA M)
+constexpr int kChunk = 64;    // 16-bit elements per 128-byte swizzle row (one K chunk)
+constexpr size_t kWsAlign = 256;
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
+
+struct Plan {
+  // problem
+  int B, C, H, W, Co, kh, kw, sh, sw, ph, pw, dh, dw, dg, dtype, has_bias;
+  int Ho, Wo, HoWo, K2;
+  long long totalP;   // B*Ho*Wo output pixels
+  int Cg, Cgp, nCB;   // channels per group, padded to 64, 64-channel blocks per group
+  int CS;             // channels per packed input pixel = dg*Cgp
+  int esz;            // bytes per element of the tensors (2 or 4)
+  int xesz;           // bytes per element of the packed input (esz)
+  int nsplit;         // 2 for f32 (bf16 hi/lo operands), else 1
+  // forward GEMM: M = pixels, N = Co tile, K = taps x groups x channel blocks
+  int nK;             // K chunks = K2*dg*nCB
+  int NT, nCoT;       // Co tile, number of Co tiles
+  int nPT;            // pixel tiles
+  // backward-data GEMM: M = pixels, N = channel chunk of a group, K = Co
+  int Cop, nKo;       // Co padded to 64, 64-channel Co chunks
+  int NC, nCC;        // channel chunk (<=256), chunks per group
+  int nU;             // units (t, g, channel chunk) = K2*dg*nCC
+  // backward-weight GEMM: M = Co (128 rows per M tile), N = channel sets, K = pixels
+  int nMT;            // 128-row Co tiles
+  int wg_mt_per_cta;  // M tiles handled by one CTA
+  int wg_ncg;         // Co groups (nMT / wg_mt_per_cta)
+  int wg_units_per_set, wg_nsets;  // (t,g,cc) units per CTA and the number of sets
+  int wg_nsplit_px;   // CTAs along the pixel reduction
+  int wg_ksteps;      // 64-pixel K steps in total (ceil(totalP/64))
+  // workspace layout (bytes)
+  size_t off_status, off_x, off_wf, off_wd, off_gx, off_gw, off_gb;
+  size_t fwd_bytes, bwd_bytes;
+  size_t wf_tile_bytes;   // one forward weight tile (NT rows x 128 B x nsplit)
+  size_t wd_tile_bytes;   // one backward-data weight tile (NC rows x 128 B x nsplit)
+};
+
+// Fills `p` from `d`; returns DCN_OK or DCN_E_INVALID / DCN_E_UNSUPPORTED.
+int make_plan(const dcn_desc* d, Plan* p, int num_sms);
+
+}  // namespace dcn
