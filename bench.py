@@ -1,0 +1,353 @@
+"""Benchmark of the DCNv2 operator: one step = forward + backward of one DCNv2
+layer (the reference README's shape by default: B=8, C=64, 128x128, Co=256, 3x3,
+stride 1, pad 1) on seeded synthetic data, per GPU.  With N GPUs every rank runs
+its own batch (weak scaling) and the weight/bias gradients are summed over the
+ranks with one NCCL all-reduce per step (the data-parallel exchange).
+
+Prints ONE JSON line (rank 0).  Throughput unit: README-formula TFLOP/s, where a
+forward counts B*Ho*Wo*Co*(10*k*k*C + 2*k*k) FLOPs (reference README.md:17) and a
+forward+backward step counts three times that.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--dtype bf16|fp16|fp32]
+  python bench.py --impl reference ...   # the CPU port of the reference path
+
+Timing: per-step CUDA events on the launching stream, L2 flushed (256 MiB write)
+before every step outside the events, max over ranks; SM clocks sampled with
+nvidia-smi during the timed region.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOADS = {
+    # name: (B, C, H, W, Co, k, stride, pad, dil, dg, off_std)
+    "readme": (8, 64, 128, 128, 256, 3, 1, 1, 1, 1, 1.5),
+}
+DTYPES = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def readme_flops(B, C, Ho, Wo, Co, k):
+    """README.md:17 forward FLOP count."""
+    return B * Ho * Wo * Co * (10.0 * k * k * C + 2.0 * k * k)
+
+
+def gemm_flops(B, C, Ho, Wo, Co, k):
+    """Algorithmic tensor-core work of one GEMM pass: 2*Co*C*k*k*B*Ho*Wo."""
+    return 2.0 * Co * C * k * k * B * Ho * Wo
+
+
+def out_hw(H, W, k, s, p, d):
+    return (H + 2 * p - (d * (k - 1) + 1)) // s + 1, (W + 2 * p - (d * (k - 1) + 1)) // s + 1
+
+
+def make_inputs(wl, dtype, device, seed):
+    B, C, H, W, Co, k, s, p, d, dg, off_std = wl
+    Ho, Wo = out_hw(H, W, k, s, p, d)
+    g = lambda i: torch.Generator().manual_seed(1000 * seed + i)  # noqa: E731
+    x = torch.randn(B, C, H, W, generator=g(0))
+    w = torch.randn(Co, C, k, k, generator=g(1)) * (2.0 / (C * k * k)) ** 0.5
+    b = torch.randn(Co, generator=g(2)) * 0.01
+    off = torch.randn(B, 2 * dg * k * k, Ho, Wo, generator=g(3)) * off_std
+    m = torch.sigmoid(torch.randn(B, dg * k * k, Ho, Wo, generator=g(4)))
+    gy = torch.randn(B, Co, Ho, Wo, generator=g(5))
+    ts = [x, w, b, off, m, gy]
+    if device is None:
+        return ts
+    return [t.to(dtype).to(device) for t in ts]
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            pk = json.load(f)
+        return {"hbm_gbs": float(pk["hbm_gbs"]), "bf16_tflops": float(pk["bf16_tflops"])}, "measured"
+    except Exception:
+        return dict(PEAKS_FALLBACK), "fallback"
+
+
+def load_traffic(kernel, workload, dtype):
+    """DRAM bytes per launch of `kernel` from a committed ncu summary, or None."""
+    path = os.path.join(ROOT, "profiles", f"traffic_{workload}_{dtype}.txt")
+    try:
+        with open(path) as f:
+            for line in f:
+                parts = line.split()
+                if len(parts) >= 2 and parts[0] == kernel:
+                    return float(parts[1])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [v.strip() for v in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        load = sorted(sm)[len(sm) // 2:] if sm else []
+        return {"sm_mhz": statistics.median(load) if load else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_port_step(wl, B_sample):
+    """One forward+backward of the C port of the reference path (float32, OpenMP)."""
+    import oracle
+    x, w, b, off, m, gy = [t.numpy() for t in make_inputs(wl, None, None, 0)]
+    _, C, H, W, Co, k, s, p, d, dg, _ = wl
+    sl = slice(0, B_sample)
+    t0 = time.perf_counter()
+    oracle.forward(x[sl], w, b, off[sl], m[sl], s, p, d, dg, dtype=np.float32)
+    oracle.backward(x[sl], w, off[sl], m[sl], gy[sl], s, p, d, dg, dtype=np.float32)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(wl, budget_s=20.0):
+    """Times the CPU port on a bounded sample of the workload (rank 0, N=1 only)."""
+    import oracle
+    B = wl[0]
+    t1 = cpu_port_step(wl, 1)  # also warms the library
+    bs = int(max(1, min(B, (budget_s / 3) // max(t1, 1e-3))))
+    times = [cpu_port_step(wl, bs) for _ in range(2)]
+    t = min(times)
+    C, H, W, Co, k, s, p, d = wl[1], wl[2], wl[3], wl[4], wl[5], wl[6], wl[7], wl[8]
+    Ho, Wo = out_hw(H, W, k, s, p, d)
+    flops = 3 * readme_flops(bs, C, Ho, Wo, Co, k)
+    return {"value": flops / t / 1e12, "unit": "TFLOP/s (README formula, fwd+bwd)",
+            "cores": oracle.num_threads(), "kind": "port",
+            "sample": f"batch {bs} of {B} (fwd+bwd, float32), best of 2, {t:.3f} s per sample"}
+
+
+def run_reference(args, wl, rank):
+    """--impl reference: the CPU port of the reference path on the host cores."""
+    if rank != 0:
+        return
+    import oracle
+    B = wl[0]
+    C, H, W, Co, k, s, p, d = wl[1], wl[2], wl[3], wl[4], wl[5], wl[6], wl[7], wl[8]
+    Ho, Wo = out_hw(H, W, k, s, p, d)
+    t1 = cpu_port_step(wl, 1)
+    # keep the whole run to about two minutes
+    per_step = 120.0 / max(1, args.steps + args.warmup)
+    bs = int(max(1, min(B, per_step // max(t1, 1e-3))))
+    for _ in range(args.warmup):
+        cpu_port_step(wl, bs)
+    ts = [cpu_port_step(wl, bs) for _ in range(args.steps)]
+    t = sum(ts) / len(ts)
+    val = 3 * readme_flops(bs, C, Ho, Wo, Co, k) / t / 1e12
+    line = {
+        "impl": "reference", "metric": "dcnv2_fwd_bwd_readme_tflops", "value": val,
+        "unit": "TFLOP/s (README formula, fwd+bwd)", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": t * 1e3 * B / bs, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_of(args, wl),
+        "cpu_baseline": {"value": val, "unit": "TFLOP/s (README formula, fwd+bwd)",
+                         "cores": oracle.num_threads(), "kind": "port",
+                         "sample": f"batch {bs} of {B} per step (fwd+bwd, float32 C port of the "
+                                   "reference arithmetic; the reference has no CPU kernel)"},
+        "e2e": {"value": val, "unit": "TFLOP/s (README formula, fwd+bwd)",
+                "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_of(args, wl):
+    B, C, H, W, Co, k, s, p, d, dg, off_std = wl
+    return {"workload": f"{args.workload}: B={B}/gpu C={C} {H}x{W} Co={Co} {k}x{k} s{s} p{p} "
+                        f"d{d} dg{dg}, fwd+bwd", "global_batch": B * args.gpus,
+            "parallelism": f"dp{args.gpus}", "l2": "flushed before every step (256 MiB write)",
+            "offset_std_px": off_std}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--dtype", default="bf16", choices=list(DTYPES))
+    ap.add_argument("--workload", default="readme", choices=list(WORKLOADS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    wl = WORKLOADS[args.workload]
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, wl, rank)
+        return
+
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    from dcnv2_b200 import _C, _lib
+
+    dtype = DTYPES[args.dtype]
+    B, C, H, W, Co, k, s, p, d, dg, _ = wl
+    Ho, Wo = out_hw(H, W, k, s, p, d)
+    x, w, b, off, m, gy = make_inputs(wl, dtype, dev, seed=rank)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(x, off, m, gy):
+        y = _C.dcn_v2_forward(x, w, m, off, b, s, s, p, p, d, d, dg)
+        gi, goff, gm, gw, gb = _C.dcn_v2_backward(x, w, m, off, b, gy, s, s, p, p, d, d, dg)
+        if world > 1:
+            flat = torch.cat([gw.reshape(-1).float(), gb.float()])
+            dist.all_reduce(flat)
+            gw, gb = flat[:gw.numel()].view_as(gw), flat[gw.numel():]
+        return y, gw, gb
+
+    def timed(fn, n):
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(n)]
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        for i in range(n):
+            flush.zero_()
+            ev[i][0].record(stream)
+            fn()
+            ev[i][1].record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ms = sum(a.elapsed_time(b_) for a, b_ in ev)
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item()) / n
+
+    # warm-up
+    for _ in range(args.warmup):
+        step(x, off, m, gy)
+    torch.cuda.synchronize()
+
+    # timed region (device-resident inputs), kernels traced with CUDA events
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    clocks = ClockSampler(vis.split(",")[local] if vis else local)
+    clocks.start()
+    _lib.trace_reset()
+    _lib.trace_enable(True)
+    ms_step = timed(lambda: step(x, off, m, gy), args.steps)
+    _lib.trace_enable(False)
+    trace = _lib.trace_collect()
+    # forward alone (reported beside the step)
+    ms_fwd = timed(lambda: _C.dcn_v2_forward(x, w, m, off, b, s, s, p, p, d, d, dg), args.steps)
+    clk = clocks.stop()
+
+    # end to end through the public API: pinned host inputs -> device -> result to host
+    hx, hoff, hm, hgy = [t.cpu().pin_memory() for t in (x, off, m, gy)]
+    hgw = torch.empty(w.shape, dtype=torch.float32 if world > 1 else w.dtype).pin_memory()
+    hgb = torch.empty(b.shape, dtype=hgw.dtype).pin_memory()
+    dx, doff, dm, dgy = [torch.empty_like(t) for t in (x, off, m, gy)]
+    h2d = sum(t.numel() * t.element_size() for t in (hx, hoff, hm, hgy))
+    d2h = hgw.numel() * hgw.element_size() + hgb.numel() * hgb.element_size()
+
+    def e2e_step():
+        for dst, src in ((dx, hx), (doff, hoff), (dm, hm), (dgy, hgy)):
+            dst.copy_(src, non_blocking=True)
+        _, gw_, gb_ = step(dx, doff, dm, dgy)
+        hgw.copy_(gw_, non_blocking=True)
+        hgb.copy_(gb_, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    ms_e2e = timed(e2e_step, args.steps)
+
+    step_flops = 3 * readme_flops(B, C, Ho, Wo, Co, k)
+    value = world * step_flops / (ms_step * 1e-3) / 1e12
+    e2e_value = world * step_flops / (ms_e2e * 1e-3) / 1e12
+
+    # roofline of the dominant kernel (algorithmic tensor work of one GEMM pass)
+    peaks, peak_kind = load_peaks()
+    kernels = {kname: (n, tot) for kname, (n, tot) in trace.items()}
+    dom = max(kernels, key=lambda kk: kernels[kk][1])
+    n_dom, tot_dom = kernels[dom]
+    per_launch_ms = tot_dom / n_dom
+    gflop = gemm_flops(B, C, Ho, Wo, Co, k)
+    achieved = gflop / (per_launch_ms * 1e-3) / 1e12
+    traffic = load_traffic(dom, args.workload, args.dtype)
+    # kernels of this library in the timed region (the accumulator memset is a runtime call)
+    launches = sum(n for kk, (n, _) in kernels.items() if kk != "zero_accumulators")
+
+    line = {
+        "metric": "dcnv2_fwd_bwd_readme_tflops", "value": value,
+        "unit": "TFLOP/s (README formula, fwd+bwd)", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": args.dtype, "data": "synthetic (seeded)",
+        "config": config_of(args, wl),
+        "fwd_ms": ms_fwd, "fwd_readme_tflops": readme_flops(B, C, Ho, Wo, Co, k) / (ms_fwd * 1e-3) / 1e12,
+        "fwd_bwd_gemm_tflops": 3 * gflop / (ms_step * 1e-3) / 1e12,
+        "kernels_ms_per_step": {kk: v[1] / args.steps for kk, v in kernels.items()},
+        "roofline": {"kernel": dom, "bound": "tensor", "achieved": achieved,
+                     "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
+                     "peak_source": f"{peak_kind} (bf16 dense, burst)", "traffic": traffic,
+                     "algorithmic": f"2*Co*C*k*k*B*Ho*Wo = {gflop:.4g} FLOP per launch"},
+        "clocks": clk,
+        "e2e": {"value": e2e_value, "unit": "TFLOP/s (README formula, fwd+bwd)",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e},
+        "gpu_launches": int(launches),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(wl)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -25,6 +25,9 @@ EXPORTS = (
     "dcn_read_device_status",
     "dcn_strerror",
     "dcn_version",
+    "dcn_trace_enable",
+    "dcn_trace_collect",
+    "dcn_trace_reset",
 )
 
 
@@ -36,10 +39,16 @@ class DcnDesc(ctypes.Structure):
         "dtype", "has_bias")]
 
 
+class TraceEntry(ctypes.Structure):
+    """Mirror of ``struct dcn_trace_entry``."""
+
+    _fields_ = [("name", ctypes.c_char_p), ("launches", ctypes.c_int64), ("total_ms", ctypes.c_double)]
+
+
 def _load() -> ctypes.CDLL:
     if not os.path.exists(LIB_PATH):
         raise ImportError(
-            f"{LIB_PATH} is missing: build it with `python -m dcnv2_b200.build` "
+            f"{LIB_PATH} is missing: build it with `python dcnv2_b200/build.py` "
             "(the DCNv2 operator has no fallback implementation)")
     lib = ctypes.CDLL(LIB_PATH)
     vp, sz, i32p = ctypes.c_void_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_int32)
@@ -58,6 +67,12 @@ def _load() -> ctypes.CDLL:
     lib.dcn_read_device_status.restype = ctypes.c_int
     lib.dcn_strerror.argtypes = [ctypes.c_int]
     lib.dcn_strerror.restype = ctypes.c_char_p
+    lib.dcn_trace_enable.argtypes = [ctypes.c_int]
+    lib.dcn_trace_enable.restype = ctypes.c_int
+    lib.dcn_trace_collect.argtypes = [ctypes.POINTER(TraceEntry), ctypes.c_int]
+    lib.dcn_trace_collect.restype = ctypes.c_int
+    lib.dcn_trace_reset.argtypes = []
+    lib.dcn_trace_reset.restype = ctypes.c_int
     lib.dcn_version.argtypes = []
     lib.dcn_version.restype = ctypes.c_char_p
     return lib
@@ -72,3 +87,20 @@ def strerror(code: int) -> str:
 
 def version() -> str:
     return lib.dcn_version().decode()
+
+
+def trace_enable(on: bool) -> None:
+    lib.dcn_trace_enable(1 if on else 0)
+
+
+def trace_reset() -> None:
+    lib.dcn_trace_reset()
+
+
+def trace_collect() -> dict:
+    """Synchronises the traced events; returns {kernel: (launches, total_ms)}."""
+    buf = (TraceEntry * 32)()
+    n = lib.dcn_trace_collect(buf, 32)
+    if n < 0:
+        raise RuntimeError(f"dcn_trace_collect: {strerror(n)}")
+    return {buf[i].name.decode(): (int(buf[i].launches), float(buf[i].total_ms)) for i in range(n)}

@@ -1,6 +1,7 @@
 """Builds ``libdcn_b200.so`` (the sm_100a kernels + C ABI) in place with nvcc.
 
-Usage: ``python -m dcnv2_b200.build [-j N] [--verbose]``.  Objects go to
+Usage: ``python dcnv2_b200/build.py [-j N] [--verbose]`` (run as a script: importing
+the package itself needs the built library).  Objects go to
 ``dcnv2_b200/_build/``; the shared library lands next to this file so it travels
 with the source tree.  Only changed sources are recompiled.
 """

@@ -9,6 +9,7 @@
 #include "dcn_b200.h"
 #include "dcn_kernels.h"
 #include "dcn_plan.h"
+#include "dcn_trace.h"
 
 namespace dcn {
 
@@ -171,8 +172,14 @@ int dcn_forward(const dcn_desc* d, const void* input, const void* weight, const 
   if (P.totalP == 0) return DCN_OK;
   if (!input || !weight || !mask || !offset || !output) return DCN_E_NULLPTR;
   if (d->has_bias && !bias) return DCN_E_NULLPTR;
-  if ((rc = launch_pack_input(P, input, ws + P.off_x, s)) != DCN_OK) return rc;
-  if ((rc = launch_pack_weight_fwd(P, weight, ws + P.off_wf, s)) != DCN_OK) return rc;
+  {
+    TraceScope ts(TR_PACK_INPUT, s);
+    if ((rc = launch_pack_input(P, input, ws + P.off_x, s)) != DCN_OK) return rc;
+  }
+  {
+    TraceScope ts(TR_PACK_WEIGHT_FWD, s);
+    if ((rc = launch_pack_weight_fwd(P, weight, ws + P.off_wf, s)) != DCN_OK) return rc;
+  }
   FwdArgs a;
   memset(&a, 0, sizeof(a));
   a.plan = P;
@@ -184,6 +191,7 @@ int dcn_forward(const dcn_desc* d, const void* input, const void* weight, const 
   a.out = output;
   a.err = reinterpret_cast<int*>(ws + P.off_status);
   a.num_sms = device_sms();
+  TraceScope ts(TR_FORWARD, s);
   return launch_forward(a, s);
 }
 
@@ -195,8 +203,9 @@ int dcn_backward(const dcn_desc* d, const void* input, const void* weight, const
   Plan P;
   int rc = make_plan(d, &P, device_sms());
   if (rc != DCN_OK) return rc;
-  if (!input || !weight || !mask || !offset || !grad_output || !grad_input || !grad_offset ||
-      !grad_mask || !grad_weight || !workspace)
+  if (!weight || !grad_weight || !workspace) return DCN_E_NULLPTR;
+  if (P.totalP > 0 && (!input || !mask || !offset || !grad_output || !grad_input ||
+                       !grad_offset || !grad_mask))
     return DCN_E_NULLPTR;
   if (d->has_bias && !grad_bias) return DCN_E_NULLPTR;
   if (workspace_bytes < P.bwd_bytes || ((uintptr_t)workspace & (kWsAlign - 1)) != 0)
@@ -208,15 +217,27 @@ int dcn_backward(const dcn_desc* d, const void* input, const void* weight, const
   float* gb = reinterpret_cast<float*>(ws + P.off_gb);
   if (cudaMemsetAsync(ws + P.off_status, 0, sizeof(int), s) != cudaSuccess) return DCN_E_CUDA;
   // gx, gw and gb accumulators are contiguous: one memset
-  if (cudaMemsetAsync(ws + P.off_gx, 0, P.bwd_bytes - P.off_gx, s) != cudaSuccess) return DCN_E_CUDA;
+  {
+    TraceScope ts(TR_ZERO_ACCUM, s);
+    if (cudaMemsetAsync(ws + P.off_gx, 0, P.bwd_bytes - P.off_gx, s) != cudaSuccess)
+      return DCN_E_CUDA;
+  }
   if (P.totalP == 0) {
     if ((rc = launch_finish_grad_weight(P, gw, gb, grad_weight, d->has_bias ? grad_bias : nullptr, s)) != DCN_OK)
       return rc;
-    if (P.B > 0) return launch_finish_grad_input(P, gxn, grad_input, s);
+    // empty output but non-empty input (cannot happen with Ho, Wo > 0): zero grad_input
+    if ((long long)P.B * P.C * P.H * P.W > 0 && grad_input)
+      return launch_finish_grad_input(P, gxn, grad_input, s);
     return DCN_OK;
   }
-  if ((rc = launch_pack_input(P, input, ws + P.off_x, s)) != DCN_OK) return rc;
-  if ((rc = launch_pack_weight_bwd(P, weight, ws + P.off_wd, s)) != DCN_OK) return rc;
+  {
+    TraceScope ts(TR_PACK_INPUT, s);
+    if ((rc = launch_pack_input(P, input, ws + P.off_x, s)) != DCN_OK) return rc;
+  }
+  {
+    TraceScope ts(TR_PACK_WEIGHT_BWD, s);
+    if ((rc = launch_pack_weight_bwd(P, weight, ws + P.off_wd, s)) != DCN_OK) return rc;
+  }
   BwdDataArgs a;
   memset(&a, 0, sizeof(a));
   a.plan = P;
@@ -231,7 +252,10 @@ int dcn_backward(const dcn_desc* d, const void* input, const void* weight, const
   a.err = reinterpret_cast<int*>(ws + P.off_status);
   a.num_sms = device_sms();
   a.vec_gout = aligned16(grad_output);
-  if ((rc = launch_backward_data(a, s)) != DCN_OK) return rc;
+  {
+    TraceScope ts(TR_BACKWARD_DATA, s);
+    if ((rc = launch_backward_data(a, s)) != DCN_OK) return rc;
+  }
   BwdWeightArgs w;
   memset(&w, 0, sizeof(w));
   w.plan = P;
@@ -244,8 +268,15 @@ int dcn_backward(const dcn_desc* d, const void* input, const void* weight, const
   w.err = a.err;
   w.num_sms = a.num_sms;
   w.vec_gout = aligned16(grad_output);
-  if ((rc = launch_backward_weight(w, s)) != DCN_OK) return rc;
-  if ((rc = launch_finish_grad_input(P, gxn, grad_input, s)) != DCN_OK) return rc;
+  {
+    TraceScope ts(TR_BACKWARD_WEIGHT, s);
+    if ((rc = launch_backward_weight(w, s)) != DCN_OK) return rc;
+  }
+  {
+    TraceScope ts(TR_FINISH_GRAD_INPUT, s);
+    if ((rc = launch_finish_grad_input(P, gxn, grad_input, s)) != DCN_OK) return rc;
+  }
+  TraceScope ts(TR_FINISH_GRAD_WEIGHT, s);
   return launch_finish_grad_weight(P, gw, gb, grad_weight, d->has_bias ? grad_bias : nullptr, s);
 }
 

@@ -105,6 +105,21 @@ DCN_API int dcn_read_device_status(void* workspace, void* stream);
 /* Human-readable text for a DCN_* return code. */
 DCN_API const char* dcn_strerror(int code);
 
+/* Kernel timing trace (no counterpart in the reference, which only times its
+ * forward inside a hard-coded benchmark loop, com_2buffer_cpasyc.cu:301-388).
+ * When enabled, every kernel the library launches is bracketed by CUDA events
+ * on its launch stream.  dcn_trace_collect synchronises those events and
+ * returns per-kernel aggregates since the last reset: the number of entries
+ * (at most max_entries are written) or a negative DCN_E* code. */
+typedef struct dcn_trace_entry {
+  const char* name;   /* kernel name, static storage */
+  int64_t launches;   /* launches recorded */
+  double total_ms;    /* summed event-to-event time */
+} dcn_trace_entry;
+DCN_API int dcn_trace_enable(int on);
+DCN_API int dcn_trace_collect(dcn_trace_entry* out, int max_entries);
+DCN_API int dcn_trace_reset(void);
+
 /* Library version string, e.g. "dcn_b200 0.1.0 sm_100a". */
 DCN_API const char* dcn_version(void);
 
