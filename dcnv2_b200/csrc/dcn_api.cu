@@ -2,6 +2,7 @@
 // workspace layout and the launch sequences of forward and backward.
 #include <cuda_runtime.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <mutex>
@@ -14,6 +15,17 @@
 namespace dcn {
 
 namespace {
+
+// Experiment switches for kernel studies (bit 0: skip the bilinear gathers,
+// bit 1: skip output stores / scatters, bit 2: skip the MMAs).  Results are
+// wrong when set; never set in normal use.
+int debug_skip() {
+  static int v = [] {
+    const char* e = getenv("DCN_DEBUG_SKIP");
+    return e ? atoi(e) : 0;
+  }();
+  return v;
+}
 
 int device_sms() {
   static int cached[64];
@@ -84,6 +96,15 @@ int make_plan(const dcn_desc* d, Plan* p, int num_sms) {
   if (ho <= 0 || wo <= 0) return DCN_E_INVALID;
   if (ho * wo > (1LL << 30) || (long long)d->H * d->W > (1LL << 30)) return DCN_E_UNSUPPORTED;
   p->Ho = (int)ho; p->Wo = (int)wo; p->HoWo = (int)(ho * wo);
+  // 32-bit element indexing inside the kernels
+  {
+    const long long cgp = (long long)ceil_div(d->C / d->dg, kChunk) * kChunk;
+    const long long big = 1LL << 31;
+    if ((long long)d->B * d->H * d->W * d->dg * cgp >= big ||
+        (long long)d->B * d->dg * 2 * d->kh * d->kw * ho * wo >= big ||
+        (long long)d->B * d->Co * ho * wo >= big || (long long)d->B * d->C * d->H * d->W >= big)
+      return DCN_E_UNSUPPORTED;
+  }
   p->K2 = d->kh * d->kw;
   p->totalP = (long long)d->B * p->HoWo;
   p->Cg = d->C / d->dg;
@@ -189,10 +210,27 @@ int dcn_forward(const dcn_desc* d, const void* input, const void* weight, const 
   a.wpk = ws + P.off_wf;
   a.bias = d->has_bias ? bias : nullptr;
   a.out = output;
+  a.vec_out = aligned16(output);
   a.err = reinterpret_cast<int*>(ws + P.off_status);
   a.num_sms = device_sms();
+  a.dbg = debug_skip();
+  static unsigned long long* dts = nullptr;
+  if (getenv("DCN_DEBUG_TS")) {  // pipeline timestamps of CTA 0, printed to stderr (studies only)
+    if (!dts && cudaMalloc(&dts, 1024 * sizeof(unsigned long long)) != cudaSuccess) dts = nullptr;
+    if (dts) cudaMemsetAsync(dts, 0, 1024 * sizeof(unsigned long long), s);
+    a.ts = dts;
+  }
   TraceScope ts(TR_FORWARD, s);
-  return launch_forward(a, s);
+  rc = launch_forward(a, s);
+  if (a.ts) {
+    unsigned long long h[1024];
+    cudaMemcpyAsync(h, a.ts, sizeof(h), cudaMemcpyDeviceToHost, s);
+    cudaStreamSynchronize(s);
+    fprintf(stderr, "DCN_TS");
+    for (int i = 0; i < 1024; ++i) fprintf(stderr, " %llu", h[i]);
+    fprintf(stderr, "\n");
+  }
+  return rc;
 }
 
 int dcn_backward(const dcn_desc* d, const void* input, const void* weight, const void* mask,
@@ -251,6 +289,7 @@ int dcn_backward(const dcn_desc* d, const void* input, const void* weight, const
   a.gmask = grad_mask;
   a.err = reinterpret_cast<int*>(ws + P.off_status);
   a.num_sms = device_sms();
+  a.dbg = debug_skip();
   a.vec_gout = aligned16(grad_output);
   {
     TraceScope ts(TR_BACKWARD_DATA, s);
@@ -267,6 +306,7 @@ int dcn_backward(const dcn_desc* d, const void* input, const void* weight, const
   w.gb = d->has_bias ? gb : nullptr;
   w.err = a.err;
   w.num_sms = a.num_sms;
+  w.dbg = a.dbg;
   w.vec_gout = aligned16(grad_output);
   {
     TraceScope ts(TR_BACKWARD_WEIGHT, s);

@@ -11,14 +11,16 @@
 //   grad_input[b, c, corner]  += gcol * mask * corner weight    (fp32 vector red.add)
 //
 // CTA roles (448 threads):
-//   warps 0-3   A producers: grad_out tile (128 pixels x 64 Co) -> smem, MN-major SW128
-//   warps 4-11  epilogue: two threads per pixel row (channel halves) read gcol from
-//               TMEM, gather the 4 bilinear corners, reduce and scatter
+//   warps 0-3   A producers: grad_out chunks (128 pixels x 64 Co) -> smem ring,
+//               MN-major SW128, loaded once per tile when all Co chunks fit
+//   warps 4-11  epilogue: gcol TMEM -> smem transpose, then 8 lanes per pixel
+//               gather the 4 bilinear corner lines, reduce and scatter
 //   warp 12     bulk-copy producer of the pre-packed W^T tile (K-major SW128)
 //   warp 13     TMEM owner and tcgen05.mma issuer
 // The accumulator is double-buffered in TMEM (unit u in buffer u & 1) so the
 // heavy epilogue of one (tap, group) overlaps the GEMM of the next.
 #include "dcn_common.cuh"
+#include "dcn_gather.cuh"
 #include "dcn_gout.cuh"
 #include "dcn_kernels.h"
 
@@ -34,19 +36,6 @@ constexpr int kTmaWarp = 12;
 constexpr int kMmaWarp = 13;
 
 template <typename T>
-__device__ __forceinline__ void load_corner8(const T* __restrict__ src, float (&v)[8]) {
-  if constexpr (std::is_same<T, float>::value) {
-    const uint4 a = ldg_nc_v4(src), c = ldg_nc_v4(src + 4);
-    v[0] = __uint_as_float(a.x); v[1] = __uint_as_float(a.y);
-    v[2] = __uint_as_float(a.z); v[3] = __uint_as_float(a.w);
-    v[4] = __uint_as_float(c.x); v[5] = __uint_as_float(c.y);
-    v[6] = __uint_as_float(c.z); v[7] = __uint_as_float(c.w);
-  } else {
-    unpack8<T>(ldg_nc_v4(src), v);
-  }
-}
-
-template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
     dcn_bwd_data_kernel(const __grid_constant__ BwdDataArgs a) {
   constexpr int NS = OpOf<T>::kSplit ? 2 : 1;
@@ -54,12 +43,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   const Plan& P = a.plan;
   const int NC = P.NC;
   const uint32_t bTile = (uint32_t)NC * 128u;
-  const uint32_t stageBytes = NS * (kATile + bTile);
+  const uint32_t stageBytes = NS * bTile;          // one W^T stage (B operand)
+  const uint32_t aSlot = NS * kATile;              // one grad_out chunk (A operand)
   const int S = a.stages;
+  const int RA = a.a_slots;
+  // A chunks (128 pixels x 64 Co) are loaded once per tile and reused by every
+  // unit when the ring holds all Co chunks (resident), else re-streamed per unit
+  const bool resident = RA >= P.nKo;
 
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t bars[2 * kMaxStages + 9];
-  __shared__ float red[2][128][3];
+  __shared__ __align__(8) uint64_t bars[2 * kMaxStages + 7];
+  __shared__ __align__(8) uint64_t abars[2 * kMaxASlots];
   __shared__ uint32_t tmem_slot;
   __shared__ volatile int abort_flag;
 
@@ -68,22 +62,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t empty0 = smem_u32(&bars[kMaxStages]);
   const uint32_t accf0 = smem_u32(&bars[2 * kMaxStages]);
   const uint32_t acce0 = smem_u32(&bars[2 * kMaxStages + 2]);
-  const uint32_t redf0 = smem_u32(&bars[2 * kMaxStages + 4]);  // partials written
-  const uint32_t rede0 = smem_u32(&bars[2 * kMaxStages + 6]);  // partials consumed
-  const uint32_t drain = smem_u32(&bars[2 * kMaxStages + 8]);
+  const uint32_t trf = smem_u32(&bars[2 * kMaxStages + 4]);  // transpose buffer filled
+  const uint32_t tre = smem_u32(&bars[2 * kMaxStages + 5]);  // transpose buffer consumed
+  const uint32_t drain = smem_u32(&bars[2 * kMaxStages + 6]);
+  const uint32_t afull0 = smem_u32(&abars[0]);
+  const uint32_t aempty0 = smem_u32(&abars[kMaxASlots]);
+  const uint32_t abase = sbase + (uint32_t)S * stageBytes;   // A ring after the B stages
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(full0 + 8 * s, kAWarps + 1);
+      mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int r = 0; r < RA; ++r) {
+      mbar_init(afull0 + 8 * r, kAWarps);
+      mbar_init(aempty0 + 8 * r, 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(accf0 + 8 * i, 1);
       mbar_init(acce0 + 8 * i, kEpiWarps);
-      mbar_init(redf0 + 8 * i, kEpiWarps / 2);
-      mbar_init(rede0 + 8 * i, kEpiWarps / 2);
     }
+    mbar_init(trf, kEpiWarps);
+    mbar_init(tre, kEpiWarps);
     mbar_init(drain, 1);
     abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -103,155 +104,242 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp < kAWarps) {
     // ------------------------------------------------ grad_out tile producer
     const T* __restrict__ gout = reinterpret_cast<const T*>(a.gout);
-    uint32_t kidx = 0;
+    uint32_t aseq = 0;
     bool ok = true;
+    const int nload = resident ? P.nKo : P.nU * P.nKo;  // chunk loads per tile
     for (int tile = blockIdx.x; tile < nTiles && ok; tile += gridDim.x) {
-      for (int u = 0; u < P.nU && ok; ++u) {
-        for (int ko = 0; ko < P.nKo; ++ko, ++kidx) {
-          const int s = kidx % S;
-          const uint32_t ph = (kidx / S) & 1u;
-          if (!mbar_wait(empty0 + 8 * s, ph ^ 1u, a.err, &abort_flag)) { ok = false; break; }
-          const uint32_t at = sbase + s * stageBytes;
-#pragma unroll 2
+      for (int l = 0; l < nload; ++l, ++aseq) {
+        const int ko = l % P.nKo;
+        const int r = aseq % RA;
+        const uint32_t ph = (aseq / RA) & 1u;
+        const long long pix0 = (long long)tile * kTileM;
+        // 8 chunks of 8 pixels per thread, all in flight before the slot wait
+        GoutRaw<T> raw[8];
+        if (vec) {
+#pragma unroll
           for (int j = 0; j < 8; ++j) {
             const int idx = tid + 128 * j;
-            const int pg = idx & 15, k = idx >> 4;
-            float v[8];
-            load8_gout<T>(gout, P, (long long)tile * kTileM + pg * 8, ko * kChunk + k, vec, v);
-            // MN-major: row = co (K), 64-pixel atoms 8192 B apart
-            const uint32_t off = (uint32_t)(pg >> 3) * 8192u + sw128_off(k, pg & 7);
-            store8_op<T>(at + off, kATile, v);
+            gout_raw_load<T>(gout, P, pix0 + (idx & 15) * 8, ko * kChunk + (idx >> 4), raw[j]);
           }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(full0 + 8 * s);
         }
+        if (!mbar_wait(aempty0 + 8 * r, ph ^ 1u, a.err, &abort_flag)) { ok = false; break; }
+        const uint32_t at = abase + (uint32_t)r * aSlot;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int idx = tid + 128 * j;
+          const int pg = idx & 15, k = idx >> 4;
+          float v[8];
+          if (vec) {
+            gout_raw_to_f<T>(raw[j], v);
+          } else {
+            load8_gout<T>(gout, P, pix0 + pg * 8, ko * kChunk + k, false, v);
+          }
+          // MN-major: row = co (K), 64-pixel atoms 8192 B apart
+          store8_op<T>(at + (uint32_t)(pg >> 3) * 8192u + sw128_off(k, pg & 7), kATile, v);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(afull0 + 8 * r);
       }
     }
   } else if (warp < kTmaWarp) {
     // ------------------------------------------------ epilogue
-    const int ew = warp - kEpiWarp0;
-    const int q = warp & 3;           // TMEM lane quarter
-    const int chalf = ew >> 2;        // channel half
-    const int row = q * 32 + lane;
+    // Per unit (tap t, group g, channel chunk cch) and per pass of CB channels:
+    //  A) TMEM -> smem transpose buffer (thread = pixel row); after the last pass
+    //     the TMEM buffer goes back to the MMA warp;
+    //  B) 8 lanes per pixel, each on 8 channels of the pixel's corner lines:
+    //     gather the 4 corners, reduce bilinear / d/dh / d/dw against gcol, and
+    //     scatter gcol * mask * corner weight with vector red.add.
+    using GS = GatherShape<T>;
+    constexpr int LPP = GS::kLPP, PPI = GS::kPPI, LD = GS::kLD;
+    constexpr int ITER = 16 / PPI;                // pixels per lane and pass
+    const int ew = warp - kEpiWarp0;              // 0..7
+    const int q4 = warp & 3;                      // TMEM lane quarter
+    const int lp = lane / LPP, q = lane % LPP;
+    const int CB = a.tb_ch;                       // channels per pass (64 or 128)
+    const int npass = NC / CB;
+    const uint32_t tbuf = abase + (uint32_t)RA * aSlot;  // [128][CB] fp32, chunk-swizzled
+    const uint32_t rowB = (uint32_t)CB * 4u;
     const T* __restrict__ xt = reinterpret_cast<const T*>(a.xt);
     const T* __restrict__ off = reinterpret_cast<const T*>(a.offset);
     const T* __restrict__ msk = reinterpret_cast<const T*>(a.mask);
     T* __restrict__ goff = reinterpret_cast<T*>(a.goffset);
     T* __restrict__ gmsk = reinterpret_cast<T*>(a.gmask);
-    uint32_t ucnt = 0, tgcnt = 0;
+    const size_t img = (size_t)P.H * P.W;
+    uint32_t ucnt = 0, trcnt = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < nTiles && ok; tile += gridDim.x) {
-      const long long pix = (long long)tile * kTileM + row;
-      const bool pv = pix < P.totalP;
-      const int b = pv ? (int)(pix / HoWo) : 0;
-      const int p = pv ? (int)(pix - (long long)b * HoWo) : 0;
-      const int ho = p / P.Wo, wo = p - ho * P.Wo;
-      const size_t xbase = (size_t)b * P.H * P.W;
-      float am = 0.f, ah = 0.f, aw = 0.f;
-      float bw[4] = {0.f, 0.f, 0.f, 0.f};
-      float hh = 0.f, hw = 0.f, lh = 0.f, lw = 0.f, m = 0.f;
-      int cidx[4] = {0, 0, 0, 0};
-      uint32_t cval = 0;
-      for (int u = 0; u < P.nU; ++u, ++ucnt) {
+      int pb[ITER], pp[ITER];
+#pragma unroll
+      for (int it = 0; it < ITER; ++it) {
+        const long long pix = (long long)tile * kTileM + ew * 16 + it * PPI + lp;
+        if (pix < P.totalP) {
+          pb[it] = (int)(pix / HoWo);
+          pp[it] = (int)(pix - (long long)pb[it] * HoWo);
+        } else {
+          pb[it] = 0;
+          pp[it] = -1;
+        }
+      }
+      float racc[ITER][3];
+      int cbase[ITER];
+      float clh[ITER], clw[ITER], cm[ITER];
+      uint32_t cval[ITER];
+      for (int u = 0; u < P.nU && ok; ++u, ++ucnt) {
         const int tg = u / P.nCC;
         const int cch = u - tg * P.nCC;
         const int t = tg / P.dg, g = tg - t * P.dg;
         if (cch == 0) {
-          float hs = 0.f, ws = 0.f;
-          m = 0.f;
-          if (pv) {
-            const int i = t / P.kw, j = t - i * P.kw;
-            const size_t ob = ((size_t)b * P.dg + g) * 2 * P.K2;
-            hs = (float)(ho * P.sh - P.ph + i * P.dh) + ldf(off + (ob + 2 * t) * HoWo + p);
-            ws = (float)(wo * P.sw - P.pw + j * P.dw) + ldf(off + (ob + 2 * t + 1) * HoWo + p);
-            m = ldf(msk + (((size_t)b * P.dg + g) * P.K2 + t) * HoWo + p);
-          }
-          const Sample smp = make_sample(hs, ws, 1.f, P.H, P.W);
-          cval = pv ? smp.cvalid : 0u;
-          lh = smp.lh; lw = smp.lw; hh = 1.f - lh; hw = 1.f - lw;
-          bw[0] = (cval & 1u) ? hh * hw : 0.f;
-          bw[1] = (cval & 2u) ? hh * lw : 0.f;
-          bw[2] = (cval & 4u) ? lh * hw : 0.f;
-          bw[3] = (cval & 8u) ? lh * lw : 0.f;
+          const int i = t / P.kw, j = t - i * P.kw;
 #pragma unroll
-          for (int i = 0; i < 4; ++i) cidx[i] = smp.cidx[i];
+          for (int it = 0; it < ITER; ++it) {
+            racc[it][0] = racc[it][1] = racc[it][2] = 0.f;
+            cval[it] = 0u;
+            cbase[it] = 0;
+            clh[it] = clw[it] = cm[it] = 0.f;
+            if (pp[it] >= 0) {
+              const int p = pp[it], ho = p / P.Wo, wo = p - ho * P.Wo;
+              const size_t ob = ((size_t)pb[it] * P.dg + g) * 2 * P.K2;
+              const float h = (float)(ho * P.sh - P.ph + i * P.dh) + ldf(off + (ob + 2 * t) * HoWo + p);
+              const float w = (float)(wo * P.sw - P.pw + j * P.dw) + ldf(off + (ob + 2 * t + 1) * HoWo + p);
+              cm[it] = ldf(msk + (((size_t)pb[it] * P.dg + g) * P.K2 + t) * HoWo + p);
+              const float hf = floorf(h), wf = floorf(w);
+              const int hl = (int)hf, wl = (int)wf;
+              clh[it] = h - hf;
+              clw[it] = w - wf;
+              if ((h > -1.f) && (w > -1.f) && (h < (float)P.H) && (w < (float)P.W)) {
+                const bool r0 = hl >= 0, r1 = hl + 1 <= P.H - 1, c0 = wl >= 0, c1 = wl + 1 <= P.W - 1;
+                cval[it] = (r0 && c0 ? 1u : 0u) | (r0 && c1 ? 2u : 0u) | (r1 && c0 ? 4u : 0u) |
+                           (r1 && c1 ? 8u : 0u);
+                cbase[it] = hl * P.W + wl;
+              }
+              if (a.dbg & 1) cval[it] = 0u;
+            }
+          }
         }
         const int ab = ucnt & 1;
         if (!mbar_wait(accf0 + 8 * ab, (ucnt >> 1) & 1, a.err, &abort_flag)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * NC);
-        const int cbase = cch * NC;                 // first channel of this chunk
-        int cend = P.Cgp - cbase;                   // channels present in this chunk
-        if (cend > NC) cend = NC;
-        const int c_lo = chalf * (NC / 2);
-        int c_hi = c_lo + NC / 2;
-        if (c_hi > cend) c_hi = cend;
-        const size_t gofs = (size_t)g * P.Cgp + cbase;
-        for (int c0 = c_lo; c0 < c_hi; c0 += 8) {
-          float gc[8];
-          tmem_ld8(tb + c0, gc);
-          if (cval != 0u) {
-            float v[4][8];
+        for (int pass = 0; pass < npass && ok; ++pass, ++trcnt) {
+          const int c0ch = cch * NC + pass * CB;  // first channel (within the group) of the pass
+          int cend = P.Cgp - c0ch;
+          if (cend > CB) cend = CB;
+          // ---- A: TMEM -> transpose buffer
+          if (!mbar_wait(tre, (trcnt & 1) ^ 1u, a.err, &abort_flag)) { ok = false; break; }
+          {
+            const int row = q4 * 32 + lane;
+            const uint32_t tb =
+                tmem_base + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(ab * NC + pass * CB);
+            const int half = ew >> 2;
+            const uint32_t rbase = tbuf + (uint32_t)row * rowB;
+            const uint32_t sw = (uint32_t)(row & 7);
+            for (int c0 = half * (CB / 2); c0 < (half + 1) * (CB / 2); c0 += 8) {
+              float v[8];
+              tmem_ld8(tb + c0, v);
+              const uint32_t ck = (uint32_t)(c0 >> 2);  // 16-byte chunk index
+              sts_v4(rbase + ((ck ^ sw) << 4), make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]),
+                                                           __float_as_uint(v[2]), __float_as_uint(v[3])));
+              sts_v4(rbase + (((ck + 1) ^ sw) << 4),
+                     make_uint4(__float_as_uint(v[4]), __float_as_uint(v[5]), __float_as_uint(v[6]),
+                                __float_as_uint(v[7])));
+            }
+          }
+          if (pass == npass - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acce0 + 8 * ab);
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(trf);
+          if (!mbar_wait(trf, trcnt & 1, a.err, &abort_flag)) { ok = false; break; }
+          // ---- B: gather, reduce, scatter
+          for (int cs = 0; cs < cend; cs += kChunk) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              if (cval & (1u << i)) {
-                load_corner8<T>(xt + (xbase + cidx[i]) * P.CS + gofs + c0, v[i]);
-              } else {
+            for (int it = 0; it < ITER; ++it) {
+              if (cval[it] == 0u) continue;
+              const int row = ew * 16 + it * PPI + lp;
+              const int ch = cs + q * 8;  // channel within the pass
+              float gc[8];
+              {
+                const uint32_t rbase = tbuf + (uint32_t)row * rowB;
+                const uint32_t ck = (uint32_t)(ch >> 2), sw = (uint32_t)(row & 7);
 #pragma unroll
-                for (int e = 0; e < 8; ++e) v[i][e] = 0.f;
+                for (int k = 0; k < 2; ++k) {
+                  uint4 r4;
+                  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                               : "=r"(r4.x), "=r"(r4.y), "=r"(r4.z), "=r"(r4.w)
+                               : "r"(rbase + (((ck + k) ^ sw) << 4)));
+                  gc[4 * k + 0] = __uint_as_float(r4.x);
+                  gc[4 * k + 1] = __uint_as_float(r4.y);
+                  gc[4 * k + 2] = __uint_as_float(r4.z);
+                  gc[4 * k + 3] = __uint_as_float(r4.w);
+                }
               }
-            }
+              const int d[4] = {0, 1, P.W, P.W + 1};
+              const size_t pixbase = (size_t)pb[it] * img + cbase[it];
+              const size_t cofs = (size_t)g * P.Cgp + c0ch + ch;
+              uint4 raw[4][LD];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const float bil = bw[0] * v[0][e] + bw[1] * v[1][e] + bw[2] * v[2][e] + bw[3] * v[3][e];
-              const float dh = hw * (v[2][e] - v[0][e]) + lw * (v[3][e] - v[1][e]);
-              const float dw = hh * (v[1][e] - v[0][e]) + lh * (v[3][e] - v[2][e]);
-              am = fmaf(gc[e], bil, am);
-              ah = fmaf(gc[e], dh, ah);
-              aw = fmaf(gc[e], dw, aw);
-            }
+              for (int k = 0; k < 4; ++k)
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              if (cval & (1u << i)) {
-                const float s = bw[i] * m;
-                float* dst = a.gx_nhwc + (xbase + cidx[i]) * P.CS + gofs + c0;
-                red_add_v4(dst, gc[0] * s, gc[1] * s, gc[2] * s, gc[3] * s);
-                red_add_v4(dst + 4, gc[4] * s, gc[5] * s, gc[6] * s, gc[7] * s);
+                for (int l = 0; l < LD; ++l)
+                  raw[k][l] = (cval[it] & (1u << k))
+                                  ? ldg_nc_v4(xt + (pixbase + d[k]) * P.CS + cofs + l * (8 / LD))
+                                  : make_uint4(0u, 0u, 0u, 0u);
+              float vv[4][8];
+#pragma unroll
+              for (int k = 0; k < 4; ++k) unpack_slice<T>(raw[k], vv[k]);
+              const float lh = clh[it], lw = clw[it], hh = 1.f - lh, hw = 1.f - lw;
+              const float bw[4] = {(cval[it] & 1u) ? hh * hw : 0.f, (cval[it] & 2u) ? hh * lw : 0.f,
+                                   (cval[it] & 4u) ? lh * hw : 0.f, (cval[it] & 8u) ? lh * lw : 0.f};
+              float am = 0.f, ah = 0.f, aw = 0.f;
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const float bil = bw[0] * vv[0][e] + bw[1] * vv[1][e] + bw[2] * vv[2][e] + bw[3] * vv[3][e];
+                const float dh = hw * (vv[2][e] - vv[0][e]) + lw * (vv[3][e] - vv[1][e]);
+                const float dw = hh * (vv[1][e] - vv[0][e]) + lh * (vv[3][e] - vv[2][e]);
+                am = fmaf(gc[e], bil, am);
+                ah = fmaf(gc[e], dh, ah);
+                aw = fmaf(gc[e], dw, aw);
+              }
+              racc[it][0] += am;
+              racc[it][1] += ah;
+              racc[it][2] += aw;
+              const float m = cm[it];
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                if ((cval[it] & (1u << k)) && !(a.dbg & 2)) {
+                  const float sk = bw[k] * m;
+                  float* dst = a.gx_nhwc + (pixbase + d[k]) * P.CS + cofs;
+                  red_add_v4(dst, gc[0] * sk, gc[1] * sk, gc[2] * sk, gc[3] * sk);
+                  red_add_v4(dst + 4, gc[4] * sk, gc[5] * sk, gc[6] * sk, gc[7] * sk);
+                }
               }
             }
           }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(tre);
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(acce0 + 8 * ab);
+        if (!ok) break;
         if (cch == P.nCC - 1) {
-          // combine the two channel halves of this (tap, group) through smem
-          const int rb = tgcnt & 1;
-          const uint32_t rph = (tgcnt >> 1) & 1;
-          if (chalf == 1) {
-            if (!mbar_wait(rede0 + 8 * rb, rph ^ 1u, a.err, &abort_flag)) { ok = false; break; }
-            red[rb][row][0] = am;
-            red[rb][row][1] = ah;
-            red[rb][row][2] = aw;
-            __syncwarp();
-            if (lane == 0) mbar_arrive(redf0 + 8 * rb);
-          } else {
-            if (!mbar_wait(redf0 + 8 * rb, rph, a.err, &abort_flag)) { ok = false; break; }
-            const float tm = am + red[rb][row][0];
-            const float th = ah + red[rb][row][1];
-            const float tw = aw + red[rb][row][2];
-            __syncwarp();
-            if (lane == 0) mbar_arrive(rede0 + 8 * rb);
-            if (pv) {
-              const size_t gb = (size_t)b * P.dg + g;
-              goff[((gb * P.K2 + t) * 2 + 0) * HoWo + p] = Elem<T>::from_f(th * m);
-              goff[((gb * P.K2 + t) * 2 + 1) * HoWo + p] = Elem<T>::from_f(tw * m);
-              gmsk[(gb * P.K2 + t) * HoWo + p] = Elem<T>::from_f(tm);
+          // reduce each pixel's per-lane partials; write grad_offset / grad_mask
+#pragma unroll
+          for (int it = 0; it < ITER; ++it) {
+            float r0 = racc[it][0], r1 = racc[it][1], r2 = racc[it][2];
+#pragma unroll
+            for (int sh = 1; sh < LPP; sh <<= 1) {
+              r0 += __shfl_xor_sync(0xffffffffu, r0, sh);
+              r1 += __shfl_xor_sync(0xffffffffu, r1, sh);
+              r2 += __shfl_xor_sync(0xffffffffu, r2, sh);
+            }
+            if (q == 0 && pp[it] >= 0) {
+              const size_t gb = (size_t)pb[it] * P.dg + g;
+              const int p = pp[it];
+              goff[((gb * P.K2 + t) * 2 + 0) * HoWo + p] = Elem<T>::from_f(r1 * cm[it]);
+              goff[((gb * P.K2 + t) * 2 + 1) * HoWo + p] = Elem<T>::from_f(r2 * cm[it]);
+              gmsk[(gb * P.K2 + t) * HoWo + p] = Elem<T>::from_f(r0);
             }
           }
-          ++tgcnt;
-          am = ah = aw = 0.f;
         }
       }
     }
@@ -266,7 +354,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int s = kidx % S;
             const uint32_t ph = (kidx / S) & 1u;
             if (!mbar_wait(empty0 + 8 * s, ph ^ 1u, a.err, &abort_flag)) { ok = false; break; }
-            const uint32_t bt = sbase + s * stageBytes + NS * kATile;
+            const uint32_t bt = sbase + s * stageBytes;
             mbar_arrive_expect_tx(full0 + 8 * s, NS * bTile);
             bulk_g2s(bt, a.wpk + (size_t)(u * P.nKo + ko) * P.wd_tile_bytes, NS * bTile,
                      full0 + 8 * s);
@@ -278,7 +366,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = make_idesc(OpOf<T>::kBF16, 1, 0, kTileM, NC);
-      uint32_t kidx = 0, ucnt = 0;
+      uint32_t kidx = 0, ucnt = 0, aseq0 = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < nTiles && ok; tile += gridDim.x) {
         for (int u = 0; u < P.nU && ok; ++u, ++ucnt) {
@@ -287,17 +375,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint32_t dt = tmem_base + (uint32_t)(ab * NC);
           for (int ko = 0; ko < P.nKo; ++ko, ++kidx) {
+            const uint32_t aseq = aseq0 + (resident ? ko : u * P.nKo + ko);
+            const int r = aseq % RA;
+            if ((!resident || u == 0) &&
+                !mbar_wait(afull0 + 8 * r, (aseq / RA) & 1u, a.err, &abort_flag)) { ok = false; break; }
             const int s = kidx % S;
             const uint32_t ph = (kidx / S) & 1u;
             if (!mbar_wait(full0 + 8 * s, ph, a.err, &abort_flag)) { ok = false; break; }
             tc_fence_after();
-            const uint32_t at = sbase + s * stageBytes;
-            const uint32_t bt = at + NS * kATile;
+            const uint32_t at = abase + (uint32_t)r * aSlot;
+            const uint32_t bt = sbase + s * stageBytes;
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
               const uint64_t ad = sw128_desc(at + kk * 2048, 8192, 1024);
               const uint64_t bd = sw128_desc(bt + kk * 32, 16, 1024);
-              umma_f16(dt, ad, bd, idesc, (ko | kk) != 0);
+              if (!(a.dbg & 4)) umma_f16(dt, ad, bd, idesc, (ko | kk) != 0);
               if constexpr (NS == 2) {
                 const uint64_t adl = sw128_desc(at + kATile + kk * 2048, 8192, 1024);
                 const uint64_t bdl = sw128_desc(bt + bTile + kk * 32, 16, 1024);
@@ -306,10 +398,12 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
             umma_commit(empty0 + 8 * s);
+            if (!resident || u == P.nU - 1) umma_commit(aempty0 + 8 * r);
           }
           if (!ok) break;
           umma_commit(accf0 + 8 * ab);
         }
+        aseq0 += resident ? P.nKo : P.nU * P.nKo;
       }
       umma_commit(drain);
       mbar_wait_drain(drain, 0, a.err);
@@ -328,13 +422,35 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 int launch_backward_data(const BwdDataArgs& a, cudaStream_t stream) {
   const Plan& P = a.plan;
-  const size_t stageBytes = (size_t)P.nsplit * (128 * 128 + (size_t)P.NC * 128);
-  int S = (int)((kBwdSmemBudget - 1024) / stageBytes);
-  if (S > kMaxStages) S = kMaxStages;
-  if (S < 2) return DCN_E_UNSUPPORTED;
+  const size_t bStage = (size_t)P.nsplit * P.NC * 128;     // W^T stage
+  const size_t aSlot = (size_t)P.nsplit * 128 * 128;       // grad_out chunk
+  const size_t avail = kBwdSmemLimit - 1024;
+  // Preference: A double-buffered across tiles (2 x nKo slots), then resident
+  // (nKo slots), then streamed (2 slots); transpose buffer of 128 channels, then
+  // 64; W^T ring of up to 4 stages, at least 2.
+  int CB = 0, S = 0, RA = 0;
+  const int cbs[2] = {P.NC < 128 ? P.NC : 128, 64};
+  const int ras[3] = {2 * P.nKo, P.nKo, 2};
+  for (int ri = 0; ri < 3 && !RA; ++ri) {
+    for (int ci = 0; ci < 2 && !RA; ++ci) {
+      const int ra = ras[ri] > kMaxASlots ? -1 : ras[ri];
+      if (ra < 0) continue;
+      const size_t fixed = (size_t)ra * aSlot + (size_t)128 * 4 * cbs[ci];
+      if (fixed + 2 * bStage > avail) continue;
+      int s = (int)((avail - fixed) / bStage);
+      if (s > 4) s = 4;
+      RA = ra;
+      CB = cbs[ci];
+      S = s;
+    }
+  }
+  if (!RA) return DCN_E_UNSUPPORTED;
+  const size_t tbytes = (size_t)128 * 4 * CB;
   BwdDataArgs args = a;
   args.stages = S;
-  const size_t smem = 1024 + (size_t)S * stageBytes;
+  args.tb_ch = CB;
+  args.a_slots = RA;
+  const size_t smem = 1024 + (size_t)S * bStage + (size_t)RA * aSlot + tbytes;
   int grid = P.nPT < a.num_sms ? P.nPT : a.num_sms;
   if (grid <= 0) return DCN_OK;
   cudaError_t e = cudaSuccess;

@@ -13,7 +13,8 @@
 // grad_out loaders of the unit-set-0 CTAs.
 //
 // CTA roles (416 threads):
-//   warps 0-7   column gather producers (B operand, MN-major SW128)
+//   warps 0-7   column gather producers (B operand, MN-major SW128), coalesced
+//               corner-line loads as in the forward
 //   warps 8-11  grad_out tile producers (A operand, K-major SW128) + bias sums,
 //               then the TMEM -> global epilogue
 //   warp 12     TMEM owner and tcgen05.mma issuer
@@ -94,45 +95,76 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp < kBWarps) {
     // ------------------------------------------------ column gather (B operand)
+    // Work items: (unit j, 64-channel block, group of 4 pixels), 8 lanes per
+    // pixel (whole corner lines per warp-wide load); BATCH items in flight.
+    using GS = GatherShape<T>;
+    constexpr int LPP = GS::kLPP, CPL = GS::kCPL, PPI = GS::kPPI;
+    constexpr int BATCH = sizeof(T) == 4 ? 2 : 4;
+    const int lp = lane / LPP, q = lane % LPP;
     const T* __restrict__ xt = reinterpret_cast<const T*>(a.xt);
     const T* __restrict__ off = reinterpret_cast<const T*>(a.offset);
     const T* __restrict__ msk = reinterpret_cast<const T*>(a.mask);
-    const int parts = NC / 32;
-    const int items = 64 * ucount * parts;
+    const size_t img = (size_t)P.H * P.W * P.CS;
+    const int nblk = NC / kChunk;
+    const int npg = 64 / PPI;
+    const int items = ucount * nblk * npg;
     for (int ks = ks0; ks < ks1; ++ks) {
       const uint32_t kidx = ks - ks0;
       const int s = kidx % S;
       const uint32_t ph = (kidx / S) & 1u;
       if (!mbar_wait(empty0 + 8 * s, ph ^ 1u, a.err, &abort_flag)) break;
       const uint32_t bt = sbase + s * stageBytes + NS * aBytes;
-      for (int it = tid; it < items; it += kBWarps * 32) {
-        const int px = it & 63;
-        const int r2 = it >> 6;
-        const int part = r2 % parts;
-        const int j = r2 / parts;
-        const int u = u0 + j;
-        const int tg = u / P.nCC, cch = u - tg * P.nCC;
-        const int t = tg / P.dg, g = tg - t * P.dg;
-        const int cc = cch * NC + part * 32;
-        const long long pix = (long long)ks * 64 + px;
-        float acc[32];
-        if (pix < P.totalP && cc < P.Cgp) {
-          const int b = (int)(pix / HoWo);
-          const int p = (int)(pix - (long long)b * HoWo);
-          const int ho = p / P.Wo, wo = p - ho * P.Wo;
-          const int i = t / P.kw, jj = t - i * P.kw;
-          const size_t ob = ((size_t)b * P.dg + g) * 2 * P.K2;
-          const float hs = (float)(ho * P.sh - P.ph + i * P.dh) + ldf(off + (ob + 2 * t) * HoWo + p);
-          const float ws = (float)(wo * P.sw - P.pw + jj * P.dw) + ldf(off + (ob + 2 * t + 1) * HoWo + p);
-          const float m = ldf(msk + (((size_t)b * P.dg + g) * P.K2 + t) * HoWo + p);
-          const Sample smp = make_sample(hs, ws, m, P.H, P.W);
-          gather32<T>(xt + (size_t)b * P.H * P.W * P.CS, smp, g * P.Cgp + cc, P.CS, acc);
-        } else {
+      for (int it0 = warp; it0 < items; it0 += kBWarps * BATCH) {
+        Geo geo[BATCH];
+        int xo[BATCH], row[BATCH], atom[BATCH];
+        size_t xb[BATCH];
 #pragma unroll
-          for (int c = 0; c < 32; ++c) acc[c] = 0.f;
+        for (int k = 0; k < BATCH; ++k) {
+          const int it = it0 + k * kBWarps;
+          geo[k] = zero_geo();
+          xb[k] = 0;
+          xo[k] = 0;
+          row[k] = -1;
+          atom[k] = 0;
+          if (it < items) {
+            const int pg = it % npg;
+            const int r2 = it / npg;
+            const int blk = r2 % nblk, j = r2 / nblk;
+            const int u = u0 + j;
+            const int tg = u / P.nCC, cch = u - tg * P.nCC;
+            const int t = tg / P.dg, g = tg - t * P.dg;
+            const int cc = cch * NC + blk * kChunk;
+            const int px = pg * PPI + lp;
+            row[k] = px;
+            atom[k] = j * nblk + blk;
+            const long long pix = (long long)ks * 64 + px;
+            if (pix < P.totalP && cc < P.Cgp) {
+              const int b = (int)(pix / HoWo);
+              const int p = (int)(pix - (long long)b * HoWo);
+              const int ho = p / P.Wo, wo = p - ho * P.Wo;
+              const int i = t / P.kw, jj = t - i * P.kw;
+              const size_t ob = ((size_t)b * P.dg + g) * 2 * P.K2;
+              const float hs = (float)(ho * P.sh - P.ph + i * P.dh) + ldf(off + (ob + 2 * t) * HoWo + p);
+              const float ws = (float)(wo * P.sw - P.pw + jj * P.dw) + ldf(off + (ob + 2 * t + 1) * HoWo + p);
+              const float m = ldf(msk + (((size_t)b * P.dg + g) * P.K2 + t) * HoWo + p);
+              geo[k] = make_geo(hs, ws, m, P.H, P.W);
+              if (a.dbg & 1) geo[k] = zero_geo();
+              xb[k] = (size_t)b * img;
+              xo[k] = g * P.Cgp + cc + q * CPL;
+            }
+          }
         }
-        const int n = j * NC + part * 32;   // N index within the B tile
-        store_row32<T>(bt + (uint32_t)(n >> 6) * 8192u, bBytes, px, (n & 63) >> 3, acc);
+        uint4 v[BATCH][4][GS::kLD];
+#pragma unroll
+        for (int k = 0; k < BATCH; ++k) load_corners<T>(xt + xb[k] + xo[k], geo[k], P.W, P.CS, v[k]);
+#pragma unroll
+        for (int k = 0; k < BATCH; ++k) {
+          if (row[k] >= 0) {
+            float sl[8];
+            blend_corners<T>(v[k], geo[k], sl);
+            store_slice<T>(bt + (uint32_t)atom[k] * 8192u, bBytes, row[k], q, sl);
+          }
+        }
       }
       fence_proxy_async_smem();
       __syncwarp();
@@ -159,14 +191,29 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int m = 0; m < kMaxMT; ++m) {
         if (m < mcount) {
+          const int c = i & 7;
+          if (vec) {
+            // all 8 chunks of this thread in flight before any is consumed
+            GoutRaw<T> raw[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              gout_raw_load<T>(gout, P, (long long)ks * 64 + c * 8, (mt0 + m) * 128 + (i >> 3) + 16 * j, raw[j]);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              float v[8];
+              gout_raw_to_f<T>(raw[j], v);
+              if (do_bias) bsum[m][j] += ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+              store8_op<T>(at + m * kATile + sw128_off((i >> 3) + 16 * j, c), aBytes, v);
+            }
+          } else {
 #pragma unroll 2
-          for (int j = 0; j < 8; ++j) {
-            const int r = (i >> 3) + 16 * j, c = i & 7;
-            const int co = (mt0 + m) * 128 + r;
-            float v[8];
-            load8_gout<T>(gout, P, (long long)ks * 64 + c * 8, co, vec, v);
-            if (do_bias) bsum[m][j] += ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
-            store8_op<T>(at + m * kATile + sw128_off(r, c), aBytes, v);
+            for (int j = 0; j < 8; ++j) {
+              const int r = (i >> 3) + 16 * j;
+              float v[8];
+              load8_gout<T>(gout, P, (long long)ks * 64 + c * 8, (mt0 + m) * 128 + r, false, v);
+              if (do_bias) bsum[m][j] += ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+              store8_op<T>(at + m * kATile + sw128_off(r, c), aBytes, v);
+            }
           }
         }
       }
@@ -235,7 +282,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int kk = 0; kk < 4; ++kk) {
               const uint64_t ad = sw128_desc(at + m * kATile + kk * 32, 16, 1024);
               const uint64_t bd = sw128_desc(bt + (uint32_t)(n0 >> 6) * 8192u + kk * 2048, 8192, 1024);
-              umma_f16(dt, ad, bd, idesc, (ks > ks0 || kk > 0) ? 1u : 0u);
+              if (!(a.dbg & 4)) umma_f16(dt, ad, bd, idesc, (ks > ks0 || kk > 0) ? 1u : 0u);
               if constexpr (NS == 2) {
                 const uint64_t adl = sw128_desc(at + aBytes + m * kATile + kk * 32, 16, 1024);
                 const uint64_t bdl =

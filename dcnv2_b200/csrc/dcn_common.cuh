@@ -65,14 +65,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err,
                                           volatile int* abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
-  while (true) {
+  // the clock and the abort flag are consulted only every 256 polls so that
+  // waiting warps cost the working warps as few issue slots as possible
+  uint64_t t0 = 0;
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (*abort_flag) return false;
-    if (globaltimer() - t0 > DCN_WAIT_TIMEOUT_NS) {
-      raise_error(err, DCN_DEVERR_TIMEOUT);
-      *abort_flag = 1;
-      return false;
+    if ((i & 255u) == 0u) {
+      if (*abort_flag) return false;
+      const uint64_t now = globaltimer();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > DCN_WAIT_TIMEOUT_NS) {
+        raise_error(err, DCN_DEVERR_TIMEOUT);
+        *abort_flag = 1;
+        return false;
+      }
     }
   }
 }
@@ -106,6 +113,17 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
           dst),
       "l"(src), "r"(bytes), "r"(bar)
       : "memory");
+}
+
+// Warpgroup register re-allocation: every warp of a warpgroup executes the same
+// call; the block's register file (launch registers x threads) is redistributed.
+template <uint32_t N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 // ---------------------------------------------------------------- tcgen05 / TMEM

@@ -6,11 +6,14 @@
 //   A[pixel, (t,g,c)] = mask * bilinear(x_nhwc[b, :, :, g, c], pos(pixel, t) + offset)
 //
 // CTA roles (448 threads):
-//   warps 0-7  gather producers: one pixel row and 32 channels per thread; build
-//              the A tile (128 pixels x 64 channels, K-major, 128B swizzle) in smem
+//   warps 0-7  gather producers: 16 pixel rows per warp, 8 lanes per pixel so
+//              each warp-wide load reads whole corner lines; build the A tile
+//              (128 pixels x 64 channels, K-major, 128B swizzle) in smem
 //   warps 8-11 epilogue: TMEM -> registers, + bias, NCHW store
 //   warp 12    bulk-copy (TMA) producer of the pre-packed weight tile
-//   warp 13    TMEM owner and single-thread tcgen05.mma issuer
+//   warp 13    TMEM owner and single-thread tcgen05.mma issuer (warps 14-15 idle)
+// Registers are moved to the gather warps with setmaxnreg (184 each; epilogue
+// 88, control warpgroup 56).
 // A/B stages form an mbarrier ring; the accumulator is double-buffered in TMEM so
 // the epilogue of tile i overlaps the main loop of tile i+1.
 #include "dcn_common.cuh"
@@ -21,7 +24,11 @@ namespace dcn {
 
 namespace {
 
-constexpr int kFwdThreads = 448;
+#define DCN_TS(slot) \
+  do { if (a.ts && blockIdx.x == 0 && lane == 0 && (slot) < 1024) a.ts[(slot)] = globaltimer(); } while (0)
+
+constexpr int kFwdThreads = 512;  // 4 warpgroups; warps 14-15 idle
+constexpr int kMaxCo = 2048;  // bias staged in smem: Co up to 2048
 constexpr int kProdThreads = 256;
 constexpr int kEpiWarp0 = 8;
 constexpr int kTmaWarp = 12;
@@ -41,6 +48,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bars[2 * kMaxStages + 5];
   __shared__ uint32_t tmem_slot;
+  __shared__ float sbias[kMaxCo];
+  __shared__ __align__(16) uint8_t epi_stage[4][16 * 32 * sizeof(T)];
   __shared__ volatile int abort_flag;
 
   const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
@@ -64,6 +73,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  // bias staged once per CTA (the epilogue reads it for every output element)
+  for (int c = tid; c < kMaxCo; c += kFwdThreads)
+    sbias[c] = (a.bias != nullptr && c < P.Co) ? ldf(reinterpret_cast<const T*>(a.bias) + c) : 0.f;
   uint32_t tmem_cols = 32;
   while (tmem_cols < (uint32_t)(2 * NT)) tmem_cols <<= 1;
   if (warp == kMmaWarp) tmem_alloc(smem_u32(&tmem_slot), tmem_cols);
@@ -74,51 +86,98 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 
   const int nTiles = P.nPT * P.nCoT;
   const int HoWo = P.HoWo;
+  if (warp == 0) DCN_TS(1000);
+
+  // register split per warpgroup: one setmaxnreg per warpgroup, same PC
+  if ((warp >> 2) < 2) {
+    regs_inc<184>();
+  } else if ((warp >> 2) == 2) {
+    regs_dec<88>();
+  } else {
+    regs_dec<56>();
+  }
 
   if (warp < kProdThreads / 32) {
     // ------------------------------------------------ gather producers
-    const int r = tid & 127, half = tid >> 7;
+    // Warp w builds rows w*16 .. w*16+15 of every A tile.  Lane r < 16 owns the
+    // sampling geometry of row w*16 + r (offsets prefetched one tap ahead) and
+    // broadcasts it; the gather runs 4 rows at a time with 8 lanes per row.
+    using GS = GatherShape<T>;
+    constexpr int LPP = GS::kLPP, CPL = GS::kCPL, PPI = GS::kPPI;
+    constexpr int ITER = 16 / PPI;
+    constexpr int BATCH = sizeof(T) == 4 ? 2 : 4;
+    const int lp = lane / LPP, q = lane % LPP;
     const T* __restrict__ xt = reinterpret_cast<const T*>(a.xt);
     const T* __restrict__ off = reinterpret_cast<const T*>(a.offset);
     const T* __restrict__ msk = reinterpret_cast<const T*>(a.mask);
+    const int HW = P.H * P.W;
     uint32_t kidx = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < nTiles && ok; tile += gridDim.x) {
       const int pt = tile / P.nCoT;
-      const long long pix = (long long)pt * kTileM + r;
+      // this lane's geometry row (lanes 16..31 mirror lanes 0..15)
+      const long long pix = (long long)pt * kTileM + warp * 16 + (lane & 15);
       const bool pv = pix < P.totalP;
       const int b = pv ? (int)(pix / HoWo) : 0;
       const int p = pv ? (int)(pix - (long long)b * HoWo) : 0;
       const int ho = p / P.Wo, wo = p - ho * P.Wo;
-      const T* xb = xt + (size_t)b * P.H * P.W * P.CS;
-      Sample smp;
-      for (int kc = 0; kc < P.nK; ++kc, ++kidx) {
-        const int t = kc / (P.dg * P.nCB);
-        const int rem = kc - t * (P.dg * P.nCB);
-        const int g = rem / P.nCB;
-        const int cb = rem - g * P.nCB;
-        if (cb == 0) {
-          float hs = 0.f, ws = 0.f, m = 0.f;
-          if (pv) {
-            const int i = t / P.kw, j = t - i * P.kw;
-            const size_t ob = ((size_t)b * P.dg + g) * 2 * P.K2;
-            hs = (float)(ho * P.sh - P.ph + i * P.dh) + ldf(off + (ob + 2 * t) * HoWo + p);
-            ws = (float)(wo * P.sw - P.pw + j * P.dw) + ldf(off + (ob + 2 * t + 1) * HoWo + p);
-            m = ldf(msk + (((size_t)b * P.dg + g) * P.K2 + t) * HoWo + p);
-          }
-          smp = make_sample(hs, ws, m, P.H, P.W);
-          if (!pv) smp.cw[0] = smp.cw[1] = smp.cw[2] = smp.cw[3] = 0.f;
+      const int obase = b * P.dg * 2 * P.K2 * HoWo + p;   // offset[b][0][p]
+      const int mbase = b * P.dg * P.K2 * HoWo + p;       // mask[b][0][p]
+      T rh = T(), rw = T(), rm = T();
+      auto fetch_raw = [&](int tg) {
+        const int t = tg / P.dg, g = tg - t * P.dg;
+        if (pv && (a.dbg & 8)) {
+          rh = Elem<T>::from_f(0.25f);
+          rw = Elem<T>::from_f(0.25f);
+          rm = Elem<T>::from_f(0.5f);
+        } else if (pv) {
+          rh = off[obase + (g * 2 * P.K2 + 2 * t) * HoWo];
+          rw = off[obase + (g * 2 * P.K2 + 2 * t + 1) * HoWo];
+          rm = msk[mbase + (g * P.K2 + t) * HoWo];
         }
-        float acc[32];
-        gather32<T>(xb, smp, g * P.Cgp + cb * kChunk + half * 32, P.CS, acc);
+      };
+      const int nTG = P.K2 * P.dg;
+      fetch_raw(0);
+      PixGeo geo[ITER];
+      for (int kc = 0; kc < P.nK && ok; ++kc, ++kidx) {
+        const int tg = kc / P.nCB;
+        const int cb = kc - tg * P.nCB;
+        const int t = tg / P.dg, g = tg - t * P.dg;
+        if (cb == 0) {
+          const int i = t / P.kw, j = t - i * P.kw;
+          PixGeo mine = zero_pixgeo();
+          if (pv && !(a.dbg & 1)) {
+            const float hs = (float)(ho * P.sh - P.ph + i * P.dh) + Elem<T>::to_f(rh);
+            const float ws = (float)(wo * P.sw - P.pw + j * P.dw) + Elem<T>::to_f(rw);
+            mine = make_pixgeo(b * HW, hs, ws, Elem<T>::to_f(rm), P.H, P.W);
+          }
+          if (tg + 1 < nTG) fetch_raw(tg + 1);
+#pragma unroll
+          for (int it = 0; it < ITER; ++it) geo[it] = shfl_pixgeo(mine, it * PPI + lp);
+        }
+        if (warp == 0) DCN_TS(4 * kidx);
         const int s = kidx % S;
         const uint32_t ph = (kidx / S) & 1u;
-        if (!mbar_wait(empty0 + 8 * s, ph ^ 1u, a.err, &abort_flag)) { ok = false; break; }
         const uint32_t atile = sbase + s * stageBytes;
-        store_row32<T>(atile, kATile, r, half * 4, acc);
+        const int cofs = g * P.Cgp + cb * kChunk + q * CPL;
+        uint4 v[BATCH][4][GS::kLD];
+#pragma unroll
+        for (int i0 = 0; i0 < ITER; i0 += BATCH) {
+#pragma unroll
+          for (int it = 0; it < BATCH; ++it)
+            load_corners_px<T>(xt, geo[i0 + it], P.W, P.CS, cofs, v[it]);
+          if (i0 == 0 && !mbar_wait(empty0 + 8 * s, ph ^ 1u, a.err, &abort_flag)) { ok = false; break; }
+          if (warp == 0 && i0 == 0) DCN_TS(4 * kidx + 1);
+#pragma unroll
+          for (int it = 0; it < BATCH; ++it)
+            blend_store<T>(v[it], geo[i0 + it], atile, kATile, warp * 16 + (i0 + it) * PPI + lp, q);
+        }
+        if (!ok) break;
+        if (warp == 0) DCN_TS(4 * kidx + 2);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(full0 + 8 * s);
+        if (warp == 0) DCN_TS(4 * kidx + 3);
       }
     }
   } else if (warp < kTmaWarp) {
@@ -126,12 +185,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const int q = warp & 3;
     const int row = q * 32 + lane;
     T* __restrict__ y = reinterpret_cast<T*>(a.out);
-    const T* __restrict__ bias = reinterpret_cast<const T*>(a.bias);
     int it = 0;
     for (int tile = blockIdx.x; tile < nTiles; tile += gridDim.x, ++it) {
       const int pt = tile / P.nCoT, ct = tile - pt * P.nCoT;
       const int ab = it & 1;
       if (!mbar_wait(accf0 + 8 * ab, (it >> 1) & 1, a.err, &abort_flag)) break;
+      if (warp == kEpiWarp0) DCN_TS(800 + 2 * it);
       tc_fence_after();
       const long long pix = (long long)pt * kTileM + row;
       const bool pv = pix < P.totalP;
@@ -139,21 +198,45 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const int p = pv ? (int)(pix - (long long)b * HoWo) : 0;
       T* yb = y + (size_t)b * P.Co * HoWo + p;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * NT);
-      for (int c0 = 0; c0 < NT; c0 += 8) {
-        float v[8];
-        tmem_ld8(tbase + c0, v);
+      // vector path: the warp's 32 pixels form aligned 16-byte runs, each inside one image
+      const long long wpix0 = (long long)pt * kTileM + q * 32;
+      const bool vec = a.vec_out && (HoWo % 8 == 0) && (wpix0 + 32 <= P.totalP);
+      T* stg = reinterpret_cast<T*>(epi_stage[q]);
+      constexpr int EPV = 16 / (int)sizeof(T);       // elements per 16-byte vector
+      constexpr int VPR = 32 / EPV;                  // vectors per 32-pixel row
+      for (int c0 = 0; c0 < NT; c0 += 16) {
+        float v[16];
+        tmem_ld16(tbase + c0, v);
+        if (vec) {
+          // stage [16 co][32 px] then store 16-byte runs of pixels per co row
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int co = ct * NT + c0 + j;
-          if (pv && co < P.Co) {
-            const float bv = (bias != nullptr) ? ldf(bias + co) : 0.f;
-            yb[(size_t)co * HoWo] = Elem<T>::from_f(v[j] + bv);
+          for (int j = 0; j < 16; ++j) stg[j * 32 + lane] = Elem<T>::from_f(v[j] + sbias[ct * NT + c0 + j]);
+          __syncwarp();
+#pragma unroll
+          for (int k = 0; k < 16 * VPR / 32; ++k) {
+            const int idx = lane + 32 * k;
+            const int j = idx / VPR, cv = idx - j * VPR;
+            const int co = ct * NT + c0 + j;
+            if (co < P.Co && !(a.dbg & 2)) {
+              const uint4 val = *reinterpret_cast<const uint4*>(stg + j * 32 + cv * EPV);
+              const long long rp = wpix0 + cv * EPV;   // a run never crosses an image (HoWo % 8 == 0)
+              const int rb = (int)(rp / HoWo), rpp = (int)(rp - (long long)rb * HoWo);
+              *reinterpret_cast<uint4*>(y + ((size_t)rb * P.Co + co) * HoWo + rpp) = val;
+            }
+          }
+          __syncwarp();
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int co = ct * NT + c0 + j;
+            if (pv && co < P.Co && !(a.dbg & 2)) yb[(size_t)co * HoWo] = Elem<T>::from_f(v[j] + sbias[co]);
           }
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acce0 + 8 * ab);
+      if (warp == kEpiWarp0) DCN_TS(801 + 2 * it);
     }
   } else if (warp == kTmaWarp) {
     // ------------------------------------------------ weight tiles (bulk copy)
@@ -174,8 +257,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
     }
   } else {
-    // ------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // ------------------------------------------------ MMA issuer (warp 13; warps 14-15 idle)
+    if (warp == kMmaWarp && lane == 0) {
       const uint32_t idesc = make_idesc(OpOf<T>::kBF16, 0, 0, kTileM, NT);
       uint32_t kidx = 0;
       int it = 0;
@@ -189,6 +272,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           const int s = kidx % S;
           const uint32_t ph = (kidx / S) & 1u;
           if (!mbar_wait(full0 + 8 * s, ph, a.err, &abort_flag)) { ok = false; break; }
+          DCN_TS(512 + 2 * kidx);
           tc_fence_after();
           const uint32_t at = sbase + s * stageBytes;
           const uint32_t bt = at + NS * kATile;
@@ -196,7 +280,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           for (int kk = 0; kk < 4; ++kk) {
             const uint64_t ad = sw128_desc(at + kk * 32, 16, 1024);
             const uint64_t bd = sw128_desc(bt + kk * 32, 16, 1024);
-            umma_f16(dt, ad, bd, idesc, (kc | kk) != 0);
+            if (!(a.dbg & 4)) umma_f16(dt, ad, bd, idesc, (kc | kk) != 0);
             if constexpr (NS == 2) {
               const uint64_t adl = sw128_desc(at + kATile + kk * 32, 16, 1024);
               const uint64_t bdl = sw128_desc(bt + bTile + kk * 32, 16, 1024);
@@ -205,6 +289,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             }
           }
           umma_commit(empty0 + 8 * s);
+          DCN_TS(513 + 2 * kidx);
         }
         if (!ok) break;
         umma_commit(accf0 + 8 * ab);
@@ -227,6 +312,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 
 int launch_forward(const FwdArgs& a, cudaStream_t stream) {
   const Plan& P = a.plan;
+  if (P.Co > kMaxCo) return DCN_E_UNSUPPORTED;
   const int NS = P.nsplit;
   const size_t stageBytes = (size_t)NS * (128 * 128 + (size_t)P.NT * 128);
   int S = (int)((kFwdSmemBudget - 1024) / stageBytes);

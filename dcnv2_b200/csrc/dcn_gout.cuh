@@ -44,6 +44,41 @@ __device__ __forceinline__ void load8_gout(const T* __restrict__ gout, const Pla
   }
 }
 
+// Raw 16-byte loads of 8 consecutive flat pixels of one grad_output row (the
+// vector path of load8_gout), issued without consuming the result so several
+// can be in flight; zero outside the tensor.
+template <typename T>
+struct GoutRaw {
+  uint4 r[sizeof(T) / 2];
+};
+
+template <typename T>
+__device__ __forceinline__ void gout_raw_load(const T* __restrict__ gout, const Plan& P,
+                                              long long pix0, int co, GoutRaw<T>& g) {
+  if (co >= P.Co || pix0 >= P.totalP) {
+#pragma unroll
+    for (int k = 0; k < (int)(sizeof(T) / 2); ++k) g.r[k] = make_uint4(0u, 0u, 0u, 0u);
+    return;
+  }
+  const int b = (int)(pix0 / P.HoWo);
+  const int p = (int)(pix0 - (long long)b * P.HoWo);
+  const T* src = gout + ((size_t)b * P.Co + co) * P.HoWo + p;
+#pragma unroll
+  for (int k = 0; k < (int)(sizeof(T) / 2); ++k) g.r[k] = ldg_nc_v4(src + k * 4);
+}
+
+template <typename T>
+__device__ __forceinline__ void gout_raw_to_f(const GoutRaw<T>& g, float (&v)[8]) {
+  if constexpr (std::is_same<T, float>::value) {
+    v[0] = __uint_as_float(g.r[0].x); v[1] = __uint_as_float(g.r[0].y);
+    v[2] = __uint_as_float(g.r[0].z); v[3] = __uint_as_float(g.r[0].w);
+    v[4] = __uint_as_float(g.r[1].x); v[5] = __uint_as_float(g.r[1].y);
+    v[6] = __uint_as_float(g.r[1].z); v[7] = __uint_as_float(g.r[1].w);
+  } else {
+    unpack8<T>(g.r[0], v);
+  }
+}
+
 // Stores 8 floats as one 16-byte operand chunk at shared address `addr`
 // (and the bf16 lo part at addr + lo_ofs for the f32 split).
 template <typename T>

@@ -7,20 +7,25 @@
 namespace dcn {
 
 constexpr int kMaxStages = 6;
+constexpr int kMaxASlots = 16;
 constexpr size_t kFwdSmemBudget = 200 * 1024;  // dynamic smem for the forward ring
 constexpr size_t kBwdSmemBudget = 200 * 1024;
+constexpr size_t kBwdSmemLimit = 226 * 1024;  // backward-data ring + transpose buffer
 
 struct FwdArgs {
   Plan plan;
+  unsigned long long* ts;  // optional pipeline timestamps of CTA 0 (DCN_DEBUG_TS), else null
   const void* xt;       // packed NHWC input [B][H][W][dg][Cgp]
   const void* offset;   // [B][dg*2*K2][Ho][Wo]
   const void* mask;     // [B][dg*K2][Ho][Wo]
   const uint8_t* wpk;   // packed weight tiles [nCoT][nK][NT x 128 B x nsplit]
   const void* bias;     // [Co] or nullptr
   void* out;            // [B][Co][Ho][Wo]
+  int vec_out;          // out is 16-byte aligned
   int* err;             // device error word
   int stages;
   int num_sms;
+  int dbg;              // experiment switches (DCN_DEBUG_SKIP); 0 in normal use
 };
 
 struct BwdDataArgs {
@@ -36,6 +41,9 @@ struct BwdDataArgs {
   int* err;
   int stages;
   int num_sms;
+  int dbg;              // experiment switches (DCN_DEBUG_SKIP); 0 in normal use
+  int tb_ch;            // channels per transpose pass (set by the launcher)
+  int a_slots;          // grad_out chunk slots in smem (set by the launcher)
   int vec_gout;         // grad_output 16-byte aligned (vector loads allowed when HoWo % 8 == 0)
 };
 
@@ -50,6 +58,7 @@ struct BwdWeightArgs {
   int* err;
   int stages;
   int num_sms;
+  int dbg;              // experiment switches (DCN_DEBUG_SKIP); 0 in normal use
   int vec_gout;
 };
 
