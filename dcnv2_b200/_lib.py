@@ -13,6 +13,8 @@ LIB_PATH = os.path.join(_HERE, "libdcn_b200.so")
 
 DCN_F32, DCN_F16, DCN_BF16 = 0, 1, 2
 DCN_OK = 0
+DCN_E_SCRATCH_LIMIT = -7
+NOALLOC_SCRATCH_BYTES = 48 << 20
 DCN_DEVERR_TIMEOUT = 1
 
 # every exported symbol of include/dcn_b200.h
@@ -28,6 +30,7 @@ EXPORTS = (
     "dcn_trace_enable",
     "dcn_trace_collect",
     "dcn_trace_reset",
+    "dcn_forward_noalloc",
 )
 
 
@@ -73,6 +76,8 @@ def _load() -> ctypes.CDLL:
     lib.dcn_trace_collect.restype = ctypes.c_int
     lib.dcn_trace_reset.argtypes = []
     lib.dcn_trace_reset.restype = ctypes.c_int
+    lib.dcn_forward_noalloc.argtypes = [dp, vp, vp, vp, vp, vp, vp, vp]
+    lib.dcn_forward_noalloc.restype = ctypes.c_int
     lib.dcn_version.argtypes = []
     lib.dcn_version.restype = ctypes.c_char_p
     return lib

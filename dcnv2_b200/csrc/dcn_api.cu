@@ -340,6 +340,8 @@ const char* dcn_strerror(int code) {
     case DCN_E_CUDA: return "CUDA runtime error";
     case DCN_E_UNSUPPORTED: return "unsupported configuration";
     case DCN_E_DEVICE: return "error recorded by a kernel";
+    case DCN_E_SCRATCH_LIMIT:
+      return "problem exceeds the fixed scratch of dcn_forward_noalloc (DCN_NOALLOC_SCRATCH_BYTES)";
     default: return "unknown error";
   }
 }

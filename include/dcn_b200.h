@@ -54,7 +54,8 @@ enum dcn_status_code {
   DCN_E_WORKSPACE = -3,     /* workspace too small or misaligned */
   DCN_E_CUDA = -4,          /* a CUDA runtime call failed (launch error) */
   DCN_E_UNSUPPORTED = -5,   /* valid but unsupported configuration */
-  DCN_E_DEVICE = -6         /* error recorded by a kernel (see device status) */
+  DCN_E_DEVICE = -6,        /* error recorded by a kernel (see device status) */
+  DCN_E_SCRATCH_LIMIT = -7  /* problem needs more scratch than dcn_forward_noalloc has */
 };
 
 /* device-side error bits (dcn_read_device_status) */
@@ -96,6 +97,24 @@ DCN_API int dcn_backward(const dcn_desc* d, const void* input, const void* weigh
                  const void* offset, const void* bias, const void* grad_output, void* grad_input,
                  void* grad_offset, void* grad_mask, void* grad_weight, void* grad_bias,
                  void* workspace, size_t workspace_bytes, void* stream);
+
+/* Forward pass that allocates nothing and takes no workspace.  No counterpart
+ * in the reference.  For callers that may not allocate GPU memory at all (code
+ * running while a framework records a stream into a graph and forbids
+ * allocation, runtimes whose memory is fixed at start-up, plugins whose host
+ * owns every buffer): same arguments and result as dcn_forward minus the
+ * workspace.  Scratch comes from one array of DCN_NOALLOC_SCRATCH_BYTES in the
+ * library's device memory, held on every GPU that loads the library until the
+ * process exits.  Problems whose dcn_forward_workspace_size exceeds that size
+ * are rejected with DCN_E_SCRATCH_LIMIT.  The first call on a device looks up
+ * the array's device address (make that first call before any stream capture).
+ * All calls share the array, so calls that overlap on the GPU race; serialise
+ * them.  Device error bits of the last call are not readable through this
+ * entry point (it exposes no workspace); errors found on the host are returned. */
+#define DCN_NOALLOC_SCRATCH_BYTES (48u << 20) /* 48 MiB */
+DCN_API int dcn_forward_noalloc(const dcn_desc* d, const void* input, const void* weight,
+                                const void* mask, const void* offset, const void* bias,
+                                void* output, void* stream);
 
 /* Synchronises `stream`, returns the device error bits recorded in `workspace`
  * by the last dcn_forward / dcn_backward that used it, and clears them.
