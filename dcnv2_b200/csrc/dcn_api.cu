@@ -140,6 +140,8 @@ int make_plan(const dcn_desc* d, Plan* p, int num_sms) {
   p->fwd_bytes = off;
   off = common;
   p->off_wd = off; off = align_up(off + (size_t)p->nU * p->nKo * p->wd_tile_bytes, kWsAlign);
+  p->nPB = (int)((p->totalP + 63) / 64);
+  p->off_go = off; off = align_up(off + (size_t)p->nPB * p->nKo * p->nsplit * 8192, kWsAlign);
   p->off_gx = off; off = align_up(off + (size_t)d->B * d->H * d->W * p->CS * 4, kWsAlign);
   p->off_gw = off; off = align_up(off + (size_t)d->Co * p->K2 * p->CS * 4, kWsAlign);
   p->off_gb = off; off = align_up(off + (size_t)d->Co * 4, kWsAlign);
@@ -276,6 +278,13 @@ int dcn_backward(const dcn_desc* d, const void* input, const void* weight, const
     TraceScope ts(TR_PACK_WEIGHT_BWD, s);
     if ((rc = launch_pack_weight_bwd(P, weight, ws + P.off_wd, s)) != DCN_OK) return rc;
   }
+  {
+    TraceScope ts(TR_PACK_GRAD_OUTPUT, s);
+    const int vec = aligned16(grad_output) && (P.HoWo % 8 == 0);
+    if ((rc = launch_pack_gout(P, grad_output, ws + P.off_go, d->has_bias ? gb : nullptr, vec, s)) !=
+        DCN_OK)
+      return rc;
+  }
   BwdDataArgs a;
   memset(&a, 0, sizeof(a));
   a.plan = P;
@@ -283,6 +292,7 @@ int dcn_backward(const dcn_desc* d, const void* input, const void* weight, const
   a.offset = offset;
   a.mask = mask;
   a.gout = grad_output;
+  a.gpk = ws + P.off_go;
   a.wpk = ws + P.off_wd;
   a.gx_nhwc = gxn;
   a.goffset = grad_offset;
@@ -302,15 +312,29 @@ int dcn_backward(const dcn_desc* d, const void* input, const void* weight, const
   w.offset = offset;
   w.mask = mask;
   w.gout = grad_output;
+  w.gpk = ws + P.off_go;
   w.gw = gw;
-  w.gb = d->has_bias ? gb : nullptr;
   w.err = a.err;
   w.num_sms = a.num_sms;
   w.dbg = a.dbg;
   w.vec_gout = aligned16(grad_output);
+  static unsigned long long* dts = nullptr;
+  if (getenv("DCN_DEBUG_TS")) {  // pipeline timestamps of CTA 0, printed to stderr (studies only)
+    if (!dts && cudaMalloc(&dts, 1024 * sizeof(unsigned long long)) != cudaSuccess) dts = nullptr;
+    if (dts) cudaMemsetAsync(dts, 0, 1024 * sizeof(unsigned long long), s);
+    w.ts = dts;
+  }
   {
     TraceScope ts(TR_BACKWARD_WEIGHT, s);
     if ((rc = launch_backward_weight(w, s)) != DCN_OK) return rc;
+  }
+  if (w.ts) {
+    unsigned long long h[1024];
+    cudaMemcpyAsync(h, w.ts, sizeof(h), cudaMemcpyDeviceToHost, s);
+    cudaStreamSynchronize(s);
+    fprintf(stderr, "DCN_TSW");
+    for (int i = 0; i < 1024; ++i) fprintf(stderr, " %llu", h[i]);
+    fprintf(stderr, "\n");
   }
   {
     TraceScope ts(TR_FINISH_GRAD_INPUT, s);

@@ -11,8 +11,9 @@
 //   grad_input[b, c, corner]  += gcol * mask * corner weight    (fp32 vector red.add)
 //
 // CTA roles (448 threads):
-//   warps 0-3   A producers: grad_out chunks (128 pixels x 64 Co) -> smem ring,
-//               MN-major SW128, loaded once per tile when all Co chunks fit
+//   warp 0      bulk copies of pre-packed grad_out chunks (128 pixels x 64 Co,
+//               K-major SW128) into an smem ring, once per tile when all Co chunks fit
+//               (warps 1-3 idle)
 //   warps 4-11  epilogue: gcol TMEM -> smem transpose, then 8 lanes per pixel
 //               gather the 4 bilinear corner lines, reduce and scatter
 //   warp 12     bulk-copy producer of the pre-packed W^T tile (K-major SW128)
@@ -76,7 +77,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(empty0 + 8 * s, 1);
     }
     for (int r = 0; r < RA; ++r) {
-      mbar_init(afull0 + 8 * r, kAWarps);
+      mbar_init(afull0 + 8 * r, 1);
       mbar_init(aempty0 + 8 * r, 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -99,47 +100,32 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int nTiles = P.nPT;
   const int HoWo = P.HoWo;
-  const bool vec = a.vec_gout && (HoWo % 8 == 0);
 
   if (warp < kAWarps) {
-    // ------------------------------------------------ grad_out tile producer
-    const T* __restrict__ gout = reinterpret_cast<const T*>(a.gout);
-    uint32_t aseq = 0;
-    bool ok = true;
-    const int nload = resident ? P.nKo : P.nU * P.nKo;  // chunk loads per tile
-    for (int tile = blockIdx.x; tile < nTiles && ok; tile += gridDim.x) {
-      for (int l = 0; l < nload; ++l, ++aseq) {
-        const int ko = l % P.nKo;
-        const int r = aseq % RA;
-        const uint32_t ph = (aseq / RA) & 1u;
-        const long long pix0 = (long long)tile * kTileM;
-        // 8 chunks of 8 pixels per thread, all in flight before the slot wait
-        GoutRaw<T> raw[8];
-        if (vec) {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const int idx = tid + 128 * j;
-            gout_raw_load<T>(gout, P, pix0 + (idx & 15) * 8, ko * kChunk + (idx >> 4), raw[j]);
+    // ------------------------------------------------ grad_out chunk loader
+    // One thread bulk-copies the two pre-packed 64-pixel blocks of each Co chunk
+    // (K-major, 128-byte swizzle; f32: hi and lo) into the A ring.
+    if (warp == 0 && lane == 0) {
+      uint32_t aseq = 0;
+      bool ok = true;
+      const int nload = resident ? P.nKo : P.nU * P.nKo;  // chunk loads per tile
+      const uint32_t blk = NS * 8192u;
+      for (int tile = blockIdx.x; tile < nTiles && ok; tile += gridDim.x) {
+        for (int l = 0; l < nload; ++l, ++aseq) {
+          const int ko = l % P.nKo;
+          const int r = aseq % RA;
+          const uint32_t ph = (aseq / RA) & 1u;
+          if (!mbar_wait(aempty0 + 8 * r, ph ^ 1u, a.err, &abort_flag)) { ok = false; break; }
+          const uint32_t at = abase + (uint32_t)r * aSlot;
+          const int pb0 = tile * 2;
+          const int nb = (pb0 + 1 < P.nPB) ? 2 : 1;
+          mbar_arrive_expect_tx(afull0 + 8 * r, (uint32_t)nb * blk);
+          for (int h = 0; h < nb; ++h) {
+            const uint8_t* src = a.gpk + ((size_t)(pb0 + h) * P.nKo + ko) * blk;
+            bulk_g2s(at + h * 8192u, src, 8192u, afull0 + 8 * r);
+            if constexpr (NS == 2) bulk_g2s(at + kATile + h * 8192u, src + 8192, 8192u, afull0 + 8 * r);
           }
         }
-        if (!mbar_wait(aempty0 + 8 * r, ph ^ 1u, a.err, &abort_flag)) { ok = false; break; }
-        const uint32_t at = abase + (uint32_t)r * aSlot;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int idx = tid + 128 * j;
-          const int pg = idx & 15, k = idx >> 4;
-          float v[8];
-          if (vec) {
-            gout_raw_to_f<T>(raw[j], v);
-          } else {
-            load8_gout<T>(gout, P, pix0 + pg * 8, ko * kChunk + k, false, v);
-          }
-          // MN-major: row = co (K), 64-pixel atoms 8192 B apart
-          store8_op<T>(at + (uint32_t)(pg >> 3) * 8192u + sw128_off(k, pg & 7), kATile, v);
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(afull0 + 8 * r);
       }
     }
   } else if (warp < kTmaWarp) {
@@ -365,7 +351,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = make_idesc(OpOf<T>::kBF16, 1, 0, kTileM, NC);
+      const uint32_t idesc = make_idesc(OpOf<T>::kBF16, 0, 0, kTileM, NC);
       uint32_t kidx = 0, ucnt = 0, aseq0 = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < nTiles && ok; tile += gridDim.x) {
@@ -387,11 +373,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t bt = sbase + s * stageBytes;
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t ad = sw128_desc(at + kk * 2048, 8192, 1024);
+              const uint64_t ad = sw128_desc(at + kk * 32, 16, 1024);
               const uint64_t bd = sw128_desc(bt + kk * 32, 16, 1024);
               if (!(a.dbg & 4)) umma_f16(dt, ad, bd, idesc, (ko | kk) != 0);
               if constexpr (NS == 2) {
-                const uint64_t adl = sw128_desc(at + kATile + kk * 2048, 8192, 1024);
+                const uint64_t adl = sw128_desc(at + kATile + kk * 32, 16, 1024);
                 const uint64_t bdl = sw128_desc(bt + bTile + kk * 32, 16, 1024);
                 umma_f16(dt, ad, bdl, idesc, 1);
                 umma_f16(dt, adl, bd, idesc, 1);

@@ -9,15 +9,16 @@
 //       kept in TMEM at once so every gathered column feeds all of them.
 //
 // The pixel reduction is split over CTAs; each CTA adds its fp32 partial into a
-// zeroed fp32 buffer with vector red.add, and grad_bias is summed by the
-// grad_out loaders of the unit-set-0 CTAs.
+// zeroed fp32 buffer with vector red.add.  grad_bias is summed while grad_output
+// is packed (pack_gout_kernel).
 //
 // CTA roles (416 threads):
 //   warps 0-7   column gather producers (B operand, MN-major SW128), coalesced
 //               corner-line loads as in the forward
-//   warps 8-11  grad_out tile producers (A operand, K-major SW128) + bias sums,
-//               then the TMEM -> global epilogue
-//   warp 12     TMEM owner and tcgen05.mma issuer
+//   warp 8      bulk copies of pre-packed grad_out blocks (A operand, MN-major
+//               SW128); warps 8-11 then run the TMEM -> global epilogue
+//   warp 12     TMEM owner and tcgen05.mma issuer (warps 13-15 idle)
+// setmaxnreg gives the gather warps 168 registers, the grad_out warps 120.
 #include "dcn_common.cuh"
 #include "dcn_gather.cuh"
 #include "dcn_gout.cuh"
@@ -27,7 +28,10 @@ namespace dcn {
 
 namespace {
 
-constexpr int kThreads = 416;
+#define DCN_TS(slot) \
+  do { if (a.ts && blockIdx.x == 0 && lane == 0 && (slot) < 1024) a.ts[(slot)] = globaltimer(); } while (0)
+
+constexpr int kThreads = 512;  // 4 warpgroups; warps 13-15 idle
 constexpr int kBWarps = 8;
 constexpr int kAWarp0 = 8;
 constexpr int kAWarps = 4;
@@ -76,7 +80,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(full0 + 8 * s, kBWarps + kAWarps);
+      mbar_init(full0 + 8 * s, kBWarps + 1);
       mbar_init(empty0 + 8 * s, 1);
     }
     mbar_init(accf, 1);
@@ -92,11 +96,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = tmem_slot;
   const int HoWo = P.HoWo;
+  if (warp == 0) DCN_TS(1000);
+
+  // register split per warpgroup (one setmaxnreg per warpgroup)
+  if ((warp >> 2) < 2) {
+    regs_inc<168>();
+  } else if ((warp >> 2) == 2) {
+    regs_dec<120>();
+  } else {
+    regs_dec<56>();
+  }
 
   if (warp < kBWarps) {
     // ------------------------------------------------ column gather (B operand)
-    // Work items: (unit j, 64-channel block, group of 4 pixels), 8 lanes per
-    // pixel (whole corner lines per warp-wide load); BATCH items in flight.
+    // Warp w owns pixel rows w*8 .. w*8+7 of every K step.  Lane L computes the
+    // sampling geometry of (unit L/8, row L%8) (and L+32 when there are more than
+    // four units), with the offsets prefetched one K step ahead; the gather runs
+    // 4 rows at a time with 8 lanes per row and packed blends.
     using GS = GatherShape<T>;
     constexpr int LPP = GS::kLPP, CPL = GS::kCPL, PPI = GS::kPPI;
     constexpr int BATCH = sizeof(T) == 4 ? 2 : 4;
@@ -104,141 +120,127 @@ __global__ void __launch_bounds__(kThreads, 1)
     const T* __restrict__ xt = reinterpret_cast<const T*>(a.xt);
     const T* __restrict__ off = reinterpret_cast<const T*>(a.offset);
     const T* __restrict__ msk = reinterpret_cast<const T*>(a.mask);
-    const size_t img = (size_t)P.H * P.W * P.CS;
+    const int HW = P.H * P.W;
     const int nblk = NC / kChunk;
-    const int npg = 64 / PPI;
-    const int items = ucount * nblk * npg;
+    const int ngeo = ucount * 8;                 // geometries per warp and K step
+    const int niter = ucount * nblk * 2;         // 4-row gather iterations per K step
+    T rh[2], rw[2], rm[2];
+    auto fetch_raw = [&](int ks) {
+#pragma unroll
+      for (int sl = 0; sl < 2; ++sl) {
+        const int item = lane + 32 * sl;
+        if (item < ngeo) {
+          const long long pix = (long long)ks * 64 + warp * 8 + (item & 7);
+          if (pix < P.totalP) {
+            const int u = u0 + (item >> 3);
+            const int tg = u / P.nCC, t = tg / P.dg, g = tg - t * P.dg;
+            const int b = (int)(pix / HoWo), p = (int)(pix - (long long)b * HoWo);
+            const int ob = ((b * P.dg + g) * 2 * P.K2 + 2 * t) * HoWo + p;
+            rh[sl] = off[ob];
+            rw[sl] = off[ob + HoWo];
+            rm[sl] = msk[((b * P.dg + g) * P.K2 + t) * HoWo + p];
+          }
+        }
+      }
+    };
+    fetch_raw(ks0);
     for (int ks = ks0; ks < ks1; ++ks) {
       const uint32_t kidx = ks - ks0;
       const int s = kidx % S;
       const uint32_t ph = (kidx / S) & 1u;
-      if (!mbar_wait(empty0 + 8 * s, ph ^ 1u, a.err, &abort_flag)) break;
-      const uint32_t bt = sbase + s * stageBytes + NS * aBytes;
-      for (int it0 = warp; it0 < items; it0 += kBWarps * BATCH) {
-        Geo geo[BATCH];
-        int xo[BATCH], row[BATCH], atom[BATCH];
-        size_t xb[BATCH];
+      PixGeo mine[2];
 #pragma unroll
-        for (int k = 0; k < BATCH; ++k) {
-          const int it = it0 + k * kBWarps;
-          geo[k] = zero_geo();
-          xb[k] = 0;
-          xo[k] = 0;
-          row[k] = -1;
-          atom[k] = 0;
-          if (it < items) {
-            const int pg = it % npg;
-            const int r2 = it / npg;
-            const int blk = r2 % nblk, j = r2 / nblk;
-            const int u = u0 + j;
-            const int tg = u / P.nCC, cch = u - tg * P.nCC;
-            const int t = tg / P.dg, g = tg - t * P.dg;
-            const int cc = cch * NC + blk * kChunk;
-            const int px = pg * PPI + lp;
-            row[k] = px;
-            atom[k] = j * nblk + blk;
-            const long long pix = (long long)ks * 64 + px;
-            if (pix < P.totalP && cc < P.Cgp) {
-              const int b = (int)(pix / HoWo);
-              const int p = (int)(pix - (long long)b * HoWo);
-              const int ho = p / P.Wo, wo = p - ho * P.Wo;
-              const int i = t / P.kw, jj = t - i * P.kw;
-              const size_t ob = ((size_t)b * P.dg + g) * 2 * P.K2;
-              const float hs = (float)(ho * P.sh - P.ph + i * P.dh) + ldf(off + (ob + 2 * t) * HoWo + p);
-              const float ws = (float)(wo * P.sw - P.pw + jj * P.dw) + ldf(off + (ob + 2 * t + 1) * HoWo + p);
-              const float m = ldf(msk + (((size_t)b * P.dg + g) * P.K2 + t) * HoWo + p);
-              geo[k] = make_geo(hs, ws, m, P.H, P.W);
-              if (a.dbg & 1) geo[k] = zero_geo();
-              xb[k] = (size_t)b * img;
-              xo[k] = g * P.Cgp + cc + q * CPL;
-            }
-          }
-        }
-        uint4 v[BATCH][4][GS::kLD];
-#pragma unroll
-        for (int k = 0; k < BATCH; ++k) load_corners<T>(xt + xb[k] + xo[k], geo[k], P.W, P.CS, v[k]);
-#pragma unroll
-        for (int k = 0; k < BATCH; ++k) {
-          if (row[k] >= 0) {
-            float sl[8];
-            blend_corners<T>(v[k], geo[k], sl);
-            store_slice<T>(bt + (uint32_t)atom[k] * 8192u, bBytes, row[k], q, sl);
-          }
+      for (int sl = 0; sl < 2; ++sl) {
+        mine[sl] = zero_pixgeo();
+        const int item = lane + 32 * sl;
+        const long long pix = (long long)ks * 64 + warp * 8 + (item & 7);
+        if (item < ngeo && pix < P.totalP && !(a.dbg & 1)) {
+          const int u = u0 + (item >> 3);
+          const int tg = u / P.nCC, t = tg / P.dg;
+          const int i = t / P.kw, jj = t - i * P.kw;
+          const int b = (int)(pix / HoWo), p = (int)(pix - (long long)b * HoWo);
+          const int ho = p / P.Wo, wo = p - ho * P.Wo;
+          const float hs = (float)(ho * P.sh - P.ph + i * P.dh) + Elem<T>::to_f(rh[sl]);
+          const float ws = (float)(wo * P.sw - P.pw + jj * P.dw) + Elem<T>::to_f(rw[sl]);
+          mine[sl] = make_pixgeo(b * HW, hs, ws, Elem<T>::to_f(rm[sl]), P.H, P.W);
         }
       }
+      if (ks + 1 < ks1) fetch_raw(ks + 1);
+      if (warp == 0) DCN_TS(4 * kidx);
+      if (!mbar_wait(empty0 + 8 * s, ph ^ 1u, a.err, &abort_flag)) break;
+      if (warp == 0) DCN_TS(4 * kidx + 1);
+      const uint32_t bt = sbase + s * stageBytes + NS * aBytes;
+      for (int i0 = 0; i0 < niter; i0 += BATCH) {
+        uint4 v[BATCH][4][GS::kLD];
+        PixGeo gg[BATCH];
+        int row[BATCH], atom[BATCH];
+#pragma unroll
+        for (int k = 0; k < BATCH; ++k) {
+          const int itr = i0 + k;
+          row[k] = -1;
+          atom[k] = 0;
+          gg[k] = zero_pixgeo();
+          if (itr < niter) {                     // warp-uniform
+            const int half = itr & 1, r2 = itr >> 1;
+            const int blk = r2 % nblk, j = r2 / nblk;
+            const int item = j * 8 + half * 4 + lp;
+            const PixGeo src = (item >> 5) ? mine[1] : mine[0];  // slot is warp-uniform
+            gg[k] = shfl_pixgeo(src, item & 31);
+            const int u = u0 + j;
+            const int tg = u / P.nCC, cch = u - tg * P.nCC;
+            const int g = tg % P.dg;
+            const int cc = cch * NC + blk * kChunk;
+            if (cc >= P.Cgp) gg[k] = zero_pixgeo();
+            row[k] = warp * 8 + half * 4 + lp;
+            atom[k] = j * nblk + blk;
+            load_corners_px<T>(xt, gg[k], P.W, P.CS, g * P.Cgp + cc + q * CPL, v[k]);
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < BATCH; ++k)
+          if (row[k] >= 0) blend_store<T>(v[k], gg[k], bt + (uint32_t)atom[k] * 8192u, bBytes, row[k], q);
+      }
+      if (warp == 0) DCN_TS(4 * kidx + 2);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(full0 + 8 * s);
     }
   } else if (warp < kAWarp0 + kAWarps) {
-    // ------------------------------------------------ grad_out tiles (A operand) + bias
-    const int i = tid - kAWarp0 * 32;  // 0..127
-    const T* __restrict__ gout = reinterpret_cast<const T*>(a.gout);
-    const bool vec = a.vec_gout && (HoWo % 8 == 0);
-    const bool do_bias = (a.gb != nullptr) && set == 0;
-    float bsum[kMaxMT][8];
-#pragma unroll
-    for (int m = 0; m < kMaxMT; ++m)
-#pragma unroll
-      for (int j = 0; j < 8; ++j) bsum[m][j] = 0.f;
+    // ------------------------------------------------ grad_out tiles (A operand)
+    // One thread bulk-copies, per K step and M tile, the two pre-packed blocks
+    // (64 pixels x 64 Co each) that form the MN-major SW128 A tile.
     bool ok = true;
-    for (int ks = ks0; ks < ks1; ++ks) {
-      const uint32_t kidx = ks - ks0;
-      const int s = kidx % S;
-      const uint32_t ph = (kidx / S) & 1u;
-      if (!mbar_wait(empty0 + 8 * s, ph ^ 1u, a.err, &abort_flag)) { ok = false; break; }
-      const uint32_t at = sbase + s * stageBytes;
-#pragma unroll
-      for (int m = 0; m < kMaxMT; ++m) {
-        if (m < mcount) {
-          const int c = i & 7;
-          if (vec) {
-            // all 8 chunks of this thread in flight before any is consumed
-            GoutRaw<T> raw[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              gout_raw_load<T>(gout, P, (long long)ks * 64 + c * 8, (mt0 + m) * 128 + (i >> 3) + 16 * j, raw[j]);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              float v[8];
-              gout_raw_to_f<T>(raw[j], v);
-              if (do_bias) bsum[m][j] += ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
-              store8_op<T>(at + m * kATile + sw128_off((i >> 3) + 16 * j, c), aBytes, v);
-            }
-          } else {
-#pragma unroll 2
-            for (int j = 0; j < 8; ++j) {
-              const int r = (i >> 3) + 16 * j;
-              float v[8];
-              load8_gout<T>(gout, P, (long long)ks * 64 + c * 8, (mt0 + m) * 128 + r, false, v);
-              if (do_bias) bsum[m][j] += ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
-              store8_op<T>(at + m * kATile + sw128_off(r, c), aBytes, v);
-            }
-          }
-        }
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(full0 + 8 * s);
-    }
-    if (do_bias && ok) {
-#pragma unroll
-      for (int m = 0; m < kMaxMT; ++m) {
-        if (m < mcount) {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            float v = bsum[m][j];
-            v += __shfl_xor_sync(0xffffffffu, v, 1);
-            v += __shfl_xor_sync(0xffffffffu, v, 2);
-            v += __shfl_xor_sync(0xffffffffu, v, 4);
-            const int co = (mt0 + m) * 128 + (i >> 3) + 16 * j;
-            if ((i & 7) == 0 && co < P.Co) atomicAdd(a.gb + co, v);
+    if (warp == kAWarp0 && lane == 0) {
+      const uint32_t blk = NS * 8192u;
+      for (int ks = ks0; ks < ks1; ++ks) {
+        const uint32_t kidx = ks - ks0;
+        const int s = kidx % S;
+        const uint32_t ph = (kidx / S) & 1u;
+        if (!mbar_wait(empty0 + 8 * s, ph ^ 1u, a.err, &abort_flag)) { ok = false; break; }
+        DCN_TS(256 + 2 * kidx);
+        const uint32_t at = sbase + s * stageBytes;
+        uint32_t bytes = 0;
+        for (int m = 0; m < mcount; ++m)
+          for (int h = 0; h < 2; ++h)
+            if (2 * (mt0 + m) + h < P.nKo) bytes += blk;
+        mbar_arrive_expect_tx(full0 + 8 * s, bytes);
+        for (int m = 0; m < mcount; ++m) {
+          for (int h = 0; h < 2; ++h) {
+            const int ko = 2 * (mt0 + m) + h;
+            if (ko >= P.nKo) continue;
+            const uint8_t* src = a.gpk + ((size_t)ks * P.nKo + ko) * blk;
+            bulk_g2s(at + m * kATile + h * 8192u, src, 8192u, full0 + 8 * s);
+            if constexpr (NS == 2)
+              bulk_g2s(at + aBytes + m * kATile + h * 8192u, src + 8192, 8192u, full0 + 8 * s);
           }
         }
       }
     }
+    __syncwarp();
+    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
     // ------------------------------------------------ epilogue: TMEM -> fp32 red.add
     if (ok && mbar_wait(accf, 0, a.err, &abort_flag)) {
+      if (warp == kAWarp0) DCN_TS(1001);
       tc_fence_after();
       const int q = warp & 3;
       for (int m = 0; m < mcount; ++m) {
@@ -263,28 +265,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    if (warp == kMmaWarp && lane == 0) {
       bool ok = true;
       for (int ks = ks0; ks < ks1; ++ks) {
         const uint32_t kidx = ks - ks0;
         const int s = kidx % S;
         const uint32_t ph = (kidx / S) & 1u;
         if (!mbar_wait(full0 + 8 * s, ph, a.err, &abort_flag)) { ok = false; break; }
+        DCN_TS(512 + 2 * kidx);
         tc_fence_after();
         const uint32_t at = sbase + s * stageBytes;
         const uint32_t bt = at + NS * aBytes;
         for (int m = 0; m < mcount; ++m) {
           for (int n0 = 0; n0 < ntot; n0 += 256) {
             const int N = min(256, ntot - n0);
-            const uint32_t idesc = make_idesc(OpOf<T>::kBF16, 0, 1, kTileM, N);
+            const uint32_t idesc = make_idesc(OpOf<T>::kBF16, 1, 1, kTileM, N);
             const uint32_t dt = tmem_base + (uint32_t)(m * ups * NC + n0);
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t ad = sw128_desc(at + m * kATile + kk * 32, 16, 1024);
+              const uint64_t ad = sw128_desc(at + m * kATile + kk * 2048, 8192, 1024);
               const uint64_t bd = sw128_desc(bt + (uint32_t)(n0 >> 6) * 8192u + kk * 2048, 8192, 1024);
               if (!(a.dbg & 4)) umma_f16(dt, ad, bd, idesc, (ks > ks0 || kk > 0) ? 1u : 0u);
               if constexpr (NS == 2) {
-                const uint64_t adl = sw128_desc(at + aBytes + m * kATile + kk * 32, 16, 1024);
+                const uint64_t adl = sw128_desc(at + aBytes + m * kATile + kk * 2048, 8192, 1024);
                 const uint64_t bdl =
                     sw128_desc(bt + bBytes + (uint32_t)(n0 >> 6) * 8192u + kk * 2048, 8192, 1024);
                 umma_f16(dt, ad, bdl, idesc, 1);
@@ -294,6 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         umma_commit(empty0 + 8 * s);
+        DCN_TS(513 + 2 * kidx);
       }
       if (ok) umma_commit(accf);
       umma_commit(drain);
@@ -313,7 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 int launch_backward_weight(const BwdWeightArgs& a, cudaStream_t stream) {
   const Plan& P = a.plan;
-  if (P.wg_mt_per_cta > kMaxMT) return DCN_E_UNSUPPORTED;
+  if (P.wg_mt_per_cta > kMaxMT || P.wg_units_per_set > 8) return DCN_E_UNSUPPORTED;
   const size_t stageBytes =
       (size_t)P.nsplit * ((size_t)P.wg_mt_per_cta * 128 * 128 +
                           (size_t)P.wg_units_per_set * P.NC * 128);

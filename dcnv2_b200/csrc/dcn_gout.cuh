@@ -52,9 +52,17 @@ struct GoutRaw {
   uint4 r[sizeof(T) / 2];
 };
 
+__device__ __forceinline__ uint4 ldg_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
 template <typename T>
 __device__ __forceinline__ void gout_raw_load(const T* __restrict__ gout, const Plan& P,
-                                              long long pix0, int co, GoutRaw<T>& g) {
+                                              long long pix0, int co, GoutRaw<T>& g, bool plain = false) {
   if (co >= P.Co || pix0 >= P.totalP) {
 #pragma unroll
     for (int k = 0; k < (int)(sizeof(T) / 2); ++k) g.r[k] = make_uint4(0u, 0u, 0u, 0u);
@@ -64,7 +72,7 @@ __device__ __forceinline__ void gout_raw_load(const T* __restrict__ gout, const 
   const int p = (int)(pix0 - (long long)b * P.HoWo);
   const T* src = gout + ((size_t)b * P.Co + co) * P.HoWo + p;
 #pragma unroll
-  for (int k = 0; k < (int)(sizeof(T) / 2); ++k) g.r[k] = ldg_nc_v4(src + k * 4);
+  for (int k = 0; k < (int)(sizeof(T) / 2); ++k) g.r[k] = plain ? ldg_v4(src + k * 4) : ldg_nc_v4(src + k * 4);
 }
 
 template <typename T>

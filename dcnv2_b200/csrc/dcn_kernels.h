@@ -34,6 +34,7 @@ struct BwdDataArgs {
   const void* offset;
   const void* mask;
   const void* gout;     // grad_output [B][Co][Ho][Wo]
+  const uint8_t* gpk;   // packed grad_output blocks [nPB][nKo][64 x 128 B x nsplit]
   const uint8_t* wpk;   // packed W^T tiles [nU][nKo][NC x 128 B x nsplit]
   float* gx_nhwc;       // fp32 [B][H][W][dg][Cgp], zero-initialised, accumulated by red.add
   void* goffset;        // [B][dg*2*K2][Ho][Wo]
@@ -49,12 +50,13 @@ struct BwdDataArgs {
 
 struct BwdWeightArgs {
   Plan plan;
+  unsigned long long* ts;  // optional pipeline timestamps of CTA 0 (DCN_DEBUG_TS), else null
   const void* xt;
   const void* offset;
   const void* mask;
   const void* gout;
+  const uint8_t* gpk;   // packed grad_output blocks (as above)
   float* gw;            // fp32 [Co][K2][dg][Cgp], zero-initialised, accumulated
-  float* gb;            // fp32 [Co] or nullptr, zero-initialised, accumulated
   int* err;
   int stages;
   int num_sms;
@@ -66,6 +68,8 @@ struct BwdWeightArgs {
 int launch_pack_input(const Plan& p, const void* x, void* xt, cudaStream_t s);
 int launch_pack_weight_fwd(const Plan& p, const void* w, uint8_t* wpk, cudaStream_t s);
 int launch_pack_weight_bwd(const Plan& p, const void* w, uint8_t* wpk, cudaStream_t s);
+int launch_pack_gout(const Plan& p, const void* gout, uint8_t* gpk, float* gb, int vec,
+                     cudaStream_t s);
 int launch_finish_grad_input(const Plan& p, const float* gx_nhwc, void* gx, cudaStream_t s);
 int launch_finish_grad_weight(const Plan& p, const float* gw, const float* gb, void* gw_out,
                               void* gb_out, cudaStream_t s);

@@ -5,6 +5,7 @@
 //    stage lands a ready-to-use 128B-swizzled tile in shared memory;
 //  * fp32 gradient accumulators -> the caller's layouts and element type.
 #include "dcn_common.cuh"
+#include "dcn_gout.cuh"
 #include "dcn_kernels.h"
 
 namespace dcn {
@@ -124,6 +125,85 @@ __global__ void pack_weight_bwd_kernel(const T* __restrict__ w, uint8_t* __restr
   }
 }
 
+// grad_output NCHW -> operand blocks: block (pixel block pb of 64 flat pixels,
+// Co chunk ko of 64) is 64 rows (pixels) x 64 Co in the operand type, rows of
+// 128 bytes with the 128-byte swizzle (f32: bf16 hi block then lo block).  The
+// same bytes serve as the K-major A operand of the backward-data GEMM (M =
+// pixels, K = Co) and the MN-major A operand of the backward-weight GEMM (M = Co,
+// K = pixels).  grad_bias partial sums (over the pixels this CTA visits) are
+// added to the fp32 accumulator `gb` when it is not null.
+template <typename T>
+__global__ void __launch_bounds__(256) pack_gout_kernel(const T* __restrict__ gout,
+                                                        uint8_t* __restrict__ gpk,
+                                                        float* __restrict__ gb, const Plan P,
+                                                        int vec) {
+  __shared__ float tile[64][65];
+  const int ko = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int nPB = (int)((P.totalP + 63) / 64);
+  const size_t blk_bytes = (size_t)P.nsplit * 8192;
+  float bsum[2] = {0.f, 0.f};
+  for (int pb = blockIdx.x; pb < nPB; pb += gridDim.x) {
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int item = tid + 256 * k;
+      const int col = item >> 3, ch = item & 7;   // Co row within the chunk, 8-pixel group
+      float v[8];
+      const int co = ko * kChunk + col;
+      if (vec) {
+        GoutRaw<T> raw;
+        gout_raw_load<T>(gout, P, (long long)pb * 64 + ch * 8, co, raw);
+        gout_raw_to_f<T>(raw, v);
+      } else {
+        load8_gout<T>(gout, P, (long long)pb * 64 + ch * 8, co, false, v);
+      }
+      bsum[k] += ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+#pragma unroll
+      for (int e = 0; e < 8; ++e) tile[col][ch * 8 + e] = v[e];
+    }
+    __syncthreads();
+    uint8_t* blk = gpk + ((size_t)pb * P.nKo + ko) * blk_bytes;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int item = tid + 256 * k;
+      const int row = item >> 3, c = item & 7;    // pixel row, 16-byte chunk (8 Co)
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = tile[c * 8 + e][row];
+      const uint32_t off = sw128_off(row, c);
+      if constexpr (OpOf<T>::kSplit) {
+        uint4 hi, lo;
+        split2(v[0], v[1], hi.x, lo.x);
+        split2(v[2], v[3], hi.y, lo.y);
+        split2(v[4], v[5], hi.z, lo.z);
+        split2(v[6], v[7], hi.w, lo.w);
+        *reinterpret_cast<uint4*>(blk + off) = hi;
+        *reinterpret_cast<uint4*>(blk + 8192 + off) = lo;
+      } else {
+        constexpr int kBF = OpOf<T>::kBF16;
+        uint4 u;
+        u.x = pack2<kBF>(v[0], v[1]);
+        u.y = pack2<kBF>(v[2], v[3]);
+        u.z = pack2<kBF>(v[4], v[5]);
+        u.w = pack2<kBF>(v[6], v[7]);
+        *reinterpret_cast<uint4*>(blk + off) = u;
+      }
+    }
+  }
+  if (gb != nullptr) {
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      float s = bsum[k];
+      s += __shfl_xor_sync(0xffffffffu, s, 1);
+      s += __shfl_xor_sync(0xffffffffu, s, 2);
+      s += __shfl_xor_sync(0xffffffffu, s, 4);
+      const int co = ko * kChunk + ((tid + 256 * k) >> 3);
+      if ((lane & 7) == 0 && co < P.Co) atomicAdd(gb + co, s);
+    }
+  }
+}
+
 // fp32 [B][H*W][dg][Cgp] -> T [B][C][H*W]
 template <typename T>
 __global__ void finish_grad_input_kernel(const float* __restrict__ gxn, T* __restrict__ gx,
@@ -208,6 +288,19 @@ int launch_pack_weight_bwd(const Plan& P, const void* w, uint8_t* wpk, cudaStrea
   return dispatch(P.dtype, [&](auto tag) {
     using T = decltype(tag);
     pack_weight_bwd_kernel<T><<<grid_for(n, 256), 256, 0, s>>>(static_cast<const T*>(w), wpk, P);
+  });
+}
+
+int launch_pack_gout(const Plan& P, const void* gout, uint8_t* gpk, float* gb, int vec,
+                     cudaStream_t s) {
+  const int nPB = (int)((P.totalP + 63) / 64);
+  int gx = 592 / P.nKo;   // about four CTAs per SM in total, pixel blocks strided
+  if (gx < 1) gx = 1;
+  if (gx > nPB) gx = nPB;
+  dim3 grid(gx, P.nKo);
+  return dispatch(P.dtype, [&](auto tag) {
+    using T = decltype(tag);
+    pack_gout_kernel<T><<<grid, 256, 0, s>>>(static_cast<const T*>(gout), gpk, gb, P, vec);
   });
 }
 

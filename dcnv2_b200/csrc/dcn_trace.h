@@ -16,6 +16,7 @@ enum TraceId {
   TR_BACKWARD_WEIGHT,
   TR_FINISH_GRAD_INPUT,
   TR_FINISH_GRAD_WEIGHT,
+  TR_PACK_GRAD_OUTPUT,
   TR_COUNT
 };
 
