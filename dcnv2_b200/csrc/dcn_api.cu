@@ -301,9 +301,23 @@ int dcn_backward(const dcn_desc* d, const void* input, const void* weight, const
   a.num_sms = device_sms();
   a.dbg = debug_skip();
   a.vec_gout = aligned16(grad_output);
+  static unsigned long long* dts_d = nullptr;
+  if (getenv("DCN_DEBUG_TS")) {  // pipeline timestamps of CTA 0, printed to stderr (studies only)
+    if (!dts_d && cudaMalloc(&dts_d, 1024 * sizeof(unsigned long long)) != cudaSuccess) dts_d = nullptr;
+    if (dts_d) cudaMemsetAsync(dts_d, 0, 1024 * sizeof(unsigned long long), s);
+    a.ts = dts_d;
+  }
   {
     TraceScope ts(TR_BACKWARD_DATA, s);
     if ((rc = launch_backward_data(a, s)) != DCN_OK) return rc;
+  }
+  if (a.ts) {
+    unsigned long long h[1024];
+    cudaMemcpyAsync(h, a.ts, sizeof(h), cudaMemcpyDeviceToHost, s);
+    cudaStreamSynchronize(s);
+    fprintf(stderr, "DCN_TSD");
+    for (int i = 0; i < 1024; ++i) fprintf(stderr, " %llu", h[i]);
+    fprintf(stderr, "\n");
   }
   BwdWeightArgs w;
   memset(&w, 0, sizeof(w));

@@ -29,7 +29,10 @@ namespace dcn {
 
 namespace {
 
-constexpr int kThreads = 448;
+#define DCN_TS(slot) \
+  do { if (a.ts && blockIdx.x == 0 && lane == 0 && (slot) < 1024) a.ts[(slot)] = globaltimer(); } while (0)
+
+constexpr int kThreads = 512;  // 4 warpgroups
 constexpr int kAWarps = 4;
 constexpr int kEpiWarp0 = 4;
 constexpr int kEpiWarps = 8;
@@ -99,9 +102,250 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = tmem_slot;
 
   const int nTiles = P.nPT;
+  if (warp == kMmaWarp) DCN_TS(1000);
   const int HoWo = P.HoWo;
 
-  if (warp < kAWarps) {
+  // Roles by warpgroup.  setmaxnreg sits at the top of each warpgroup's branch
+  // (one instruction per warpgroup): the two epilogue warpgroups grow to 200
+  // registers, the loader/idle and control warpgroups shrink to 56.
+  if (warp >= kEpiWarp0 && warp < kTmaWarp) {
+    regs_inc<200>();
+    // ------------------------------------------------ epilogue
+    // Per unit (tap t, group g, channel chunk cch) and per pass of CB channels:
+    //  A) TMEM -> smem transpose buffer (thread = pixel row); after the last pass
+    //     the TMEM buffer goes back to the MMA warp;
+    //  B) 8 lanes per pixel, each on 8 channels of the pixel's corner lines:
+    //     gather the 4 corners, reduce bilinear / d/dh / d/dw against gcol, and
+    //     scatter gcol * mask * corner weight with vector red.add.
+    // Geometry: lane r < 16 of epilogue warp e owns row 16e + r (offsets
+    // prefetched one (tap, group) ahead) and broadcasts it to the gather lanes.
+    using GS = GatherShape<T>;
+    constexpr int LPP = GS::kLPP, PPI = GS::kPPI, LD = GS::kLD;
+    constexpr int ITER = 16 / PPI;                // pixels per lane and pass
+    constexpr int BATCH = sizeof(T) == 4 ? 2 : 4;
+    const int ew = warp - kEpiWarp0;              // 0..7
+    const int q4 = warp & 3;                      // TMEM lane quarter
+    const int lp = lane / LPP, q = lane % LPP;
+    const int CB = a.tb_ch;                       // channels per pass (64 or 128)
+    const int npass = NC / CB;
+    const uint32_t tbuf = abase + (uint32_t)RA * aSlot;  // [128][CB] fp32, chunk-swizzled
+    const uint32_t rowB = (uint32_t)CB * 4u;
+    const T* __restrict__ xt = reinterpret_cast<const T*>(a.xt);
+    const T* __restrict__ off = reinterpret_cast<const T*>(a.offset);
+    const T* __restrict__ msk = reinterpret_cast<const T*>(a.mask);
+    T* __restrict__ goff = reinterpret_cast<T*>(a.goffset);
+    T* __restrict__ gmsk = reinterpret_cast<T*>(a.gmask);
+    const int HW = P.H * P.W;
+    const int nTG = P.K2 * P.dg;
+    uint32_t ucnt = 0, trcnt = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < nTiles && ok; tile += gridDim.x) {
+      // this lane's geometry row
+      const long long mpix = (long long)tile * kTileM + ew * 16 + (lane & 15);
+      const bool mpv = mpix < P.totalP;
+      const int mb = mpv ? (int)(mpix / HoWo) : 0;
+      const int mp = mpv ? (int)(mpix - (long long)mb * HoWo) : 0;
+      const int mho = mp / P.Wo, mwo = mp - mho * P.Wo;
+      T rh = T(), rw = T(), rm = T();
+      auto fetch_raw = [&](int tg) {
+        if (!mpv) return;
+        const int t = tg / P.dg, g = tg - t * P.dg;
+        const int ob = ((mb * P.dg + g) * 2 * P.K2 + 2 * t) * HoWo + mp;
+        rh = off[ob];
+        rw = off[ob + HoWo];
+        rm = msk[((mb * P.dg + g) * P.K2 + t) * HoWo + mp];
+      };
+      fetch_raw(0);
+      float racc[ITER][3];
+      int gidx[ITER];
+      float glh[ITER], glw[ITER], gm[ITER];
+      uint32_t gval[ITER];
+      for (int u = 0; u < P.nU && ok; ++u, ++ucnt) {
+        const int tg = u / P.nCC;
+        const int cch = u - tg * P.nCC;
+        const int t = tg / P.dg, g = tg - t * P.dg;
+        if (cch == 0) {
+          const int i = t / P.kw, j = t - i * P.kw;
+          int mi = 0;
+          float mlh = 0.f, mlw = 0.f, mm = 0.f;
+          uint32_t mval = 0u;
+          if (mpv) {
+            const float h = (float)(mho * P.sh - P.ph + i * P.dh) + Elem<T>::to_f(rh);
+            const float w = (float)(mwo * P.sw - P.pw + j * P.dw) + Elem<T>::to_f(rw);
+            mm = Elem<T>::to_f(rm);
+            const float hf = floorf(h), wf = floorf(w);
+            const int hl = (int)hf, wl = (int)wf;
+            mlh = h - hf;
+            mlw = w - wf;
+            if ((h > -1.f) && (w > -1.f) && (h < (float)P.H) && (w < (float)P.W) && !(a.dbg & 1)) {
+              const bool r0 = hl >= 0, r1 = hl + 1 <= P.H - 1, c0 = wl >= 0, c1 = wl + 1 <= P.W - 1;
+              mval = (r0 && c0 ? 1u : 0u) | (r0 && c1 ? 2u : 0u) | (r1 && c0 ? 4u : 0u) |
+                     (r1 && c1 ? 8u : 0u);
+              mi = mb * HW + hl * P.W + wl;
+            }
+          }
+          if (tg + 1 < nTG) fetch_raw(tg + 1);
+#pragma unroll
+          for (int it = 0; it < ITER; ++it) {
+            const int src = it * PPI + lp;
+            racc[it][0] = racc[it][1] = racc[it][2] = 0.f;
+            gidx[it] = __shfl_sync(0xffffffffu, mi, src);
+            glh[it] = __shfl_sync(0xffffffffu, mlh, src);
+            glw[it] = __shfl_sync(0xffffffffu, mlw, src);
+            gm[it] = __shfl_sync(0xffffffffu, mm, src);
+            gval[it] = __shfl_sync(0xffffffffu, mval, src);
+          }
+        }
+        if (ew == 0) DCN_TS(4 * ucnt);
+        const int ab = ucnt & 1;
+        if (!mbar_wait(accf0 + 8 * ab, (ucnt >> 1) & 1, a.err, &abort_flag)) { ok = false; break; }
+        if (ew == 0) DCN_TS(4 * ucnt + 1);
+        tc_fence_after();
+        for (int pass = 0; pass < npass && ok; ++pass, ++trcnt) {
+          const int c0ch = cch * NC + pass * CB;  // first channel (within the group) of the pass
+          int cend = P.Cgp - c0ch;
+          if (cend > CB) cend = CB;
+          // ---- A: TMEM -> transpose buffer
+          if (!mbar_wait(tre, (trcnt & 1) ^ 1u, a.err, &abort_flag)) { ok = false; break; }
+          {
+            const int row = q4 * 32 + lane;
+            const uint32_t tb =
+                tmem_base + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(ab * NC + pass * CB);
+            const int half = ew >> 2;
+            const uint32_t rbase = tbuf + (uint32_t)row * rowB;
+            const uint32_t sw = (uint32_t)(row & 7);
+            for (int c0 = half * (CB / 2); c0 < (half + 1) * (CB / 2); c0 += 16) {
+              float v[16];
+              tmem_ld16(tb + c0, v);
+              const uint32_t ck = (uint32_t)(c0 >> 2);  // 16-byte chunk index
+#pragma unroll
+              for (int k = 0; k < 4; ++k)
+                sts_v4(rbase + (((ck + k) ^ sw) << 4),
+                       make_uint4(__float_as_uint(v[4 * k]), __float_as_uint(v[4 * k + 1]),
+                                  __float_as_uint(v[4 * k + 2]), __float_as_uint(v[4 * k + 3])));
+            }
+          }
+          if (pass == npass - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acce0 + 8 * ab);
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(trf);
+          if (!mbar_wait(trf, trcnt & 1, a.err, &abort_flag)) { ok = false; break; }
+          if (ew == 0) DCN_TS(4 * ucnt + 2);
+          // ---- B: gather, reduce, scatter (all corner loads of a batch in flight)
+          const int d[4] = {0, 1, P.W, P.W + 1};
+          for (int cs = 0; cs < cend; cs += kChunk) {
+            // lane q owns channels [4q, 4q+4) and [32+4q, 32+4q+4) of the 64-channel
+            // block, so each red.add instruction of a pixel's 8 lanes covers whole
+            // 32-byte sectors (two lanes per sector)
+            const int ch = cs + q * 4;                 // first group (within the pass)
+            const int cofs = g * P.Cgp + c0ch + ch;
+#pragma unroll
+            for (int i0 = 0; i0 < ITER; i0 += BATCH) {
+              uint4 raw[BATCH][4][LD];
+              float gc[BATCH][8];
+#pragma unroll
+              for (int k = 0; k < BATCH; ++k) {
+                const int it = i0 + k;
+                const int row = ew * 16 + it * PPI + lp;
+                const uint32_t rbase = tbuf + (uint32_t)row * rowB;
+                const uint32_t ck = (uint32_t)(ch >> 2), sw = (uint32_t)(row & 7);
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                  uint4 r4;
+                  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                               : "=r"(r4.x), "=r"(r4.y), "=r"(r4.z), "=r"(r4.w)
+                               : "r"(rbase + (((ck + 8 * h) ^ sw) << 4)));
+                  gc[k][4 * h + 0] = __uint_as_float(r4.x);
+                  gc[k][4 * h + 1] = __uint_as_float(r4.y);
+                  gc[k][4 * h + 2] = __uint_as_float(r4.z);
+                  gc[k][4 * h + 3] = __uint_as_float(r4.w);
+                }
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                  const T* src = xt + (size_t)(unsigned)((gidx[it] + d[c]) * P.CS + cofs);
+                  const bool on = (gval[it] & (1u << c)) != 0u;
+                  if constexpr (LD == 2) {
+                    raw[k][c][0] = on ? ldg_nc_v4(src) : make_uint4(0u, 0u, 0u, 0u);
+                    raw[k][c][LD - 1] = on ? ldg_nc_v4(src + 32) : make_uint4(0u, 0u, 0u, 0u);
+                  } else {
+                    const uint2 lo = on ? ldg_nc_v2(src) : make_uint2(0u, 0u);
+                    const uint2 hi = on ? ldg_nc_v2(src + 32) : make_uint2(0u, 0u);
+                    raw[k][c][0] = make_uint4(lo.x, lo.y, hi.x, hi.y);
+                  }
+                }
+              }
+#pragma unroll
+              for (int k = 0; k < BATCH; ++k) {
+                const int it = i0 + k;
+                if (gval[it] == 0u) continue;
+                // S_c = sum_e gcol_e * corner_c[e]; bilinear and its h/w derivatives
+                // are linear in the corners, so the three channel sums follow from S
+                float S[4];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                  float vv[8];
+                  unpack_slice<T>(raw[k][c], vv);
+                  float acc = 0.f;
+#pragma unroll
+                  for (int e = 0; e < 8; ++e) acc = fmaf(gc[k][e], vv[e], acc);
+                  S[c] = acc;
+                }
+                const float lh = glh[it], lw = glw[it], hh = 1.f - lh, hw = 1.f - lw;
+                const float bw[4] = {(gval[it] & 1u) ? hh * hw : 0.f, (gval[it] & 2u) ? hh * lw : 0.f,
+                                     (gval[it] & 4u) ? lh * hw : 0.f, (gval[it] & 8u) ? lh * lw : 0.f};
+                const float am = bw[0] * S[0] + bw[1] * S[1] + bw[2] * S[2] + bw[3] * S[3];
+                const float ah = hw * (S[2] - S[0]) + lw * (S[3] - S[1]);
+                const float aw = hh * (S[1] - S[0]) + lh * (S[3] - S[2]);
+                racc[it][0] += am;
+                racc[it][1] += ah;
+                racc[it][2] += aw;
+                const float m = gm[it];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                  if ((gval[it] & (1u << c)) && !(a.dbg & 2)) {
+                    const float sk = bw[c] * m;
+                    float* dst = a.gx_nhwc + (size_t)(unsigned)((gidx[it] + d[c]) * P.CS + cofs);
+                    red_add_v4(dst, gc[k][0] * sk, gc[k][1] * sk, gc[k][2] * sk, gc[k][3] * sk);
+                    red_add_v4(dst + 32, gc[k][4] * sk, gc[k][5] * sk, gc[k][6] * sk, gc[k][7] * sk);
+                  }
+                }
+              }
+            }
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(tre);
+          if (ew == 0) DCN_TS(4 * ucnt + 3);
+        }
+        if (!ok) break;
+        if (cch == P.nCC - 1) {
+          // reduce each pixel's per-lane partials; write grad_offset / grad_mask
+#pragma unroll
+          for (int it = 0; it < ITER; ++it) {
+            float r0 = racc[it][0], r1 = racc[it][1], r2 = racc[it][2];
+#pragma unroll
+            for (int sh = 1; sh < LPP; sh <<= 1) {
+              r0 += __shfl_xor_sync(0xffffffffu, r0, sh);
+              r1 += __shfl_xor_sync(0xffffffffu, r1, sh);
+              r2 += __shfl_xor_sync(0xffffffffu, r2, sh);
+            }
+            const long long pix = (long long)tile * kTileM + ew * 16 + it * PPI + lp;
+            if (q == 0 && pix < P.totalP) {
+              const int b = (int)(pix / HoWo), p = (int)(pix - (long long)b * HoWo);
+              const size_t gbi = (size_t)b * P.dg + g;
+              goff[((gbi * P.K2 + t) * 2 + 0) * HoWo + p] = Elem<T>::from_f(r1 * gm[it]);
+              goff[((gbi * P.K2 + t) * 2 + 1) * HoWo + p] = Elem<T>::from_f(r2 * gm[it]);
+              gmsk[(gbi * P.K2 + t) * HoWo + p] = Elem<T>::from_f(r0);
+            }
+          }
+        }
+      }
+    }
+  } else {
+    regs_dec<56>();
+    if (warp < kAWarps) {
     // ------------------------------------------------ grad_out chunk loader
     // One thread bulk-copies the two pre-packed 64-pixel blocks of each Co chunk
     // (K-major, 128-byte swizzle; f32: hi and lo) into the A ring.
@@ -128,208 +372,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp < kTmaWarp) {
-    // ------------------------------------------------ epilogue
-    // Per unit (tap t, group g, channel chunk cch) and per pass of CB channels:
-    //  A) TMEM -> smem transpose buffer (thread = pixel row); after the last pass
-    //     the TMEM buffer goes back to the MMA warp;
-    //  B) 8 lanes per pixel, each on 8 channels of the pixel's corner lines:
-    //     gather the 4 corners, reduce bilinear / d/dh / d/dw against gcol, and
-    //     scatter gcol * mask * corner weight with vector red.add.
-    using GS = GatherShape<T>;
-    constexpr int LPP = GS::kLPP, PPI = GS::kPPI, LD = GS::kLD;
-    constexpr int ITER = 16 / PPI;                // pixels per lane and pass
-    const int ew = warp - kEpiWarp0;              // 0..7
-    const int q4 = warp & 3;                      // TMEM lane quarter
-    const int lp = lane / LPP, q = lane % LPP;
-    const int CB = a.tb_ch;                       // channels per pass (64 or 128)
-    const int npass = NC / CB;
-    const uint32_t tbuf = abase + (uint32_t)RA * aSlot;  // [128][CB] fp32, chunk-swizzled
-    const uint32_t rowB = (uint32_t)CB * 4u;
-    const T* __restrict__ xt = reinterpret_cast<const T*>(a.xt);
-    const T* __restrict__ off = reinterpret_cast<const T*>(a.offset);
-    const T* __restrict__ msk = reinterpret_cast<const T*>(a.mask);
-    T* __restrict__ goff = reinterpret_cast<T*>(a.goffset);
-    T* __restrict__ gmsk = reinterpret_cast<T*>(a.gmask);
-    const size_t img = (size_t)P.H * P.W;
-    uint32_t ucnt = 0, trcnt = 0;
-    bool ok = true;
-    for (int tile = blockIdx.x; tile < nTiles && ok; tile += gridDim.x) {
-      int pb[ITER], pp[ITER];
-#pragma unroll
-      for (int it = 0; it < ITER; ++it) {
-        const long long pix = (long long)tile * kTileM + ew * 16 + it * PPI + lp;
-        if (pix < P.totalP) {
-          pb[it] = (int)(pix / HoWo);
-          pp[it] = (int)(pix - (long long)pb[it] * HoWo);
-        } else {
-          pb[it] = 0;
-          pp[it] = -1;
-        }
-      }
-      float racc[ITER][3];
-      int cbase[ITER];
-      float clh[ITER], clw[ITER], cm[ITER];
-      uint32_t cval[ITER];
-      for (int u = 0; u < P.nU && ok; ++u, ++ucnt) {
-        const int tg = u / P.nCC;
-        const int cch = u - tg * P.nCC;
-        const int t = tg / P.dg, g = tg - t * P.dg;
-        if (cch == 0) {
-          const int i = t / P.kw, j = t - i * P.kw;
-#pragma unroll
-          for (int it = 0; it < ITER; ++it) {
-            racc[it][0] = racc[it][1] = racc[it][2] = 0.f;
-            cval[it] = 0u;
-            cbase[it] = 0;
-            clh[it] = clw[it] = cm[it] = 0.f;
-            if (pp[it] >= 0) {
-              const int p = pp[it], ho = p / P.Wo, wo = p - ho * P.Wo;
-              const size_t ob = ((size_t)pb[it] * P.dg + g) * 2 * P.K2;
-              const float h = (float)(ho * P.sh - P.ph + i * P.dh) + ldf(off + (ob + 2 * t) * HoWo + p);
-              const float w = (float)(wo * P.sw - P.pw + j * P.dw) + ldf(off + (ob + 2 * t + 1) * HoWo + p);
-              cm[it] = ldf(msk + (((size_t)pb[it] * P.dg + g) * P.K2 + t) * HoWo + p);
-              const float hf = floorf(h), wf = floorf(w);
-              const int hl = (int)hf, wl = (int)wf;
-              clh[it] = h - hf;
-              clw[it] = w - wf;
-              if ((h > -1.f) && (w > -1.f) && (h < (float)P.H) && (w < (float)P.W)) {
-                const bool r0 = hl >= 0, r1 = hl + 1 <= P.H - 1, c0 = wl >= 0, c1 = wl + 1 <= P.W - 1;
-                cval[it] = (r0 && c0 ? 1u : 0u) | (r0 && c1 ? 2u : 0u) | (r1 && c0 ? 4u : 0u) |
-                           (r1 && c1 ? 8u : 0u);
-                cbase[it] = hl * P.W + wl;
-              }
-              if (a.dbg & 1) cval[it] = 0u;
-            }
-          }
-        }
-        const int ab = ucnt & 1;
-        if (!mbar_wait(accf0 + 8 * ab, (ucnt >> 1) & 1, a.err, &abort_flag)) { ok = false; break; }
-        tc_fence_after();
-        for (int pass = 0; pass < npass && ok; ++pass, ++trcnt) {
-          const int c0ch = cch * NC + pass * CB;  // first channel (within the group) of the pass
-          int cend = P.Cgp - c0ch;
-          if (cend > CB) cend = CB;
-          // ---- A: TMEM -> transpose buffer
-          if (!mbar_wait(tre, (trcnt & 1) ^ 1u, a.err, &abort_flag)) { ok = false; break; }
-          {
-            const int row = q4 * 32 + lane;
-            const uint32_t tb =
-                tmem_base + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(ab * NC + pass * CB);
-            const int half = ew >> 2;
-            const uint32_t rbase = tbuf + (uint32_t)row * rowB;
-            const uint32_t sw = (uint32_t)(row & 7);
-            for (int c0 = half * (CB / 2); c0 < (half + 1) * (CB / 2); c0 += 8) {
-              float v[8];
-              tmem_ld8(tb + c0, v);
-              const uint32_t ck = (uint32_t)(c0 >> 2);  // 16-byte chunk index
-              sts_v4(rbase + ((ck ^ sw) << 4), make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]),
-                                                           __float_as_uint(v[2]), __float_as_uint(v[3])));
-              sts_v4(rbase + (((ck + 1) ^ sw) << 4),
-                     make_uint4(__float_as_uint(v[4]), __float_as_uint(v[5]), __float_as_uint(v[6]),
-                                __float_as_uint(v[7])));
-            }
-          }
-          if (pass == npass - 1) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(acce0 + 8 * ab);
-          }
-          __syncwarp();
-          if (lane == 0) mbar_arrive(trf);
-          if (!mbar_wait(trf, trcnt & 1, a.err, &abort_flag)) { ok = false; break; }
-          // ---- B: gather, reduce, scatter
-          for (int cs = 0; cs < cend; cs += kChunk) {
-#pragma unroll
-            for (int it = 0; it < ITER; ++it) {
-              if (cval[it] == 0u) continue;
-              const int row = ew * 16 + it * PPI + lp;
-              const int ch = cs + q * 8;  // channel within the pass
-              float gc[8];
-              {
-                const uint32_t rbase = tbuf + (uint32_t)row * rowB;
-                const uint32_t ck = (uint32_t)(ch >> 2), sw = (uint32_t)(row & 7);
-#pragma unroll
-                for (int k = 0; k < 2; ++k) {
-                  uint4 r4;
-                  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-                               : "=r"(r4.x), "=r"(r4.y), "=r"(r4.z), "=r"(r4.w)
-                               : "r"(rbase + (((ck + k) ^ sw) << 4)));
-                  gc[4 * k + 0] = __uint_as_float(r4.x);
-                  gc[4 * k + 1] = __uint_as_float(r4.y);
-                  gc[4 * k + 2] = __uint_as_float(r4.z);
-                  gc[4 * k + 3] = __uint_as_float(r4.w);
-                }
-              }
-              const int d[4] = {0, 1, P.W, P.W + 1};
-              const size_t pixbase = (size_t)pb[it] * img + cbase[it];
-              const size_t cofs = (size_t)g * P.Cgp + c0ch + ch;
-              uint4 raw[4][LD];
-#pragma unroll
-              for (int k = 0; k < 4; ++k)
-#pragma unroll
-                for (int l = 0; l < LD; ++l)
-                  raw[k][l] = (cval[it] & (1u << k))
-                                  ? ldg_nc_v4(xt + (pixbase + d[k]) * P.CS + cofs + l * (8 / LD))
-                                  : make_uint4(0u, 0u, 0u, 0u);
-              float vv[4][8];
-#pragma unroll
-              for (int k = 0; k < 4; ++k) unpack_slice<T>(raw[k], vv[k]);
-              const float lh = clh[it], lw = clw[it], hh = 1.f - lh, hw = 1.f - lw;
-              const float bw[4] = {(cval[it] & 1u) ? hh * hw : 0.f, (cval[it] & 2u) ? hh * lw : 0.f,
-                                   (cval[it] & 4u) ? lh * hw : 0.f, (cval[it] & 8u) ? lh * lw : 0.f};
-              float am = 0.f, ah = 0.f, aw = 0.f;
-#pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                const float bil = bw[0] * vv[0][e] + bw[1] * vv[1][e] + bw[2] * vv[2][e] + bw[3] * vv[3][e];
-                const float dh = hw * (vv[2][e] - vv[0][e]) + lw * (vv[3][e] - vv[1][e]);
-                const float dw = hh * (vv[1][e] - vv[0][e]) + lh * (vv[3][e] - vv[2][e]);
-                am = fmaf(gc[e], bil, am);
-                ah = fmaf(gc[e], dh, ah);
-                aw = fmaf(gc[e], dw, aw);
-              }
-              racc[it][0] += am;
-              racc[it][1] += ah;
-              racc[it][2] += aw;
-              const float m = cm[it];
-#pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                if ((cval[it] & (1u << k)) && !(a.dbg & 2)) {
-                  const float sk = bw[k] * m;
-                  float* dst = a.gx_nhwc + (pixbase + d[k]) * P.CS + cofs;
-                  red_add_v4(dst, gc[0] * sk, gc[1] * sk, gc[2] * sk, gc[3] * sk);
-                  red_add_v4(dst + 4, gc[4] * sk, gc[5] * sk, gc[6] * sk, gc[7] * sk);
-                }
-              }
-            }
-          }
-          __syncwarp();
-          if (lane == 0) mbar_arrive(tre);
-        }
-        if (!ok) break;
-        if (cch == P.nCC - 1) {
-          // reduce each pixel's per-lane partials; write grad_offset / grad_mask
-#pragma unroll
-          for (int it = 0; it < ITER; ++it) {
-            float r0 = racc[it][0], r1 = racc[it][1], r2 = racc[it][2];
-#pragma unroll
-            for (int sh = 1; sh < LPP; sh <<= 1) {
-              r0 += __shfl_xor_sync(0xffffffffu, r0, sh);
-              r1 += __shfl_xor_sync(0xffffffffu, r1, sh);
-              r2 += __shfl_xor_sync(0xffffffffu, r2, sh);
-            }
-            if (q == 0 && pp[it] >= 0) {
-              const size_t gb = (size_t)pb[it] * P.dg + g;
-              const int p = pp[it];
-              goff[((gb * P.K2 + t) * 2 + 0) * HoWo + p] = Elem<T>::from_f(r1 * cm[it]);
-              goff[((gb * P.K2 + t) * 2 + 1) * HoWo + p] = Elem<T>::from_f(r2 * cm[it]);
-              gmsk[(gb * P.K2 + t) * HoWo + p] = Elem<T>::from_f(r0);
-            }
-          }
-        }
-      }
-    }
-  } else if (warp == kTmaWarp) {
+    } else if (warp == kTmaWarp) {
     // ------------------------------------------------ W^T tiles (bulk copy)
     if (lane == 0) {
       uint32_t kidx = 0;
@@ -348,9 +391,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else {
+    } else {
     // ------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    if (warp == kMmaWarp && lane == 0) {
       const uint32_t idesc = make_idesc(OpOf<T>::kBF16, 0, 0, kTileM, NC);
       uint32_t kidx = 0, ucnt = 0, aseq0 = 0;
       bool ok = true;
@@ -384,6 +427,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
             umma_commit(empty0 + 8 * s);
+            DCN_TS(600 + ucnt);
             if (!resident || u == P.nU - 1) umma_commit(aempty0 + 8 * r);
           }
           if (!ok) break;
@@ -394,8 +438,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       umma_commit(drain);
       mbar_wait_drain(drain, 0, a.err);
     }
+    }
   }
-
   tc_fence_before();
   __syncthreads();
   if (warp == kMmaWarp) {

@@ -30,6 +30,7 @@ struct FwdArgs {
 
 struct BwdDataArgs {
   Plan plan;
+  unsigned long long* ts;  // optional pipeline timestamps of CTA 0 (DCN_DEBUG_TS), else null
   const void* xt;       // packed NHWC input
   const void* offset;
   const void* mask;
