@@ -141,50 +141,73 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int tile = blockIdx.x; tile < nTiles && ok; tile += gridDim.x) {
       // this lane's geometry row
-      const long long mpix = (long long)tile * kTileM + ew * 16 + (lane & 15);
+      const int mpix = tile * kTileM + ew * 16 + (lane & 15);
       const bool mpv = mpix < P.totalP;
       const int mb = mpv ? (int)(mpix / HoWo) : 0;
-      const int mp = mpv ? (int)(mpix - (long long)mb * HoWo) : 0;
+      const int mp = mpv ? (int)(mpix - mb * HoWo) : 0;
       const int mho = mp / P.Wo, mwo = mp - mho * P.Wo;
-      T rh = T(), rw = T(), rm = T();
+      uint32_t rh = 0, rw = 0, rm = 0;  // raw prefetched offset / mask bits
       auto fetch_raw = [&](int tg) {
         if (!mpv) return;
         const int t = tg / P.dg, g = tg - t * P.dg;
         const int ob = ((mb * P.dg + g) * 2 * P.K2 + 2 * t) * HoWo + mp;
-        rh = off[ob];
-        rw = off[ob + HoWo];
-        rm = msk[((mb * P.dg + g) * P.K2 + t) * HoWo + mp];
+        rh = ldg_raw<T>(off + (ob));
+        rw = ldg_raw<T>(off + (ob + HoWo));
+        rm = ldg_raw<T>(msk + (((mb * P.dg + g) * P.K2 + t) * HoWo + mp));
       };
       fetch_raw(0);
+      // grad_offset / grad_mask bases (offset[b][0][p], mask[b][0][p]) of this lane's
+      // pixels, -1 for padding rows
+      int wob[ITER], wmb[ITER];
+#pragma unroll
+      for (int it = 0; it < ITER; ++it) {
+        const int pix = tile * kTileM + ew * 16 + it * PPI + lp;
+        wob[it] = wmb[it] = -1;
+        if (pix < P.totalP) {
+          const int b = pix / HoWo, p = pix - b * HoWo;
+          wob[it] = b * P.dg * 2 * P.K2 * HoWo + p;
+          wmb[it] = b * P.dg * P.K2 * HoWo + p;
+        }
+      }
       float racc[ITER][3];
       int gidx[ITER];
       float glh[ITER], glw[ITER], gm[ITER];
       uint32_t gval[ITER];
+      // this lane's row geometry for (tap, group) tg from the prefetched raw values
+      // (and the prefetch of tg + 1)
+      int mi = 0;
+      float mlh = 0.f, mlw = 0.f, mm = 0.f;
+      uint32_t mval = 0u;
+      auto compute_mine = [&](int tg) {
+        const int t = tg / P.dg;
+        const int i = t / P.kw, j = t - i * P.kw;
+        mi = 0;
+        mlh = mlw = mm = 0.f;
+        mval = 0u;
+        if (mpv) {
+          const float h = (float)(mho * P.sh - P.ph + i * P.dh) + raw_to_f<T>(rh);
+          const float w = (float)(mwo * P.sw - P.pw + j * P.dw) + raw_to_f<T>(rw);
+          mm = raw_to_f<T>(rm);
+          const float hf = floorf(h), wf = floorf(w);
+          const int hl = (int)hf, wl = (int)wf;
+          mlh = h - hf;
+          mlw = w - wf;
+          if ((h > -1.f) && (w > -1.f) && (h < (float)P.H) && (w < (float)P.W) && !(a.dbg & 1)) {
+            const bool r0 = hl >= 0, r1 = hl + 1 <= P.H - 1, c0 = wl >= 0, c1 = wl + 1 <= P.W - 1;
+            mval = (r0 && c0 ? 1u : 0u) | (r0 && c1 ? 2u : 0u) | (r1 && c0 ? 4u : 0u) |
+                   (r1 && c1 ? 8u : 0u);
+            mi = mb * HW + hl * P.W + wl;
+          }
+        }
+        if (tg + 1 < nTG) fetch_raw(tg + 1);
+      };
+      compute_mine(0);
       for (int u = 0; u < P.nU && ok; ++u, ++ucnt) {
         const int tg = u / P.nCC;
         const int cch = u - tg * P.nCC;
         const int t = tg / P.dg, g = tg - t * P.dg;
         if (cch == 0) {
-          const int i = t / P.kw, j = t - i * P.kw;
-          int mi = 0;
-          float mlh = 0.f, mlw = 0.f, mm = 0.f;
-          uint32_t mval = 0u;
-          if (mpv) {
-            const float h = (float)(mho * P.sh - P.ph + i * P.dh) + Elem<T>::to_f(rh);
-            const float w = (float)(mwo * P.sw - P.pw + j * P.dw) + Elem<T>::to_f(rw);
-            mm = Elem<T>::to_f(rm);
-            const float hf = floorf(h), wf = floorf(w);
-            const int hl = (int)hf, wl = (int)wf;
-            mlh = h - hf;
-            mlw = w - wf;
-            if ((h > -1.f) && (w > -1.f) && (h < (float)P.H) && (w < (float)P.W) && !(a.dbg & 1)) {
-              const bool r0 = hl >= 0, r1 = hl + 1 <= P.H - 1, c0 = wl >= 0, c1 = wl + 1 <= P.W - 1;
-              mval = (r0 && c0 ? 1u : 0u) | (r0 && c1 ? 2u : 0u) | (r1 && c0 ? 4u : 0u) |
-                     (r1 && c1 ? 8u : 0u);
-              mi = mb * HW + hl * P.W + wl;
-            }
-          }
-          if (tg + 1 < nTG) fetch_raw(tg + 1);
+          if (tg > 0) compute_mine(tg);
 #pragma unroll
           for (int it = 0; it < ITER; ++it) {
             const int src = it * PPI + lp;
@@ -320,6 +343,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (ew == 0) DCN_TS(4 * ucnt + 3);
         }
         if (!ok) break;
+        if (ew == 0) DCN_TS(400 + 2 * ucnt);
         if (cch == P.nCC - 1) {
           // reduce each pixel's per-lane partials; write grad_offset / grad_mask
 #pragma unroll
@@ -331,13 +355,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               r1 += __shfl_xor_sync(0xffffffffu, r1, sh);
               r2 += __shfl_xor_sync(0xffffffffu, r2, sh);
             }
-            const long long pix = (long long)tile * kTileM + ew * 16 + it * PPI + lp;
-            if (q == 0 && pix < P.totalP) {
-              const int b = (int)(pix / HoWo), p = (int)(pix - (long long)b * HoWo);
-              const size_t gbi = (size_t)b * P.dg + g;
-              goff[((gbi * P.K2 + t) * 2 + 0) * HoWo + p] = Elem<T>::from_f(r1 * gm[it]);
-              goff[((gbi * P.K2 + t) * 2 + 1) * HoWo + p] = Elem<T>::from_f(r2 * gm[it]);
-              gmsk[(gbi * P.K2 + t) * HoWo + p] = Elem<T>::from_f(r0);
+            if (q == 0 && wob[it] >= 0) {
+              const int oo = wob[it] + (g * P.K2 + t) * 2 * HoWo;
+              goff[oo] = Elem<T>::from_f(r1 * gm[it]);
+              goff[oo + HoWo] = Elem<T>::from_f(r2 * gm[it]);
+              gmsk[wmb[it] + (g * P.K2 + t) * HoWo] = Elem<T>::from_f(r0);
             }
           }
         }

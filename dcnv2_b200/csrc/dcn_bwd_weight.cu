@@ -124,21 +124,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int nblk = NC / kChunk;
     const int ngeo = ucount * 8;                 // geometries per warp and K step
     const int niter = ucount * nblk * 2;         // 4-row gather iterations per K step
-    T rh[2], rw[2], rm[2];
+    uint32_t rh[2] = {0, 0}, rw[2] = {0, 0}, rm[2] = {0, 0};  // raw prefetched bits
     auto fetch_raw = [&](int ks) {
 #pragma unroll
       for (int sl = 0; sl < 2; ++sl) {
         const int item = lane + 32 * sl;
         if (item < ngeo) {
-          const long long pix = (long long)ks * 64 + warp * 8 + (item & 7);
+          const int pix = ks * 64 + warp * 8 + (item & 7);
           if (pix < P.totalP) {
             const int u = u0 + (item >> 3);
             const int tg = u / P.nCC, t = tg / P.dg, g = tg - t * P.dg;
-            const int b = (int)(pix / HoWo), p = (int)(pix - (long long)b * HoWo);
+            const int b = (int)(pix / HoWo), p = (int)(pix - b * HoWo);
             const int ob = ((b * P.dg + g) * 2 * P.K2 + 2 * t) * HoWo + p;
-            rh[sl] = off[ob];
-            rw[sl] = off[ob + HoWo];
-            rm[sl] = msk[((b * P.dg + g) * P.K2 + t) * HoWo + p];
+            rh[sl] = ldg_raw<T>(off + (ob));
+            rw[sl] = ldg_raw<T>(off + (ob + HoWo));
+            rm[sl] = ldg_raw<T>(msk + (((b * P.dg + g) * P.K2 + t) * HoWo + p));
           }
         }
       }
@@ -153,16 +153,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int sl = 0; sl < 2; ++sl) {
         mine[sl] = zero_pixgeo();
         const int item = lane + 32 * sl;
-        const long long pix = (long long)ks * 64 + warp * 8 + (item & 7);
+        const int pix = ks * 64 + warp * 8 + (item & 7);
         if (item < ngeo && pix < P.totalP && !(a.dbg & 1)) {
           const int u = u0 + (item >> 3);
           const int tg = u / P.nCC, t = tg / P.dg;
           const int i = t / P.kw, jj = t - i * P.kw;
-          const int b = (int)(pix / HoWo), p = (int)(pix - (long long)b * HoWo);
+          const int b = (int)(pix / HoWo), p = (int)(pix - b * HoWo);
           const int ho = p / P.Wo, wo = p - ho * P.Wo;
-          const float hs = (float)(ho * P.sh - P.ph + i * P.dh) + Elem<T>::to_f(rh[sl]);
-          const float ws = (float)(wo * P.sw - P.pw + jj * P.dw) + Elem<T>::to_f(rw[sl]);
-          mine[sl] = make_pixgeo(b * HW, hs, ws, Elem<T>::to_f(rm[sl]), P.H, P.W);
+          const float hs = (float)(ho * P.sh - P.ph + i * P.dh) + raw_to_f<T>(rh[sl]);
+          const float ws = (float)(wo * P.sw - P.pw + jj * P.dw) + raw_to_f<T>(rw[sl]);
+          mine[sl] = make_pixgeo(b * HW, hs, ws, raw_to_f<T>(rm[sl]), P.H, P.W);
         }
       }
       if (ks + 1 < ks1) fetch_raw(ks + 1);

@@ -315,6 +315,33 @@ __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
   return r;
 }
 
+// Raw element load issued where it is written (volatile asm is not moved to the
+// first use), for prefetching: 16-bit types as their bit pattern, f32 as bits.
+template <typename T>
+__device__ __forceinline__ uint32_t ldg_raw(const T* p) {
+  uint32_t r;
+  if constexpr (sizeof(T) == 2) {
+    unsigned short h;
+    asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(h) : "l"(p));
+    r = h;
+  } else {
+    asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(r) : "l"(p));
+  }
+  return r;
+}
+
+// Converts a raw element (see ldg_raw) to float.
+template <typename T>
+__device__ __forceinline__ float raw_to_f(uint32_t r) {
+  if constexpr (std::is_same<T, float>::value) {
+    return __uint_as_float(r);
+  } else if constexpr (std::is_same<T, __half>::value) {
+    return __half2float(__ushort_as_half((unsigned short)r));
+  } else {
+    return __uint_as_float(r << 16);
+  }
+}
+
 __device__ __forceinline__ uint2 ldg_nc_v2(const void* p) {
   uint2 r;
   asm volatile("ld.global.nc.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));

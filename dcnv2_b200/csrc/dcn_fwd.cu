@@ -116,24 +116,22 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     for (int tile = blockIdx.x; tile < nTiles && ok; tile += gridDim.x) {
       const int pt = tile / P.nCoT;
       // this lane's geometry row (lanes 16..31 mirror lanes 0..15)
-      const long long pix = (long long)pt * kTileM + warp * 16 + (lane & 15);
+      const int pix = pt * kTileM + warp * 16 + (lane & 15);
       const bool pv = pix < P.totalP;
       const int b = pv ? (int)(pix / HoWo) : 0;
-      const int p = pv ? (int)(pix - (long long)b * HoWo) : 0;
+      const int p = pv ? (int)(pix - b * HoWo) : 0;
       const int ho = p / P.Wo, wo = p - ho * P.Wo;
       const int obase = b * P.dg * 2 * P.K2 * HoWo + p;   // offset[b][0][p]
       const int mbase = b * P.dg * P.K2 * HoWo + p;       // mask[b][0][p]
-      T rh = T(), rw = T(), rm = T();
+      uint32_t rh = 0, rw = 0, rm = 0;  // raw prefetched offset / mask bits
       auto fetch_raw = [&](int tg) {
         const int t = tg / P.dg, g = tg - t * P.dg;
         if (pv && (a.dbg & 8)) {
-          rh = Elem<T>::from_f(0.25f);
-          rw = Elem<T>::from_f(0.25f);
-          rm = Elem<T>::from_f(0.5f);
+          rh = rw = rm = 0u;
         } else if (pv) {
-          rh = off[obase + (g * 2 * P.K2 + 2 * t) * HoWo];
-          rw = off[obase + (g * 2 * P.K2 + 2 * t + 1) * HoWo];
-          rm = msk[mbase + (g * P.K2 + t) * HoWo];
+          rh = ldg_raw<T>(off + (obase + (g * 2 * P.K2 + 2 * t) * HoWo));
+          rw = ldg_raw<T>(off + (obase + (g * 2 * P.K2 + 2 * t + 1) * HoWo));
+          rm = ldg_raw<T>(msk + (mbase + (g * P.K2 + t) * HoWo));
         }
       };
       const int nTG = P.K2 * P.dg;
@@ -147,9 +145,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           const int i = t / P.kw, j = t - i * P.kw;
           PixGeo mine = zero_pixgeo();
           if (pv && !(a.dbg & 1)) {
-            const float hs = (float)(ho * P.sh - P.ph + i * P.dh) + Elem<T>::to_f(rh);
-            const float ws = (float)(wo * P.sw - P.pw + j * P.dw) + Elem<T>::to_f(rw);
-            mine = make_pixgeo(b * HW, hs, ws, Elem<T>::to_f(rm), P.H, P.W);
+            const float hs = (float)(ho * P.sh - P.ph + i * P.dh) + raw_to_f<T>(rh);
+            const float ws = (float)(wo * P.sw - P.pw + j * P.dw) + raw_to_f<T>(rw);
+            mine = make_pixgeo(b * HW, hs, ws, raw_to_f<T>(rm), P.H, P.W);
           }
           if (tg + 1 < nTG) fetch_raw(tg + 1);
 #pragma unroll
@@ -192,14 +190,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       if (!mbar_wait(accf0 + 8 * ab, (it >> 1) & 1, a.err, &abort_flag)) break;
       if (warp == kEpiWarp0) DCN_TS(800 + 2 * it);
       tc_fence_after();
-      const long long pix = (long long)pt * kTileM + row;
+      const int pix = pt * kTileM + row;
       const bool pv = pix < P.totalP;
       const int b = pv ? (int)(pix / HoWo) : 0;
-      const int p = pv ? (int)(pix - (long long)b * HoWo) : 0;
+      const int p = pv ? (int)(pix - b * HoWo) : 0;
       T* yb = y + (size_t)b * P.Co * HoWo + p;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * NT);
       // vector path: the warp's 32 pixels form aligned 16-byte runs, each inside one image
-      const long long wpix0 = (long long)pt * kTileM + q * 32;
+      const int wpix0 = pt * kTileM + q * 32;
       const bool vec = a.vec_out && (HoWo % 8 == 0) && (wpix0 + 32 <= P.totalP);
       T* stg = reinterpret_cast<T*>(epi_stage[q]);
       constexpr int EPV = 16 / (int)sizeof(T);       // elements per 16-byte vector
@@ -219,8 +217,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             const int co = ct * NT + c0 + j;
             if (co < P.Co && !(a.dbg & 2)) {
               const uint4 val = *reinterpret_cast<const uint4*>(stg + j * 32 + cv * EPV);
-              const long long rp = wpix0 + cv * EPV;   // a run never crosses an image (HoWo % 8 == 0)
-              const int rb = (int)(rp / HoWo), rpp = (int)(rp - (long long)rb * HoWo);
+              const int rp = wpix0 + cv * EPV;   // a run never crosses an image (HoWo % 8 == 0)
+              const int rb = (int)(rp / HoWo), rpp = (int)(rp - rb * HoWo);
               *reinterpret_cast<uint4*>(y + ((size_t)rb * P.Co + co) * HoWo + rpp) = val;
             }
           }

@@ -11,7 +11,7 @@ namespace dcn {
 // tensor is 16-byte aligned, so the 8 pixels lie in one image and one line.
 template <typename T>
 __device__ __forceinline__ void load8_gout(const T* __restrict__ gout, const Plan& P,
-                                           long long pix0, int co, bool vec, float (&v)[8]) {
+                                           int pix0, int co, bool vec, float (&v)[8]) {
   if (co >= P.Co || pix0 >= P.totalP) {
 #pragma unroll
     for (int e = 0; e < 8; ++e) v[e] = 0.f;
@@ -19,7 +19,7 @@ __device__ __forceinline__ void load8_gout(const T* __restrict__ gout, const Pla
   }
   if (vec) {
     const int b = (int)(pix0 / P.HoWo);
-    const int p = (int)(pix0 - (long long)b * P.HoWo);
+    const int p = (int)(pix0 - b * P.HoWo);
     const T* src = gout + ((size_t)b * P.Co + co) * P.HoWo + p;
     if constexpr (std::is_same<T, float>::value) {
       const uint4 a = ldg_nc_v4(src), c = ldg_nc_v4(src + 4);
@@ -33,11 +33,11 @@ __device__ __forceinline__ void load8_gout(const T* __restrict__ gout, const Pla
   } else {
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      const long long pix = pix0 + e;
+      const int pix = pix0 + e;
       v[e] = 0.f;
       if (pix < P.totalP) {
         const int b = (int)(pix / P.HoWo);
-        const int p = (int)(pix - (long long)b * P.HoWo);
+        const int p = (int)(pix - b * P.HoWo);
         v[e] = ldf(gout + ((size_t)b * P.Co + co) * P.HoWo + p);
       }
     }
@@ -62,14 +62,14 @@ __device__ __forceinline__ uint4 ldg_v4(const void* p) {
 
 template <typename T>
 __device__ __forceinline__ void gout_raw_load(const T* __restrict__ gout, const Plan& P,
-                                              long long pix0, int co, GoutRaw<T>& g, bool plain = false) {
+                                              int pix0, int co, GoutRaw<T>& g, bool plain = false) {
   if (co >= P.Co || pix0 >= P.totalP) {
 #pragma unroll
     for (int k = 0; k < (int)(sizeof(T) / 2); ++k) g.r[k] = make_uint4(0u, 0u, 0u, 0u);
     return;
   }
   const int b = (int)(pix0 / P.HoWo);
-  const int p = (int)(pix0 - (long long)b * P.HoWo);
+  const int p = (int)(pix0 - b * P.HoWo);
   const T* src = gout + ((size_t)b * P.Co + co) * P.HoWo + p;
 #pragma unroll
   for (int k = 0; k < (int)(sizeof(T) / 2); ++k) g.r[k] = plain ? ldg_v4(src + k * 4) : ldg_nc_v4(src + k * 4);

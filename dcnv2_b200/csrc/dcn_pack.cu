@@ -153,10 +153,10 @@ __global__ void __launch_bounds__(256) pack_gout_kernel(const T* __restrict__ go
       const int co = ko * kChunk + col;
       if (vec) {
         GoutRaw<T> raw;
-        gout_raw_load<T>(gout, P, (long long)pb * 64 + ch * 8, co, raw);
+        gout_raw_load<T>(gout, P, pb * 64 + ch * 8, co, raw);
         gout_raw_to_f<T>(raw, v);
       } else {
-        load8_gout<T>(gout, P, (long long)pb * 64 + ch * 8, co, false, v);
+        load8_gout<T>(gout, P, pb * 64 + ch * 8, co, false, v);
       }
       bsum[k] += ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
 #pragma unroll
