@@ -12,29 +12,43 @@ namespace dcn {
 
 namespace {
 
-// [B][C][H*W] -> [B][H*W][dg][Cgp]; padded channels are written as zero.
+// [B][C][H*W] -> [B][H*W][dg][Cgp]; padded channels are written as zero.  One
+// CTA moves a 64-pixel x 64-channel block: 16-byte loads along pixels (when
+// `vec`: H*W % 8 == 0 and x 16-byte aligned), 16-byte stores along channels.
 template <typename T>
-__global__ void pack_input_kernel(const T* __restrict__ x, T* __restrict__ xt, int C, int HW,
-                                  int Cg, int Cgp, int CS) {
-  __shared__ float tile[32][33];
+__global__ void __launch_bounds__(256) pack_input_kernel(const T* __restrict__ x,
+                                                         T* __restrict__ xt, int C, int HW,
+                                                         int Cg, int Cgp, int CS, int vec) {
+  constexpr int EPV = 16 / (int)sizeof(T);           // elements per 16-byte vector
+  __shared__ __align__(16) T tile[64][64 + EPV];      // [channel][pixel]
   const int b = blockIdx.z;
-  const int d0 = blockIdx.y * 32;  // destination channel (in [0, CS))
-  const int p0 = blockIdx.x * 32;  // pixel
+  const int d0 = blockIdx.y * 64;                     // destination channel block
+  const int p0 = blockIdx.x * 64;
+  const int g = d0 / Cgp, cb = d0 - g * Cgp;
   const T* xb = x + (size_t)b * C * HW;
-  for (int k = threadIdx.y; k < 32; k += 8) {
-    const int d = d0 + k, p = p0 + threadIdx.x;
-    float v = 0.f;
-    if (d < CS && p < HW) {
-      const int g = d / Cgp, cc = d - g * Cgp;
-      if (cc < Cg) v = ldf(xb + (size_t)(g * Cg + cc) * HW + p);
+  const int tid = threadIdx.x;
+  for (int item = tid; item < 64 * (64 / EPV); item += 256) {
+    const int c = item / (64 / EPV), pv = item - c * (64 / EPV);
+    const int cc = cb + c, p = p0 + pv * EPV;
+    T* dst = &tile[c][pv * EPV];
+    if (cc < Cg && vec && p + EPV <= HW) {
+      *reinterpret_cast<uint4*>(dst) =
+          ldg_nc_v4(xb + (size_t)(g * Cg + cc) * HW + p);
+    } else {
+      for (int e = 0; e < EPV; ++e)
+        dst[e] = (cc < Cg && p + e < HW) ? xb[(size_t)(g * Cg + cc) * HW + p + e] : Elem<T>::from_f(0.f);
     }
-    tile[k][threadIdx.x] = v;
   }
   __syncthreads();
-  T* xo = xt + (size_t)b * HW * CS;
-  for (int k = threadIdx.y; k < 32; k += 8) {
-    const int p = p0 + k, d = d0 + threadIdx.x;
-    if (d < CS && p < HW) xo[(size_t)p * CS + d] = Elem<T>::from_f(tile[threadIdx.x][k]);
+  T* xo = xt + (size_t)b * HW * CS + d0;
+  for (int item = tid; item < 64 * (64 / EPV); item += 256) {
+    const int pl = item / (64 / EPV), cv = item - pl * (64 / EPV);
+    const int p = p0 + pl;
+    if (p >= HW) continue;
+    alignas(16) T v[EPV];
+#pragma unroll
+    for (int e = 0; e < EPV; ++e) v[e] = tile[cv * EPV + e][pl];
+    *reinterpret_cast<uint4*>(xo + (size_t)p * CS + cv * EPV) = *reinterpret_cast<const uint4*>(v);
   }
 }
 
@@ -204,29 +218,47 @@ __global__ void __launch_bounds__(256) pack_gout_kernel(const T* __restrict__ go
   }
 }
 
-// fp32 [B][H*W][dg][Cgp] -> T [B][C][H*W]
+// fp32 [B][H*W][dg][Cgp] -> T [B][C][H*W].  One CTA moves 64 pixels x 64
+// channels of one group block: 16-byte loads along channels, 16-byte stores
+// along pixels (when `vec`: H*W % 8 == 0 and gx 16-byte aligned).
 template <typename T>
-__global__ void finish_grad_input_kernel(const float* __restrict__ gxn, T* __restrict__ gx,
-                                         int C, int HW, int Cg, int Cgp, int CS) {
-  __shared__ float tile[32][33];
+__global__ void __launch_bounds__(256) finish_grad_input_kernel(const float* __restrict__ gxn,
+                                                                T* __restrict__ gx, int C, int HW,
+                                                                int Cg, int Cgp, int CS, int vec) {
+  constexpr int EPV = 16 / (int)sizeof(T);
+  __shared__ float tile[64][65];                      // [pixel][channel]
   const int b = blockIdx.z;
-  const int c0 = blockIdx.y * 32;
-  const int p0 = blockIdx.x * 32;
-  const float* src = gxn + (size_t)b * HW * CS;
-  for (int k = threadIdx.y; k < 32; k += 8) {
-    const int p = p0 + k, c = c0 + threadIdx.x;
-    float v = 0.f;
-    if (c < C && p < HW) {
-      const int g = c / Cg, cc = c - g * Cg;
-      v = src[(size_t)p * CS + g * Cgp + cc];
-    }
-    tile[k][threadIdx.x] = v;
+  const int d0 = blockIdx.y * 64;
+  const int p0 = blockIdx.x * 64;
+  const int g = d0 / Cgp, cb = d0 - g * Cgp;
+  const float* src = gxn + (size_t)b * HW * CS + d0;
+  const int tid = threadIdx.x;
+  for (int item = tid; item < 64 * 16; item += 256) {
+    const int pl = item >> 4, cv = item & 15;
+    const int p = p0 + pl;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (p < HW) v = *reinterpret_cast<const float4*>(src + (size_t)p * CS + cv * 4);
+    tile[pl][cv * 4 + 0] = v.x;
+    tile[pl][cv * 4 + 1] = v.y;
+    tile[pl][cv * 4 + 2] = v.z;
+    tile[pl][cv * 4 + 3] = v.w;
   }
   __syncthreads();
   T* dst = gx + (size_t)b * C * HW;
-  for (int k = threadIdx.y; k < 32; k += 8) {
-    const int c = c0 + k, p = p0 + threadIdx.x;
-    if (c < C && p < HW) dst[(size_t)c * HW + p] = Elem<T>::from_f(tile[threadIdx.x][k]);
+  for (int item = tid; item < 64 * (64 / EPV); item += 256) {
+    const int c = item / (64 / EPV), pv = item - c * (64 / EPV);
+    const int cc = cb + c;
+    if (cc >= Cg) continue;
+    const int p = p0 + pv * EPV;
+    T* o = dst + (size_t)(g * Cg + cc) * HW + p;
+    if (vec && p + EPV <= HW) {
+      alignas(16) T v[EPV];
+#pragma unroll
+      for (int e = 0; e < EPV; ++e) v[e] = Elem<T>::from_f(tile[pv * EPV + e][c]);
+      *reinterpret_cast<uint4*>(o) = *reinterpret_cast<const uint4*>(v);
+    } else {
+      for (int e = 0; e < EPV && p + e < HW; ++e) o[e] = Elem<T>::from_f(tile[pv * EPV + e][c]);
+    }
   }
 }
 
@@ -267,11 +299,12 @@ int grid_for(long long n, int threads) {
 
 int launch_pack_input(const Plan& P, const void* x, void* xt, cudaStream_t s) {
   const int HW = P.H * P.W;
-  dim3 grid(ceil_div(HW, 32), ceil_div(P.CS, 32), P.B), block(32, 8);
+  const int vec = (HW % 8 == 0) && (((uintptr_t)x & 15u) == 0);
+  dim3 grid(ceil_div(HW, 64), P.CS / 64, P.B);
   return dispatch(P.dtype, [&](auto tag) {
     using T = decltype(tag);
-    pack_input_kernel<T><<<grid, block, 0, s>>>(static_cast<const T*>(x), static_cast<T*>(xt),
-                                                P.C, HW, P.Cg, P.Cgp, P.CS);
+    pack_input_kernel<T><<<grid, 256, 0, s>>>(static_cast<const T*>(x), static_cast<T*>(xt), P.C,
+                                              HW, P.Cg, P.Cgp, P.CS, vec);
   });
 }
 
@@ -294,7 +327,7 @@ int launch_pack_weight_bwd(const Plan& P, const void* w, uint8_t* wpk, cudaStrea
 int launch_pack_gout(const Plan& P, const void* gout, uint8_t* gpk, float* gb, int vec,
                      cudaStream_t s) {
   const int nPB = (int)((P.totalP + 63) / 64);
-  int gx = 592 / P.nKo;   // about four CTAs per SM in total, pixel blocks strided
+  int gx = 2048 / P.nKo;  // about 14 CTAs per SM in total, pixel blocks strided
   if (gx < 1) gx = 1;
   if (gx > nPB) gx = nPB;
   dim3 grid(gx, P.nKo);
@@ -306,11 +339,12 @@ int launch_pack_gout(const Plan& P, const void* gout, uint8_t* gpk, float* gb, i
 
 int launch_finish_grad_input(const Plan& P, const float* gxn, void* gx, cudaStream_t s) {
   const int HW = P.H * P.W;
-  dim3 grid(ceil_div(HW, 32), ceil_div(P.C, 32), P.B), block(32, 8);
+  const int vec = (HW % 8 == 0) && (((uintptr_t)gx & 15u) == 0);
+  dim3 grid(ceil_div(HW, 64), P.CS / 64, P.B);
   return dispatch(P.dtype, [&](auto tag) {
     using T = decltype(tag);
-    finish_grad_input_kernel<T><<<grid, block, 0, s>>>(gxn, static_cast<T*>(gx), P.C, HW, P.Cg,
-                                                       P.Cgp, P.CS);
+    finish_grad_input_kernel<T><<<grid, 256, 0, s>>>(gxn, static_cast<T*>(gx), P.C, HW, P.Cg,
+                                                     P.Cgp, P.CS, vec);
   });
 }
 
