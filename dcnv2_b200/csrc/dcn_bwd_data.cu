@@ -260,11 +260,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           // ---- B: gather, reduce, scatter (all corner loads of a batch in flight)
           const int d[4] = {0, 1, P.W, P.W + 1};
           for (int cs = 0; cs < cend; cs += kChunk) {
-            // lane q owns channels [4q, 4q+4) and [32+4q, 32+4q+4) of the 64-channel
-            // block, so each red.add instruction of a pixel's 8 lanes covers whole
-            // 32-byte sectors (two lanes per sector)
-            const int ch = cs + q * 4;                 // first group (within the pass)
-            const int cofs = g * P.Cgp + c0ch + ch;
+            // lane q owns packed slice q = logical channels [4q, 4q+4) and
+            // [32+4q, 32+4q+4) of the 64-channel block (perm_logical): one 16-byte
+            // load per corner from the packed input, and each red.add instruction
+            // of a pixel's 8 lanes fills whole 32-byte sectors of grad_input
+            const int ch = cs + q * 8;                      // packed position in the pass
+            const int cofs = g * P.Cgp + c0ch + ch;         // packed input
+            const int lofs = g * P.Cgp + c0ch + cs + 4 * q;  // grad_input (logical order)
 #pragma unroll
             for (int i0 = 0; i0 < ITER; i0 += BATCH) {
               uint4 raw[BATCH][4][LD];
@@ -280,25 +282,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                   uint4 r4;
                   asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
                                : "=r"(r4.x), "=r"(r4.y), "=r"(r4.z), "=r"(r4.w)
-                               : "r"(rbase + (((ck + 8 * h) ^ sw) << 4)));
+                               : "r"(rbase + (((ck + h) ^ sw) << 4)));
                   gc[k][4 * h + 0] = __uint_as_float(r4.x);
                   gc[k][4 * h + 1] = __uint_as_float(r4.y);
                   gc[k][4 * h + 2] = __uint_as_float(r4.z);
                   gc[k][4 * h + 3] = __uint_as_float(r4.w);
                 }
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                  const T* src = xt + (size_t)(unsigned)((gidx[it] + d[c]) * P.CS + cofs);
-                  const bool on = (gval[it] & (1u << c)) != 0u;
-                  if constexpr (LD == 2) {
-                    raw[k][c][0] = on ? ldg_nc_v4(src) : make_uint4(0u, 0u, 0u, 0u);
-                    raw[k][c][LD - 1] = on ? ldg_nc_v4(src + 32) : make_uint4(0u, 0u, 0u, 0u);
-                  } else {
-                    const uint2 lo = on ? ldg_nc_v2(src) : make_uint2(0u, 0u);
-                    const uint2 hi = on ? ldg_nc_v2(src + 32) : make_uint2(0u, 0u);
-                    raw[k][c][0] = make_uint4(lo.x, lo.y, hi.x, hi.y);
-                  }
-                }
+                for (int c = 0; c < 4; ++c)
+#pragma unroll
+                  for (int l = 0; l < LD; ++l)
+                    raw[k][c][l] = (gval[it] & (1u << c))
+                                       ? ldg_nc_v4(xt + (size_t)(unsigned)((gidx[it] + d[c]) * P.CS + cofs) + l * (8 / LD))
+                                       : make_uint4(0u, 0u, 0u, 0u);
               }
 #pragma unroll
               for (int k = 0; k < BATCH; ++k) {
@@ -330,7 +326,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int c = 0; c < 4; ++c) {
                   if ((gval[it] & (1u << c)) && !(a.dbg & 2)) {
                     const float sk = bw[c] * m;
-                    float* dst = a.gx_nhwc + (size_t)(unsigned)((gidx[it] + d[c]) * P.CS + cofs);
+                    float* dst = a.gx_nhwc + (size_t)(unsigned)((gidx[it] + d[c]) * P.CS + lofs);
                     red_add_v4(dst, gc[k][0] * sk, gc[k][1] * sk, gc[k][2] * sk, gc[k][3] * sk);
                     red_add_v4(dst + 32, gc[k][4] * sk, gc[k][5] * sk, gc[k][6] * sk, gc[k][7] * sk);
                   }

@@ -256,8 +256,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             float v[8];
             tmem_ld8(tb + c0, v);
             if (co < P.Co) {
-              red_add_v4(dst + c0, v[0], v[1], v[2], v[3]);
-              red_add_v4(dst + c0 + 4, v[4], v[5], v[6], v[7]);
+              // packed columns c0..c0+7 are logical channels blk+4q' .. and blk+32+4q' ..
+              const int lc = (c0 & ~63) + 4 * ((c0 & 63) >> 3);
+              red_add_v4(dst + lc, v[0], v[1], v[2], v[3]);
+              red_add_v4(dst + lc + 32, v[4], v[5], v[6], v[7]);
             }
           }
         }

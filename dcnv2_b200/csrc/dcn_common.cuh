@@ -361,6 +361,18 @@ __device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, 
                : "memory");
 }
 
+// ---------------------------------------------------------------- channel order
+// Inside every 64-channel block the packed input (and every operand derived
+// from it) stores channels in the order that makes the 8 channels a lane owns
+// contiguous: physical position 8q + r holds logical channel 4q + r (r < 4) or
+// 32 + 4q + (r - 4) (r >= 4).  A lane's 16-byte slice q is then logical channels
+// [4q, 4q+4) and [32+4q, 32+4q+4), so the grad_input scatter (in logical order)
+// fills whole 32-byte sectors with two lanes per red.add instruction.
+__host__ __device__ __forceinline__ int perm_logical(int pp) {
+  const int q = pp >> 3, r = pp & 7;
+  return r < 4 ? 4 * q + r : 32 + 4 * q + (r - 4);
+}
+
 // ---------------------------------------------------------------- sampling geometry
 // Bilinear sampling geometry of one (pixel, tap, group): the four corner
 // weights (already multiplied by the modulation mask; zero for corners outside

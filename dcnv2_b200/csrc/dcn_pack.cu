@@ -12,7 +12,8 @@ namespace dcn {
 
 namespace {
 
-// [B][C][H*W] -> [B][H*W][dg][Cgp]; padded channels are written as zero.  One
+// [B][C][H*W] -> [B][H*W][dg][Cgp] (channel order of perm_logical inside each
+// 64-channel block); padded channels are written as zero.  One
 // CTA moves a 64-pixel x 64-channel block: 16-byte loads along pixels (when
 // `vec`: H*W % 8 == 0 and x 16-byte aligned), 16-byte stores along channels.
 template <typename T>
@@ -47,7 +48,7 @@ __global__ void __launch_bounds__(256) pack_input_kernel(const T* __restrict__ x
     if (p >= HW) continue;
     alignas(16) T v[EPV];
 #pragma unroll
-    for (int e = 0; e < EPV; ++e) v[e] = tile[cv * EPV + e][pl];
+    for (int e = 0; e < EPV; ++e) v[e] = tile[perm_logical(cv * EPV + e)][pl];
     *reinterpret_cast<uint4*>(xo + (size_t)p * CS + cv * EPV) = *reinterpret_cast<const uint4*>(v);
   }
 }
@@ -98,7 +99,7 @@ __global__ void pack_weight_fwd_kernel(const T* __restrict__ w, uint8_t* __restr
     float v[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      const int cc = cb * kChunk + chunk * 8 + e;
+      const int cc = cb * kChunk + perm_logical(chunk * 8 + e);
       v[e] = (co < P.Co && cc < P.Cg)
                  ? ldf(w + ((size_t)co * P.C + g * P.Cg + cc) * P.K2 + t)
                  : 0.f;
@@ -125,7 +126,7 @@ __global__ void pack_weight_bwd_kernel(const T* __restrict__ w, uint8_t* __restr
     const int t = u / (P.dg * P.nCC);
     const int rem = u - t * (P.dg * P.nCC);
     const int g = rem / P.nCC, cch = rem - g * P.nCC;
-    const int cc = cch * P.NC + n;
+    const int cc = cch * P.NC + (n & ~63) + perm_logical(n & 63);
     float v[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
