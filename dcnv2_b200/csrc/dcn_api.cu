@@ -27,6 +27,14 @@ int debug_skip() {
   return v;
 }
 
+long long gcol_budget_mb() {
+  static long long v = [] {
+    const char* e = getenv("DCN_GCOL_MB");
+    return e ? atoll(e) : 512LL;
+  }();
+  return v;
+}
+
 int device_sms() {
   static int cached[64];
   static std::once_flag flags[64];
@@ -125,12 +133,20 @@ int make_plan(const dcn_desc* d, Plan* p, int num_sms) {
   p->NC = p->Cgp < 256 ? p->Cgp : 256;
   p->nCC = ceil_div(p->Cgp, p->NC);
   p->nU = p->K2 * d->dg * p->nCC;
+  {
+    const int nTG = p->K2 * d->dg;
+    p->gT = p->nCC == 1 ? 256 / p->NC : 1;
+    if (p->gT > nTG) p->gT = nTG;
+    if (p->gT < 1) p->gT = 1;
+    p->gNC = p->gT * p->NC;
+    p->gnU = ceil_div(nTG, p->gT) * p->nCC;
+  }
   // backward weight
   p->nMT = ceil_div(d->Co, 128);
   plan_weight_grad(p, num_sms);
   // packed tiles
   p->wf_tile_bytes = (size_t)p->nsplit * p->NT * 128;
-  p->wd_tile_bytes = (size_t)p->nsplit * p->NC * 128;
+  p->wd_tile_bytes = (size_t)p->nsplit * p->gNC * 128;
   // workspace layout
   size_t off = 0;
   p->off_status = off; off += kWsAlign;
@@ -139,9 +155,23 @@ int make_plan(const dcn_desc* d, Plan* p, int num_sms) {
   p->off_wf = off; off = align_up(off + (size_t)p->nCoT * p->nK * p->wf_tile_bytes, kWsAlign);
   p->fwd_bytes = off;
   off = common;
-  p->off_wd = off; off = align_up(off + (size_t)p->nU * p->nKo * p->wd_tile_bytes, kWsAlign);
+  p->off_wd = off; off = align_up(off + (size_t)p->gnU * p->nKo * p->wd_tile_bytes, kWsAlign);
   p->nPB = (int)((p->totalP + 63) / 64);
   p->off_go = off; off = align_up(off + (size_t)p->nPB * p->nKo * p->nsplit * 8192, kWsAlign);
+  // backward-data runs in pixel chunks whose column gradients fit a fixed
+  // budget (512 MB; DCN_GCOL_MB overrides), keeping 32-bit indexing and the
+  // workspace bounded for large batches
+  {
+    const long long row_bytes = (long long)p->K2 * p->CS * p->esz;
+    long long chunk = (gcol_budget_mb() << 20) / row_bytes / kTileM * kTileM;
+    if (chunk < kTileM) chunk = kTileM;
+    const long long need = (p->totalP + kTileM - 1) / kTileM * kTileM;
+    if (chunk > need) chunk = need;
+    if (chunk * row_bytes / p->esz >= (1LL << 31)) return DCN_E_UNSUPPORTED;
+    p->gcol_chunk = (int)chunk;
+  }
+  p->off_gcol = off;
+  off = align_up(off + (size_t)p->gcol_chunk * p->K2 * p->CS * p->esz, kWsAlign);
   p->off_gx = off; off = align_up(off + (size_t)d->B * d->H * d->W * p->CS * 4, kWsAlign);
   p->off_gw = off; off = align_up(off + (size_t)d->Co * p->K2 * p->CS * 4, kWsAlign);
   p->off_gb = off; off = align_up(off + (size_t)d->Co * 4, kWsAlign);
@@ -295,6 +325,7 @@ int dcn_backward(const dcn_desc* d, const void* input, const void* weight, const
   a.gpk = ws + P.off_go;
   a.wpk = ws + P.off_wd;
   a.gx_nhwc = gxn;
+  a.gcol = ws + P.off_gcol;
   a.goffset = grad_offset;
   a.gmask = grad_mask;
   a.err = reinterpret_cast<int*>(ws + P.off_status);
@@ -307,9 +338,17 @@ int dcn_backward(const dcn_desc* d, const void* input, const void* weight, const
     if (dts_d) cudaMemsetAsync(dts_d, 0, 1024 * sizeof(unsigned long long), s);
     a.ts = dts_d;
   }
-  {
-    TraceScope ts(TR_BACKWARD_DATA, s);
-    if ((rc = launch_backward_data(a, s)) != DCN_OK) return rc;
+  for (long long p0 = 0; p0 < P.totalP; p0 += P.gcol_chunk) {
+    a.pix0 = (int)p0;
+    a.npix = (int)(P.totalP - p0 < P.gcol_chunk ? P.totalP - p0 : P.gcol_chunk);
+    {
+      TraceScope ts(TR_BACKWARD_DATA, s);
+      if ((rc = launch_backward_data(a, s)) != DCN_OK) return rc;
+    }
+    {
+      TraceScope ts(TR_BACKWARD_SCATTER, s);
+      if ((rc = launch_backward_scatter(a, s)) != DCN_OK) return rc;
+    }
   }
   if (a.ts) {
     unsigned long long h[1024];

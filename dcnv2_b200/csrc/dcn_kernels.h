@@ -6,7 +6,7 @@
 
 namespace dcn {
 
-constexpr int kMaxStages = 6;
+constexpr int kMaxStages = 12;
 constexpr int kMaxASlots = 16;
 constexpr size_t kFwdSmemBudget = 200 * 1024;  // dynamic smem for the forward ring
 constexpr size_t kBwdSmemBudget = 200 * 1024;
@@ -37,6 +37,8 @@ struct BwdDataArgs {
   const void* gout;     // grad_output [B][Co][Ho][Wo]
   const uint8_t* gpk;   // packed grad_output blocks [nPB][nKo][64 x 128 B x nsplit]
   const uint8_t* wpk;   // packed W^T tiles [nU][nKo][NC x 128 B x nsplit]
+  void* gcol;           // [npix][K2][dg][Cgp] column gradients of the chunk (T, f32 for f32)
+  int pix0, npix;       // pixel chunk handled by this launch (pix0 % 128 == 0)
   float* gx_nhwc;       // fp32 [B][H][W][dg][Cgp], zero-initialised, accumulated by red.add
   void* goffset;        // [B][dg*2*K2][Ho][Wo]
   void* gmask;          // [B][dg*K2][Ho][Wo]
@@ -44,7 +46,6 @@ struct BwdDataArgs {
   int stages;
   int num_sms;
   int dbg;              // experiment switches (DCN_DEBUG_SKIP); 0 in normal use
-  int tb_ch;            // channels per transpose pass (set by the launcher)
   int a_slots;          // grad_out chunk slots in smem (set by the launcher)
   int vec_gout;         // grad_output 16-byte aligned (vector loads allowed when HoWo % 8 == 0)
 };
@@ -78,6 +79,7 @@ int launch_finish_grad_weight(const Plan& p, const float* gw, const float* gb, v
 // Main kernels
 int launch_forward(const FwdArgs& a, cudaStream_t s);
 int launch_backward_data(const BwdDataArgs& a, cudaStream_t s);
+int launch_backward_scatter(const BwdDataArgs& a, cudaStream_t s);
 int launch_backward_weight(const BwdWeightArgs& a, cudaStream_t s);
 
 }  // namespace dcn

@@ -109,34 +109,38 @@ __global__ void pack_weight_fwd_kernel(const T* __restrict__ w, uint8_t* __restr
   }
 }
 
-// Backward-data B operand (W transposed): tile (u, ko) holds rows n = channel
-// cc = chunk*NC + n of group g at tap t, K elements co = ko*64 + e.
+// Backward-data B operand (W transposed): tile (u, ko) of unit u = (set, cch)
+// holds rows n = j*NC + nn for the gT (tap, group)s tg = set*gT + j of the set,
+// channel cc = cch*NC + nn (packed order inside 64-channel blocks), and K
+// elements co = ko*64 + e; rows of (tap, group)s past the end are zero.
 template <typename T>
 __global__ void pack_weight_bwd_kernel(const T* __restrict__ w, uint8_t* __restrict__ wpk,
                                        const Plan P) {
-  const long long nchunks = (long long)P.nU * P.nKo * P.NC * 8;
+  const long long nchunks = (long long)P.gnU * P.nKo * P.gNC * 8;
+  const int nTG = P.K2 * P.dg;
   for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < nchunks;
        idx += (long long)gridDim.x * blockDim.x) {
     const int chunk = (int)(idx & 7);
     const long long rt = idx >> 3;
-    const int n = (int)(rt % P.NC);
-    const long long uk = rt / P.NC;
+    const int n = (int)(rt % P.gNC);
+    const long long uk = rt / P.gNC;
     const int ko = (int)(uk % P.nKo);
     const int u = (int)(uk / P.nKo);
-    const int t = u / (P.dg * P.nCC);
-    const int rem = u - t * (P.dg * P.nCC);
-    const int g = rem / P.nCC, cch = rem - g * P.nCC;
-    const int cc = cch * P.NC + (n & ~63) + perm_logical(n & 63);
+    const int set = u / P.nCC, cch = u - set * P.nCC;
+    const int j = n / P.NC, nn = n - j * P.NC;
+    const int tg = set * P.gT + j;
+    const int t = tg / P.dg, g = tg - t * P.dg;
+    const int cc = cch * P.NC + (nn & ~63) + perm_logical(nn & 63);
     float v[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       const int co = ko * kChunk + chunk * 8 + e;
-      v[e] = (co < P.Co && cc < P.Cg)
+      v[e] = (tg < nTG && co < P.Co && cc < P.Cg)
                  ? ldf(w + ((size_t)co * P.C + g * P.Cg + cc) * P.K2 + t)
                  : 0.f;
     }
     uint8_t* tile = wpk + (size_t)(u * P.nKo + ko) * P.wd_tile_bytes;
-    write_chunk<T>(tile, (size_t)P.NC * 128, n, chunk, v);
+    write_chunk<T>(tile, (size_t)P.gNC * 128, n, chunk, v);
   }
 }
 
@@ -318,7 +322,7 @@ int launch_pack_weight_fwd(const Plan& P, const void* w, uint8_t* wpk, cudaStrea
 }
 
 int launch_pack_weight_bwd(const Plan& P, const void* w, uint8_t* wpk, cudaStream_t s) {
-  const long long n = (long long)P.nU * P.nKo * P.NC * 8;
+  const long long n = (long long)P.gnU * P.nKo * P.gNC * 8;
   return dispatch(P.dtype, [&](auto tag) {
     using T = decltype(tag);
     pack_weight_bwd_kernel<T><<<grid_for(n, 256), 256, 0, s>>>(static_cast<const T*>(w), wpk, P);

@@ -31,7 +31,9 @@ struct Plan {
   // backward-data GEMM: M = pixels, N = channel chunk of a group, K = Co
   int Cop, nKo;       // Co padded to 64, 64-channel Co chunks
   int NC, nCC;        // channel chunk (<=256), chunks per group
-  int nU;             // units (t, g, channel chunk) = K2*dg*nCC
+  int nU;             // units (t, g, channel chunk) = K2*dg*nCC (backward-weight)
+  int gT, gNC, gnU;   // backward-data GEMM units: gT (tap, group)s x NC channels = gNC
+                      // columns (<= 256), gnU = ceil(K2*dg / gT) * nCC units
   // backward-weight GEMM: M = Co (128 rows per M tile), N = channel sets, K = pixels
   int nMT;            // 128-row Co tiles
   int wg_mt_per_cta;  // M tiles handled by one CTA
@@ -40,11 +42,12 @@ struct Plan {
   int wg_nsplit_px;   // CTAs along the pixel reduction
   int wg_ksteps;      // 64-pixel K steps in total (ceil(totalP/64))
   // workspace layout (bytes)
-  size_t off_status, off_x, off_wf, off_wd, off_go, off_gx, off_gw, off_gb;
+  size_t off_status, off_x, off_wf, off_wd, off_go, off_gcol, off_gx, off_gw, off_gb;
   int nPB;               // 64-pixel blocks of the packed grad_output
+  int gcol_chunk;        // pixels per backward-data chunk (multiple of 128)
   size_t fwd_bytes, bwd_bytes;
   size_t wf_tile_bytes;   // one forward weight tile (NT rows x 128 B x nsplit)
-  size_t wd_tile_bytes;   // one backward-data weight tile (NC rows x 128 B x nsplit)
+  size_t wd_tile_bytes;   // one backward-data weight tile (gNC rows x 128 B x nsplit)
 };
 
 // Fills `p` from `d`; returns DCN_OK or DCN_E_INVALID / DCN_E_UNSUPPORTED.

@@ -13,7 +13,7 @@ const char* kNames[TR_COUNT] = {
     "pack_input",          "pack_weight_fwd",     "forward",
     "pack_weight_bwd",     "zero_accumulators",   "backward_data",
     "backward_weight",     "finish_grad_input",   "finish_grad_weight",
-    "pack_grad_output",
+    "pack_grad_output",    "backward_scatter",
 };
 
 struct Rec {

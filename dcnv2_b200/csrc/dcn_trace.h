@@ -17,6 +17,7 @@ enum TraceId {
   TR_FINISH_GRAD_INPUT,
   TR_FINISH_GRAD_WEIGHT,
   TR_PACK_GRAD_OUTPUT,
+  TR_BACKWARD_SCATTER,
   TR_COUNT
 };
 
