@@ -8,9 +8,11 @@
 //   grad_input[b, c, corner]    += gcol * mask * corner weight   (fp32 red.add)
 //
 // A plain SIMT kernel run at high occupancy so the load and reduction latencies
-// are hidden by many warps.  A warp handles 4 pixels of one (tap, group); the
-// 8 lanes of a pixel own one 16-byte slice (8 channels, packed order) of the
-// pixel's gcol row and of each bilinear corner line.  bilinear and its two
+// are hidden by many warps.  A warp handles 32 pixels of one (tap, group): each
+// lane computes the sampling geometry of one pixel, then 8 sub-iterations take
+// 4 pixels at a time, the 8 lanes of a pixel owning one 16-byte slice (8
+// channels, packed order) of the pixel's gcol row and of each bilinear corner
+// line; the per-pixel sums return to the owner lane for coalesced stores.  bilinear and its two
 // derivatives are linear in the four corners, so each lane only forms
 // S_c = sum_e gcol_e * corner_c[e]; the three channel sums follow from S and
 // are reduced over the 8 lanes with shuffles.  The scatter writes grad_input in
@@ -26,6 +28,16 @@ namespace {
 
 constexpr int kThreads = 256;
 
+// 2 x f32 packed multiply (sm_100): {a.x * s, a.y * s}
+__device__ __forceinline__ float2 mul2(float2 a, float s) {
+  unsigned long long r;
+  asm("{\n\t.reg .b64 x, y;\n\tmov.b64 x, {%1, %2};\n\tmov.b64 y, {%3, %3};\n\t"
+      "mul.rn.f32x2 %0, x, y;\n\t}"
+      : "=l"(r)
+      : "f"(a.x), "f"(a.y), "f"(s));
+  return make_float2(__uint_as_float((uint32_t)r), __uint_as_float((uint32_t)(r >> 32)));
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads) dcn_bwd_scatter_kernel(const __grid_constant__ BwdDataArgs a) {
   using G = typename std::conditional<std::is_same<T, float>::value, float, T>::type;
@@ -36,9 +48,9 @@ __global__ void __launch_bounds__(kThreads) dcn_bwd_scatter_kernel(const __grid_
   const int HoWo = P.HoWo, HW = P.H * P.W;
   const int nTG = P.K2 * P.dg;
   const int rowlen = nTG * P.Cgp;
-  const int npg = (a.npix + 3) / 4;
   const int pend = a.pix0 + a.npix;
-  const int nitems = npg * nTG;                 // < 2^31 (the plan bounds B*Ho*Wo*K2*dg)
+  const int ngrp = (a.npix + 31) / 32;          // 32-pixel groups of the chunk
+  const int nitems = ngrp * nTG;                // warp items: (32-pixel group, tap-group)
   const T* __restrict__ xt = reinterpret_cast<const T*>(a.xt);
   const T* __restrict__ off = reinterpret_cast<const T*>(a.offset);
   const T* __restrict__ msk = reinterpret_cast<const T*>(a.mask);
@@ -49,99 +61,124 @@ __global__ void __launch_bounds__(kThreads) dcn_bwd_scatter_kernel(const __grid_
   const int nwarps = (int)((gridDim.x * kThreads) >> 5);
 
   for (int item = warp0; item < nitems; item += nwarps) {
-    const int pg = item / nTG;
-    const int tg = item - pg * nTG;
+    const int grp = item / nTG;
+    const int tg = item - grp * nTG;
     const int t = tg / P.dg, g = tg - t * P.dg;
-    const int pix = a.pix0 + pg * 4 + lp;
-    const bool pv = pix < pend;
-    const int b = pv ? pix / HoWo : 0;
-    const int p = pv ? pix - b * HoWo : 0;
-    // sampling geometry (reference validity rule -1 < h < H, -1 < w < W)
-    float lh = 0.f, lw = 0.f, m = 0.f;
-    int gidx = 0;
-    uint32_t cval = 0u;
-    const int obase = ((b * P.dg + g) * 2 * P.K2 + 2 * t) * HoWo + p;
-    const int mbase = ((b * P.dg + g) * P.K2 + t) * HoWo + p;
-    if (pv) {
+    // ---- geometry of pixel (group base + lane), computed once per lane
+    const int mpix = a.pix0 + grp * 32 + lane;
+    const bool mpv = mpix < pend;
+    const int mb = mpv ? mpix / HoWo : 0;
+    const int mp = mpv ? mpix - mb * HoWo : 0;
+    const int obase = ((mb * P.dg + g) * 2 * P.K2 + 2 * t) * HoWo + mp;
+    const int mbase = ((mb * P.dg + g) * P.K2 + t) * HoWo + mp;
+    float mlh = 0.f, mlw = 0.f, mm = 0.f;
+    int mgidx = 0;
+    uint32_t mval = 0u;
+    if (mpv) {
       const int i = t / P.kw, j = t - i * P.kw;
-      const int ho = p / P.Wo, wo = p - ho * P.Wo;
+      const int ho = mp / P.Wo, wo = mp - ho * P.Wo;
       const float h = (float)(ho * P.sh - P.ph + i * P.dh) + ldf(off + obase);
       const float w = (float)(wo * P.sw - P.pw + j * P.dw) + ldf(off + obase + HoWo);
-      m = ldf(msk + mbase);
+      mm = ldf(msk + mbase);
       const float hf = floorf(h), wf = floorf(w);
       const int hl = (int)hf, wl = (int)wf;
-      lh = h - hf;
-      lw = w - wf;
+      mlh = h - hf;
+      mlw = w - wf;
       if ((h > -1.f) && (w > -1.f) && (h < (float)P.H) && (w < (float)P.W) && !(a.dbg & 1)) {
         const bool r0 = hl >= 0, r1 = hl + 1 <= P.H - 1, c0 = wl >= 0, c1 = wl + 1 <= P.W - 1;
-        cval = (r0 && c0 ? 1u : 0u) | (r0 && c1 ? 2u : 0u) | (r1 && c0 ? 4u : 0u) |
+        mval = (r0 && c0 ? 1u : 0u) | (r0 && c1 ? 2u : 0u) | (r1 && c0 ? 4u : 0u) |
                (r1 && c1 ? 8u : 0u);
-        gidx = b * HW + hl * P.W + wl;
+        mgidx = mb * HW + hl * P.W + wl;
       }
     }
-    const float hh = 1.f - lh, hw = 1.f - lw;
-    const float bw[4] = {(cval & 1u) ? hh * hw : 0.f, (cval & 2u) ? hh * lw : 0.f,
-                         (cval & 4u) ? lh * hw : 0.f, (cval & 8u) ? lh * lw : 0.f};
     const int d[4] = {0, 1, P.W, P.W + 1};
-    float S[4] = {0.f, 0.f, 0.f, 0.f};
-    if (cval != 0u) {
-      const G* grow = gcol + (size_t)(unsigned)(pix - a.pix0) * rowlen + tg * P.Cgp + q * 8;
-      for (int cb = 0; cb < P.nCB; ++cb) {
-        const int cofs = g * P.Cgp + cb * kChunk;
-        // gcol slice and the four corner slices, all loads issued first
-        uint4 graw[sizeof(G) / 2];
+    float om = 0.f, oh = 0.f, ow = 0.f;   // results of this lane's own pixel
+    // ---- 8 sub-iterations of 4 pixels, 8 lanes per pixel
+#pragma unroll 1
+    for (int sub = 0; sub < 8; ++sub) {
+      const int src = sub * 4 + lp;
+      const int gidx = __shfl_sync(0xffffffffu, mgidx, src);
+      const float lh = __shfl_sync(0xffffffffu, mlh, src);
+      const float lw = __shfl_sync(0xffffffffu, mlw, src);
+      const float m = __shfl_sync(0xffffffffu, mm, src);
+      const uint32_t cval = __shfl_sync(0xffffffffu, mval, src);
+      const int pix = a.pix0 + grp * 32 + src;
+      const float hh = 1.f - lh, hw = 1.f - lw;
+      const float bw[4] = {(cval & 1u) ? hh * hw : 0.f, (cval & 2u) ? hh * lw : 0.f,
+                           (cval & 4u) ? lh * hw : 0.f, (cval & 8u) ? lh * lw : 0.f};
+      float S[4] = {0.f, 0.f, 0.f, 0.f};
+      if (cval != 0u) {
+        const G* grow = gcol + (size_t)(unsigned)(pix - a.pix0) * rowlen + tg * P.Cgp + q * 8;
+        for (int cb = 0; cb < P.nCB; ++cb) {
+          const int cofs = g * P.Cgp + cb * kChunk;
+          uint4 graw[sizeof(G) / 2];
 #pragma unroll
-        for (int l = 0; l < (int)(sizeof(G) / 2); ++l) graw[l] = ldg_nc_v4(grow + cb * kChunk + l * 4);
-        uint4 raw[4][LD];
+          for (int l = 0; l < (int)(sizeof(G) / 2); ++l) graw[l] = ldg_nc_v4(grow + cb * kChunk + l * 4);
+          uint4 raw[4][LD];
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+          for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int l = 0; l < LD; ++l)
-            raw[c][l] = (cval & (1u << c))
-                            ? ldg_nc_v4(xt + (size_t)(unsigned)((gidx + d[c]) * P.CS + cofs + q * 8) + l * (8 / LD))
-                            : make_uint4(0u, 0u, 0u, 0u);
-        float gc[8];
-        if constexpr (sizeof(G) == 4) {
-          gc[0] = __uint_as_float(graw[0].x); gc[1] = __uint_as_float(graw[0].y);
-          gc[2] = __uint_as_float(graw[0].z); gc[3] = __uint_as_float(graw[0].w);
-          gc[4] = __uint_as_float(graw[LD - 1].x); gc[5] = __uint_as_float(graw[LD - 1].y);
-          gc[6] = __uint_as_float(graw[LD - 1].z); gc[7] = __uint_as_float(graw[LD - 1].w);
-        } else {
-          unpack8<G>(graw[0], gc);
-        }
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float v[8];
-          unpack_slice<T>(raw[c], v);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) S[c] = fmaf(gc[e], v[e], S[c]);
-        }
-        if (!(a.dbg & 2)) {
+            for (int l = 0; l < LD; ++l)
+              raw[c][l] = (cval & (1u << c))
+                              ? ldg_nc_v4(xt + (size_t)(unsigned)((gidx + d[c]) * P.CS + cofs + q * 8) + l * (8 / LD))
+                              : make_uint4(0u, 0u, 0u, 0u);
+          float gc[8];
+          if constexpr (sizeof(G) == 4) {
+            gc[0] = __uint_as_float(graw[0].x); gc[1] = __uint_as_float(graw[0].y);
+            gc[2] = __uint_as_float(graw[0].z); gc[3] = __uint_as_float(graw[0].w);
+            gc[4] = __uint_as_float(graw[LD - 1].x); gc[5] = __uint_as_float(graw[LD - 1].y);
+            gc[6] = __uint_as_float(graw[LD - 1].z); gc[7] = __uint_as_float(graw[LD - 1].w);
+          } else {
+            unpack8<G>(graw[0], gc);
+          }
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
-            if (cval & (1u << c)) {
-              const float sk = bw[c] * m;
-              float* dst = a.gx_nhwc + (size_t)(unsigned)((gidx + d[c]) * P.CS + cofs + 4 * q);
-              red_add_v4(dst, gc[0] * sk, gc[1] * sk, gc[2] * sk, gc[3] * sk);
-              red_add_v4(dst + 32, gc[4] * sk, gc[5] * sk, gc[6] * sk, gc[7] * sk);
+            float v[8];
+            unpack_slice<T>(raw[c], v);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) S[c] = fmaf(gc[e], v[e], S[c]);
+          }
+          if (!(a.dbg & 2)) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              if (cval & (1u << c)) {
+                const float sk = bw[c] * m;
+                float* dst = a.gx_nhwc + (size_t)(unsigned)((gidx + d[c]) * P.CS + cofs + 4 * q);
+                const float2 s0 = mul2(make_float2(gc[0], gc[1]), sk);
+                const float2 s1 = mul2(make_float2(gc[2], gc[3]), sk);
+                const float2 s2 = mul2(make_float2(gc[4], gc[5]), sk);
+                const float2 s3 = mul2(make_float2(gc[6], gc[7]), sk);
+                red_add_v4(dst, s0.x, s0.y, s1.x, s1.y);
+                red_add_v4(dst + 32, s2.x, s2.y, s3.x, s3.y);
+              }
             }
           }
         }
       }
-    }
-    float am = bw[0] * S[0] + bw[1] * S[1] + bw[2] * S[2] + bw[3] * S[3];
-    float ah = hw * (S[2] - S[0]) + lw * (S[3] - S[1]);
-    float aw = hh * (S[1] - S[0]) + lh * (S[3] - S[2]);
+      float am = bw[0] * S[0] + bw[1] * S[1] + bw[2] * S[2] + bw[3] * S[3];
+      float ah = hw * (S[2] - S[0]) + lw * (S[3] - S[1]);
+      float aw = hh * (S[1] - S[0]) + lh * (S[3] - S[2]);
 #pragma unroll
-    for (int sh = 1; sh < 8; sh <<= 1) {
-      am += __shfl_xor_sync(0xffffffffu, am, sh);
-      ah += __shfl_xor_sync(0xffffffffu, ah, sh);
-      aw += __shfl_xor_sync(0xffffffffu, aw, sh);
+      for (int sh = 1; sh < 8; sh <<= 1) {
+        am += __shfl_xor_sync(0xffffffffu, am, sh);
+        ah += __shfl_xor_sync(0xffffffffu, ah, sh);
+        aw += __shfl_xor_sync(0xffffffffu, aw, sh);
+      }
+      // hand the sums of pixel src to its owner lane (held by lane 8 * (owner - 4*sub))
+      const int from = 8 * ((lane - sub * 4) & 3);
+      const float tm = __shfl_sync(0xffffffffu, am, from);
+      const float th = __shfl_sync(0xffffffffu, ah, from);
+      const float tw = __shfl_sync(0xffffffffu, aw, from);
+      if ((lane >> 2) == sub) {
+        om = tm;
+        oh = th;
+        ow = tw;
+      }
     }
-    if (q == 0 && pv) {
-      goff[obase] = Elem<T>::from_f(ah * m);
-      goff[obase + HoWo] = Elem<T>::from_f(aw * m);
-      gmsk[mbase] = Elem<T>::from_f(am);
+    if (mpv) {
+      goff[obase] = Elem<T>::from_f(oh * mm);
+      goff[obase + HoWo] = Elem<T>::from_f(ow * mm);
+      gmsk[mbase] = Elem<T>::from_f(om);
     }
   }
 }
@@ -150,7 +187,7 @@ __global__ void __launch_bounds__(kThreads) dcn_bwd_scatter_kernel(const __grid_
 
 int launch_backward_scatter(const BwdDataArgs& a, cudaStream_t stream) {
   const Plan& P = a.plan;
-  const long long nitems = (long long)(a.npix + 3) / 4 * (P.K2 * P.dg);
+  const long long nitems = (long long)(a.npix + 31) / 32 * (P.K2 * P.dg);
   long long blocks = (nitems + 7) / 8;
   const long long cap = (long long)a.num_sms * 16;
   if (blocks > cap) blocks = cap;
