@@ -237,6 +237,7 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", device_id=dev)
     from dcnv2_b200 import _C, _lib
+    from dcnv2_b200.dp import allreduce_tensors
 
     dtype = DTYPES[args.dtype]
     B, C, H, W, Co, k, s, p, d, dg, _ = wl
@@ -248,10 +249,8 @@ def main():
     def step(x, off, m, gy):
         y = _C.dcn_v2_forward(x, w, m, off, b, s, s, p, p, d, d, dg)
         gi, goff, gm, gw, gb = _C.dcn_v2_backward(x, w, m, off, b, gy, s, s, p, p, d, d, dg)
-        if world > 1:
-            flat = torch.cat([gw.reshape(-1).float(), gb.float()])
-            dist.all_reduce(flat)
-            gw, gb = flat[:gw.numel()].view_as(gw), flat[gw.numel():]
+        if world > 1:  # the data-parallel exchange: one bucketed all-reduce
+            gw, gb = allreduce_tensors([gw, gb])
         return y, gw, gb
 
     def timed(fn, n):
