@@ -59,6 +59,8 @@ def _failing_worker(rank, world, port, q):
     _init(rank, world, port, timeout_s=5)
     if rank == 1:
         q.put((rank, "left before the collective"))
+        q.close()
+        q.join_thread()
         os._exit(0)  # the rank dies between steps, none of its work in flight
     t = torch.ones(4)
     try:
