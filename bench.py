@@ -26,7 +26,10 @@ import sys
 import time
 
 import numpy as np
-import torch
+
+# NCCL prints its version on stdout by default; the bench's stdout is one JSON line
+os.environ.setdefault("NCCL_DEBUG", "WARN")
+import torch  # noqa: E402
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
@@ -321,14 +324,30 @@ def main():
     value = world * step_flops / (ms_step * 1e-3) / 1e12
     e2e_value = world * step_flops / (ms_e2e * 1e-3) / 1e12
 
-    # roofline of the dominant kernel (algorithmic tensor work of one GEMM pass)
+    # roofline of the dominant kernel: tensor kernels against the measured bf16
+    # dense peak with the algorithmic FLOPs of one GEMM pass; the SIMT scatter
+    # against the measured HBM copy bandwidth with its algorithmic bytes
     peaks, peak_kind = load_peaks()
     kernels = {kname: (n, tot) for kname, (n, tot) in trace.items()}
     dom = max(kernels, key=lambda kk: kernels[kk][1])
     n_dom, tot_dom = kernels[dom]
     per_launch_ms = tot_dom / n_dom
     gflop = gemm_flops(B, C, Ho, Wo, Co, k)
-    achieved = gflop / (per_launch_ms * 1e-3) / 1e12
+    esz = torch.tensor([], dtype=dtype).element_size()
+    K2 = k * k
+    if dom in ("forward", "backward_data", "backward_weight"):
+        work, bound, unit, peak = gflop, "tensor", "TFLOP/s", peaks["bf16_tflops"]
+        basis = f"2*Co*C*k*k*B*Ho*Wo = {gflop:.4g} FLOP per launch"
+        achieved = work / (per_launch_ms * 1e-3) / 1e12
+    else:
+        # scatter: read gcol (P*K2*C), x (B*C*H*W), offset+mask (3*K2*P); read+write the
+        # fp32 grad_input accumulator (2 * 4*B*C*H*W); write grad_offset+grad_mask (3*K2*P)
+        P = B * Ho * Wo
+        nbytes = (P * K2 * C * esz + B * C * H * W * esz + 6 * K2 * P * esz + 8 * B * C * H * W)
+        nbytes /= n_dom / args.steps  # per launch (the scatter may run in chunks)
+        work, bound, unit, peak = nbytes, "hbm", "GB/s", peaks["hbm_gbs"]
+        basis = f"algorithmic bytes {nbytes:.4g} per launch (gcol, x, offset/mask, fp32 grad_input acc, outputs)"
+        achieved = work / (per_launch_ms * 1e-3) / 1e9
     traffic = load_traffic(dom, args.workload, args.dtype)
     # kernels of this library in the timed region (the accumulator memset is a runtime call)
     launches = sum(n for kk, (n, _) in kernels.items() if kk != "zero_accumulators")
@@ -342,10 +361,10 @@ def main():
         "fwd_ms": ms_fwd, "fwd_readme_tflops": readme_flops(B, C, Ho, Wo, Co, k) / (ms_fwd * 1e-3) / 1e12,
         "fwd_bwd_gemm_tflops": 3 * gflop / (ms_step * 1e-3) / 1e12,
         "kernels_ms_per_step": {kk: v[1] / args.steps for kk, v in kernels.items()},
-        "roofline": {"kernel": dom, "bound": "tensor", "achieved": achieved,
-                     "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
-                     "peak_source": f"{peak_kind} (bf16 dense, burst)", "traffic": traffic,
-                     "algorithmic": f"2*Co*C*k*k*B*Ho*Wo = {gflop:.4g} FLOP per launch"},
+        "roofline": {"kernel": dom, "bound": bound, "achieved": achieved, "peak": peak,
+                     "unit": unit, "frac": achieved / peak,
+                     "peak_source": f"{peak_kind} ({'bf16 dense, burst' if bound == 'tensor' else 'HBM copy'})",
+                     "traffic": traffic, "algorithmic": basis},
         "clocks": clk,
         "e2e": {"value": e2e_value, "unit": "TFLOP/s (README formula, fwd+bwd)",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e},
