@@ -27,12 +27,14 @@ namespace {
 #define DCN_TS(slot) \
   do { if (a.ts && blockIdx.x == 0 && lane == 0 && (slot) < 1024) a.ts[(slot)] = globaltimer(); } while (0)
 
-constexpr int kFwdThreads = 512;  // 4 warpgroups; warps 14-15 idle
+constexpr int kFwdThreads = 640;  // 5 warpgroups; warps 18-19 idle
 constexpr int kMaxCo = 2048;  // bias staged in smem: Co up to 2048
+constexpr int kGeoTaps = 9;   // (tap, group)s per geometry window
 constexpr int kProdThreads = 256;
 constexpr int kEpiWarp0 = 8;
-constexpr int kTmaWarp = 12;
-constexpr int kMmaWarp = 13;
+constexpr int kEpiWarps = 8;
+constexpr int kTmaWarp = 16;
+constexpr int kMmaWarp = 17;
 
 template <typename T>
 __global__ void __launch_bounds__(kFwdThreads, 1)
@@ -46,10 +48,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const int S = a.stages;
 
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t bars[2 * kMaxStages + 5];
+  __shared__ __align__(8) uint64_t bars[2 * kMaxStages + 7];
   __shared__ uint32_t tmem_slot;
-  __shared__ float sbias[kMaxCo];
-  __shared__ __align__(16) uint8_t epi_stage[4][16 * 32 * sizeof(T)];
+  __shared__ __align__(16) uint8_t epi_stage[kEpiWarps][16 * 32 * 2];
   __shared__ volatile int abort_flag;
 
   const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
@@ -58,6 +59,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const uint32_t accf0 = smem_u32(&bars[2 * kMaxStages]);
   const uint32_t acce0 = smem_u32(&bars[2 * kMaxStages + 2]);
   const uint32_t drain = smem_u32(&bars[2 * kMaxStages + 4]);
+  const uint32_t geof = smem_u32(&bars[2 * kMaxStages + 5]);  // geometry window written
+  const uint32_t geoe = smem_u32(&bars[2 * kMaxStages + 6]);  // geometry window consumed
+  // geometry window after the stage ring: [kGeoTaps][128] corner weights and indices
+  float4* sgeo_w = reinterpret_cast<float4*>(smem_raw + ((sbase - smem_u32(smem_raw)) + S * stageBytes));
+  int* sgeo_idx = reinterpret_cast<int*>(sgeo_w + kGeoTaps * kTileM);
+  float* sbias = reinterpret_cast<float*>(sgeo_idx + kGeoTaps * kTileM);  // [Co]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
@@ -67,14 +74,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(accf0 + 8 * i, 1);
-      mbar_init(acce0 + 8 * i, 4);
+      mbar_init(acce0 + 8 * i, kEpiWarps);
     }
     mbar_init(drain, 1);
+    mbar_init(geof, kProdThreads / 32);
+    mbar_init(geoe, kProdThreads / 32);
     abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   // bias staged once per CTA (the epilogue reads it for every output element)
-  for (int c = tid; c < kMaxCo; c += kFwdThreads)
+  for (int c = tid; c < P.nCoT * NT; c += kFwdThreads)
     sbias[c] = (a.bias != nullptr && c < P.Co) ? ldf(reinterpret_cast<const T*>(a.bias) + c) : 0.f;
   uint32_t tmem_cols = 32;
   while (tmem_cols < (uint32_t)(2 * NT)) tmem_cols <<= 1;
@@ -88,20 +97,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const int HoWo = P.HoWo;
   if (warp == 0) DCN_TS(1000);
 
-  // register split per warpgroup: one setmaxnreg per warpgroup, same PC
-  if ((warp >> 2) < 2) {
-    regs_inc<184>();
-  } else if ((warp >> 2) == 2) {
-    regs_dec<88>();
-  } else {
-    regs_dec<56>();
-  }
-
+  // Roles by warpgroup; setmaxnreg at the top of each branch (one instruction
+  // per warpgroup).  Launch: 640 threads x 96 registers; after the split
+  // producers 2 x 4 warps x 160, epilogue 2 x 4 warps x 64, control 4 warps x 32
+  // (= 61440, the launch pool).
   if (warp < kProdThreads / 32) {
+    regs_inc<160>();
     // ------------------------------------------------ gather producers
-    // Warp w builds rows w*16 .. w*16+15 of every A tile.  Lane r < 16 owns the
-    // sampling geometry of row w*16 + r (offsets prefetched one tap ahead) and
-    // broadcasts it; the gather runs 4 rows at a time with 8 lanes per row.
+    // Warp w builds rows w*16 .. w*16+15 of every A tile, 4 rows at a time with
+    // 8 lanes per row.
     using GS = GatherShape<T>;
     constexpr int LPP = GS::kLPP, CPL = GS::kCPL, PPI = GS::kPPI;
     constexpr int ITER = 16 / PPI;
@@ -111,47 +115,64 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const T* __restrict__ off = reinterpret_cast<const T*>(a.offset);
     const T* __restrict__ msk = reinterpret_cast<const T*>(a.mask);
     const int HW = P.H * P.W;
-    uint32_t kidx = 0;
+    uint32_t kidx = 0, gcnt = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < nTiles && ok; tile += gridDim.x) {
       const int pt = tile / P.nCoT;
-      // this lane's geometry row (lanes 16..31 mirror lanes 0..15)
-      const int pix = pt * kTileM + warp * 16 + (lane & 15);
-      const bool pv = pix < P.totalP;
-      const int b = pv ? (int)(pix / HoWo) : 0;
-      const int p = pv ? (int)(pix - b * HoWo) : 0;
-      const int ho = p / P.Wo, wo = p - ho * P.Wo;
-      const int obase = b * P.dg * 2 * P.K2 * HoWo + p;   // offset[b][0][p]
-      const int mbase = b * P.dg * P.K2 * HoWo + p;       // mask[b][0][p]
-      uint32_t rh = 0, rw = 0, rm = 0;  // raw prefetched offset / mask bits
-      auto fetch_raw = [&](int tg) {
-        const int t = tg / P.dg, g = tg - t * P.dg;
-        if (pv && (a.dbg & 8)) {
-          rh = rw = rm = 0u;
-        } else if (pv) {
-          rh = ldg_raw<T>(off + (obase + (g * 2 * P.K2 + 2 * t) * HoWo));
-          rw = ldg_raw<T>(off + (obase + (g * 2 * P.K2 + 2 * t + 1) * HoWo));
-          rm = ldg_raw<T>(msk + (mbase + (g * P.K2 + t) * HoWo));
-        }
-      };
+      // Sampling geometry of the tile's 128 rows for a window of up to kGeoTaps
+      // (tap, group)s is computed by all producer threads at once (every offset
+      // load of the window in flight together) into shared memory; the gather
+      // lanes then read it with broadcast loads.  Two bounded mbarrier handoffs
+      // per window: everyone is done with the previous window, everyone wrote
+      // the new one.
       const int nTG = P.K2 * P.dg;
-      fetch_raw(0);
+      const int nwin_t = nTG < kGeoTaps ? nTG : kGeoTaps;
       PixGeo geo[ITER];
       for (int kc = 0; kc < P.nK && ok; ++kc, ++kidx) {
         const int tg = kc / P.nCB;
         const int cb = kc - tg * P.nCB;
-        const int t = tg / P.dg, g = tg - t * P.dg;
-        if (cb == 0) {
-          const int i = t / P.kw, j = t - i * P.kw;
-          PixGeo mine = zero_pixgeo();
-          if (pv && !(a.dbg & 1)) {
-            const float hs = (float)(ho * P.sh - P.ph + i * P.dh) + raw_to_f<T>(rh);
-            const float ws = (float)(wo * P.sw - P.pw + j * P.dw) + raw_to_f<T>(rw);
-            mine = make_pixgeo(b * HW, hs, ws, raw_to_f<T>(rm), P.H, P.W);
+        const int g = tg % P.dg;
+        const int tl = tg % nwin_t;                 // tap slot inside the window
+        if (cb == 0 && tl == 0) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(geoe);
+          if (!mbar_wait(geoe, gcnt & 1u, a.err, &abort_flag)) { ok = false; break; }
+          const int wt = min(nwin_t, nTG - tg);     // taps in this window
+          for (int item = tid; item < wt * kTileM; item += kProdThreads) {
+            const int slot = item / kTileM, row = item - slot * kTileM;
+            const int tgi = tg + slot;
+            const int t = tgi / P.dg, gi = tgi - t * P.dg;
+            const int pix = pt * kTileM + row;
+            PixGeo r = zero_pixgeo();
+            if (pix < P.totalP && !(a.dbg & 1)) {
+              const int b = pix / HoWo, p = pix - b * HoWo;
+              const int ho = p / P.Wo, wo = p - ho * P.Wo;
+              const int i = t / P.kw, j = t - i * P.kw;
+              const int ob = ((b * P.dg + gi) * 2 * P.K2 + 2 * t) * HoWo + p;
+              const float hs = (float)(ho * P.sh - P.ph + i * P.dh) + ldf(off + ob);
+              const float ws = (float)(wo * P.sw - P.pw + j * P.dw) + ldf(off + ob + HoWo);
+              const float m = ldf(msk + ((b * P.dg + gi) * P.K2 + t) * HoWo + p);
+              r = make_pixgeo(b * HW, hs, ws, m, P.H, P.W);
+            }
+            sgeo_idx[item] = r.gidx;
+            sgeo_w[item] = make_float4(r.w[0], r.w[1], r.w[2], r.w[3]);
           }
-          if (tg + 1 < nTG) fetch_raw(tg + 1);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(geof);
+          if (!mbar_wait(geof, gcnt & 1u, a.err, &abort_flag)) { ok = false; break; }
+          ++gcnt;
+        }
+        if (cb == 0) {
 #pragma unroll
-          for (int it = 0; it < ITER; ++it) geo[it] = shfl_pixgeo(mine, it * PPI + lp);
+          for (int it = 0; it < ITER; ++it) {
+            const int e = tl * kTileM + warp * 16 + it * PPI + lp;
+            const float4 w4 = sgeo_w[e];
+            geo[it].gidx = sgeo_idx[e];
+            geo[it].w[0] = w4.x;
+            geo[it].w[1] = w4.y;
+            geo[it].w[2] = w4.z;
+            geo[it].w[3] = w4.w;
+          }
         }
         if (warp == 0) DCN_TS(4 * kidx);
         const int s = kidx % S;
@@ -179,8 +200,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
     }
   } else if (warp < kTmaWarp) {
+    regs_dec<64>();
     // ------------------------------------------------ epilogue
     const int q = warp & 3;
+    const int chalf = (warp - kEpiWarp0) >> 2;   // the two warps of a lane quarter interleave 16-column blocks
     const int row = q * 32 + lane;
     T* __restrict__ y = reinterpret_cast<T*>(a.out);
     int it = 0;
@@ -199,30 +222,36 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       // vector path: the warp's 32 pixels form aligned 16-byte runs, each inside one image
       const int wpix0 = pt * kTileM + q * 32;
       const bool vec = a.vec_out && (HoWo % 8 == 0) && (wpix0 + 32 <= P.totalP);
-      T* stg = reinterpret_cast<T*>(epi_stage[q]);
+      T* stg = reinterpret_cast<T*>(epi_stage[warp - kEpiWarp0]);
       constexpr int EPV = 16 / (int)sizeof(T);       // elements per 16-byte vector
       constexpr int VPR = 32 / EPV;                  // vectors per 32-pixel row
-      for (int c0 = 0; c0 < NT; c0 += 16) {
+      constexpr int JH = sizeof(T) == 4 ? 8 : 16;    // columns staged per pass
+      for (int c0 = 16 * chalf; c0 < NT; c0 += 32) {
         float v[16];
         tmem_ld16(tbase + c0, v);
         if (vec) {
-          // stage [16 co][32 px] then store 16-byte runs of pixels per co row
+          // stage [JH co][32 px] (JH = 16 columns for 16-bit outputs, 8 per pass for
+          // f32 so the stage stays 1 KB a warp) then store 16-byte runs of pixels per co row
 #pragma unroll
-          for (int j = 0; j < 16; ++j) stg[j * 32 + lane] = Elem<T>::from_f(v[j] + sbias[ct * NT + c0 + j]);
-          __syncwarp();
+          for (int h = 0; h < 16 / JH; ++h) {
 #pragma unroll
-          for (int k = 0; k < 16 * VPR / 32; ++k) {
-            const int idx = lane + 32 * k;
-            const int j = idx / VPR, cv = idx - j * VPR;
-            const int co = ct * NT + c0 + j;
-            if (co < P.Co && !(a.dbg & 2)) {
-              const uint4 val = *reinterpret_cast<const uint4*>(stg + j * 32 + cv * EPV);
-              const int rp = wpix0 + cv * EPV;   // a run never crosses an image (HoWo % 8 == 0)
-              const int rb = (int)(rp / HoWo), rpp = (int)(rp - rb * HoWo);
-              *reinterpret_cast<uint4*>(y + ((size_t)rb * P.Co + co) * HoWo + rpp) = val;
+            for (int j = 0; j < JH; ++j)
+              stg[j * 32 + lane] = Elem<T>::from_f(v[h * JH + j] + sbias[ct * NT + c0 + h * JH + j]);
+            __syncwarp();
+#pragma unroll
+            for (int k = 0; k < JH * VPR / 32; ++k) {
+              const int idx = lane + 32 * k;
+              const int j = idx / VPR, cv = idx - j * VPR;
+              const int co = ct * NT + c0 + h * JH + j;
+              if (co < P.Co && !(a.dbg & 2)) {
+                const uint4 val = *reinterpret_cast<const uint4*>(stg + j * 32 + cv * EPV);
+                const int rp = wpix0 + cv * EPV;   // a run never crosses an image (HoWo % 8 == 0)
+                const int rb = (int)(rp / HoWo), rpp = (int)(rp - rb * HoWo);
+                *reinterpret_cast<uint4*>(y + ((size_t)rb * P.Co + co) * HoWo + rpp) = val;
+              }
             }
+            __syncwarp();
           }
-          __syncwarp();
         } else {
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
@@ -236,7 +265,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       if (lane == 0) mbar_arrive(acce0 + 8 * ab);
       if (warp == kEpiWarp0) DCN_TS(801 + 2 * it);
     }
-  } else if (warp == kTmaWarp) {
+  } else {
+    regs_dec<32>();
+    if (warp == kTmaWarp) {
     // ------------------------------------------------ weight tiles (bulk copy)
     if (lane == 0) {
       uint32_t kidx = 0;
@@ -254,7 +285,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
       }
     }
-  } else {
+    } else {
     // ------------------------------------------------ MMA issuer (warp 13; warps 14-15 idle)
     if (warp == kMmaWarp && lane == 0) {
       const uint32_t idesc = make_idesc(OpOf<T>::kBF16, 0, 0, kTileM, NT);
@@ -298,6 +329,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
   }
 
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == kMmaWarp) {
@@ -313,12 +345,14 @@ int launch_forward(const FwdArgs& a, cudaStream_t stream) {
   if (P.Co > kMaxCo) return DCN_E_UNSUPPORTED;
   const int NS = P.nsplit;
   const size_t stageBytes = (size_t)NS * (128 * 128 + (size_t)P.NT * 128);
-  int S = (int)((kFwdSmemBudget - 1024) / stageBytes);
+  const size_t geoBytes = (size_t)kGeoTaps * kTileM * (sizeof(float4) + sizeof(int)) +
+                          (size_t)P.nCoT * P.NT * sizeof(float);   // geometry window + bias
+  int S = (int)((kFwdSmemBudget - 1024 - geoBytes) / stageBytes);
   if (S > kMaxStages) S = kMaxStages;
   if (S < 2) return DCN_E_UNSUPPORTED;
   FwdArgs args = a;
   args.stages = S;
-  const size_t smem = 1024 + (size_t)S * stageBytes;
+  const size_t smem = 1024 + (size_t)S * stageBytes + geoBytes;
   const int nTiles = P.nPT * P.nCoT;
   int grid = nTiles < a.num_sms ? nTiles : a.num_sms;
   if (grid <= 0) return DCN_OK;

@@ -8,7 +8,7 @@ namespace dcn {
 
 constexpr int kMaxStages = 12;
 constexpr int kMaxASlots = 16;
-constexpr size_t kFwdSmemBudget = 200 * 1024;  // dynamic smem for the forward ring
+constexpr size_t kFwdSmemBudget = 218 * 1024;  // dynamic smem of the forward kernel
 constexpr size_t kBwdSmemBudget = 200 * 1024;
 constexpr size_t kBwdSmemLimit = 226 * 1024;  // backward-data ring + transpose buffer
 
