@@ -30,7 +30,7 @@ int debug_skip() {
 long long gcol_budget_mb() {
   static long long v = [] {
     const char* e = getenv("DCN_GCOL_MB");
-    return e ? atoll(e) : 512LL;
+    return e ? atoll(e) : 1024LL;
   }();
   return v;
 }
@@ -158,12 +158,13 @@ int make_plan(const dcn_desc* d, Plan* p, int num_sms) {
   p->off_wd = off; off = align_up(off + (size_t)p->gnU * p->nKo * p->wd_tile_bytes, kWsAlign);
   p->nPB = (int)((p->totalP + 63) / 64);
   p->off_go = off; off = align_up(off + (size_t)p->nPB * p->nKo * p->nsplit * 8192, kWsAlign);
-  // backward-data runs in pixel chunks whose column gradients fit a fixed
-  // budget (512 MB; DCN_GCOL_MB overrides), keeping 32-bit indexing and the
-  // workspace bounded for large batches
+  // the backward runs in pixel chunks whose column gradients and sampled
+  // columns fit a fixed budget (1 GB; DCN_GCOL_MB overrides), keeping 32-bit
+  // indexing and the workspace bounded for large batches
   {
     const long long row_bytes = (long long)p->K2 * p->CS * p->esz;
-    long long chunk = (gcol_budget_mb() << 20) / row_bytes / kTileM * kTileM;
+    const long long cols_row = (long long)p->nsplit * p->nU * p->NC * 2;
+    long long chunk = (gcol_budget_mb() << 20) / (row_bytes + cols_row) / kTileM * kTileM;
     if (chunk < kTileM) chunk = kTileM;
     const long long need = (p->totalP + kTileM - 1) / kTileM * kTileM;
     if (chunk > need) chunk = need;
@@ -172,6 +173,8 @@ int make_plan(const dcn_desc* d, Plan* p, int num_sms) {
   }
   p->off_gcol = off;
   off = align_up(off + (size_t)p->gcol_chunk * p->K2 * p->CS * p->esz, kWsAlign);
+  p->off_cols = off;
+  off = align_up(off + (size_t)p->gcol_chunk * p->nsplit * p->nU * p->NC * 2, kWsAlign);
   p->off_gx = off; off = align_up(off + (size_t)d->B * d->H * d->W * p->CS * 4, kWsAlign);
   p->off_gw = off; off = align_up(off + (size_t)d->Co * p->K2 * p->CS * 4, kWsAlign);
   p->off_gb = off; off = align_up(off + (size_t)d->Co * 4, kWsAlign);
@@ -332,12 +335,30 @@ int dcn_backward(const dcn_desc* d, const void* input, const void* weight, const
   a.num_sms = device_sms();
   a.dbg = debug_skip();
   a.vec_gout = aligned16(grad_output);
+  a.cols = ws + P.off_cols;
   static unsigned long long* dts_d = nullptr;
   if (getenv("DCN_DEBUG_TS")) {  // pipeline timestamps of CTA 0, printed to stderr (studies only)
     if (!dts_d && cudaMalloc(&dts_d, 1024 * sizeof(unsigned long long)) != cudaSuccess) dts_d = nullptr;
     if (dts_d) cudaMemsetAsync(dts_d, 0, 1024 * sizeof(unsigned long long), s);
     a.ts = dts_d;
   }
+  BwdWeightArgs w;
+  memset(&w, 0, sizeof(w));
+  w.plan = P;
+  w.cols = a.cols;
+  w.gpk = ws + P.off_go;
+  w.gw = gw;
+  w.err = a.err;
+  w.num_sms = a.num_sms;
+  w.dbg = a.dbg;
+  static unsigned long long* dts = nullptr;
+  if (getenv("DCN_DEBUG_TS")) {  // pipeline timestamps of CTA 0, printed to stderr (studies only)
+    if (!dts && cudaMalloc(&dts, 1024 * sizeof(unsigned long long)) != cudaSuccess) dts = nullptr;
+    if (dts) cudaMemsetAsync(dts, 0, 1024 * sizeof(unsigned long long), s);
+    w.ts = dts;
+  }
+  // per pixel chunk: column gradients (tcgen05), then the scatter (grad_input,
+  // grad_offset, grad_mask and the sampled columns), then the weight gradient
   for (long long p0 = 0; p0 < P.totalP; p0 += P.gcol_chunk) {
     a.pix0 = (int)p0;
     a.npix = (int)(P.totalP - p0 < P.gcol_chunk ? P.totalP - p0 : P.gcol_chunk);
@@ -349,41 +370,26 @@ int dcn_backward(const dcn_desc* d, const void* input, const void* weight, const
       TraceScope ts(TR_BACKWARD_SCATTER, s);
       if ((rc = launch_backward_scatter(a, s)) != DCN_OK) return rc;
     }
+    w.ks0 = (int)(p0 / 64);
+    w.nks = (a.npix + 63) / 64;
+    {
+      TraceScope ts(TR_BACKWARD_WEIGHT, s);
+      if ((rc = launch_backward_weight(w, s)) != DCN_OK) return rc;
+    }
+    if (w.ts) w.ts = nullptr;   // timestamps of the first chunk only
+    if (a.ts) a.ts = nullptr;
   }
-  if (a.ts) {
+  if (dts_d && getenv("DCN_DEBUG_TS")) {
     unsigned long long h[1024];
-    cudaMemcpyAsync(h, a.ts, sizeof(h), cudaMemcpyDeviceToHost, s);
+    cudaMemcpyAsync(h, dts_d, sizeof(h), cudaMemcpyDeviceToHost, s);
     cudaStreamSynchronize(s);
     fprintf(stderr, "DCN_TSD");
     for (int i = 0; i < 1024; ++i) fprintf(stderr, " %llu", h[i]);
     fprintf(stderr, "\n");
   }
-  BwdWeightArgs w;
-  memset(&w, 0, sizeof(w));
-  w.plan = P;
-  w.xt = ws + P.off_x;
-  w.offset = offset;
-  w.mask = mask;
-  w.gout = grad_output;
-  w.gpk = ws + P.off_go;
-  w.gw = gw;
-  w.err = a.err;
-  w.num_sms = a.num_sms;
-  w.dbg = a.dbg;
-  w.vec_gout = aligned16(grad_output);
-  static unsigned long long* dts = nullptr;
-  if (getenv("DCN_DEBUG_TS")) {  // pipeline timestamps of CTA 0, printed to stderr (studies only)
-    if (!dts && cudaMalloc(&dts, 1024 * sizeof(unsigned long long)) != cudaSuccess) dts = nullptr;
-    if (dts) cudaMemsetAsync(dts, 0, 1024 * sizeof(unsigned long long), s);
-    w.ts = dts;
-  }
-  {
-    TraceScope ts(TR_BACKWARD_WEIGHT, s);
-    if ((rc = launch_backward_weight(w, s)) != DCN_OK) return rc;
-  }
-  if (w.ts) {
+  if (dts && getenv("DCN_DEBUG_TS")) {
     unsigned long long h[1024];
-    cudaMemcpyAsync(h, w.ts, sizeof(h), cudaMemcpyDeviceToHost, s);
+    cudaMemcpyAsync(h, dts, sizeof(h), cudaMemcpyDeviceToHost, s);
     cudaStreamSynchronize(s);
     fprintf(stderr, "DCN_TSW");
     for (int i = 0; i < 1024; ++i) fprintf(stderr, " %llu", h[i]);

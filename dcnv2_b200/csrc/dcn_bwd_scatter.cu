@@ -18,6 +18,13 @@
 // are reduced over the 8 lanes with shuffles.  The scatter writes grad_input in
 // logical channel order (lane q: channels 4q..4q+3 and 32+4q..32+4q+3 of the
 // block), so each red.add instruction of a pixel fills whole 32-byte sectors.
+//
+// The same corner loads also give the sampled column mask * bilinear(x_c) of
+// every (pixel, tap, channel): the kernel writes it, rounded to the operand type
+// (a bf16 hi/lo pair for f32), in the layout of the weight-gradient GEMM's B
+// tiles, so that GEMM streams it with bulk copies instead of gathering it again
+// (the reference re-runs im2col for it, com.cu:637-706).  Pixels past the end
+// of the chunk up to its last 64-pixel block get zero columns.
 #include "dcn_common.cuh"
 #include "dcn_gather.cuh"
 #include "dcn_kernels.h"
@@ -39,7 +46,7 @@ __device__ __forceinline__ float2 mul2(float2 a, float s) {
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kThreads) dcn_bwd_scatter_kernel(const __grid_constant__ BwdDataArgs a) {
+__global__ void __launch_bounds__(kThreads, 3) dcn_bwd_scatter_kernel(const __grid_constant__ BwdDataArgs a) {
   using G = typename std::conditional<std::is_same<T, float>::value, float, T>::type;
   constexpr int LD = GatherShape<T>::kLD;
   const Plan& P = a.plan;
@@ -49,7 +56,9 @@ __global__ void __launch_bounds__(kThreads) dcn_bwd_scatter_kernel(const __grid_
   const int nTG = P.K2 * P.dg;
   const int rowlen = nTG * P.Cgp;
   const int pend = a.pix0 + a.npix;
-  const int ngrp = (a.npix + 31) / 32;          // 32-pixel groups of the chunk
+  const int ngrp = (a.npix + 63) / 64 * 2;      // 32-pixel groups covering the chunk's 64-pixel blocks
+  const int nblk = P.NC / kChunk;
+  const int natoms = P.nU * nblk;               // 8 KB column blocks per 64 pixels (one of hi/lo)
   const int nitems = ngrp * nTG;                // warp items: (32-pixel group, tap-group)
   const T* __restrict__ xt = reinterpret_cast<const T*>(a.xt);
   const T* __restrict__ off = reinterpret_cast<const T*>(a.offset);
@@ -107,9 +116,15 @@ __global__ void __launch_bounds__(kThreads) dcn_bwd_scatter_kernel(const __grid_
       const float bw[4] = {(cval & 1u) ? hh * hw : 0.f, (cval & 2u) ? hh * lw : 0.f,
                            (cval & 4u) ? lh * hw : 0.f, (cval & 8u) ? lh * lw : 0.f};
       float S[4] = {0.f, 0.f, 0.f, 0.f};
-      if (cval != 0u) {
-        const G* grow = gcol + (size_t)(unsigned)(pix - a.pix0) * rowlen + tg * P.Cgp + q * 8;
-        for (int cb = 0; cb < P.nCB; ++cb) {
+      const G* grow = gcol + (size_t)(unsigned)(pix - a.pix0) * rowlen + tg * P.Cgp + q * 8;
+      const float wc[4] = {bw[0] * m, bw[1] * m, bw[2] * m, bw[3] * m};
+      const int pl = pix - a.pix0, crow = pl & 63;
+      uint8_t* cdst = a.cols == nullptr ? nullptr
+                      : a.cols + ((size_t)(unsigned)(pl >> 6) * P.nsplit * natoms) * 8192u +
+                            crow * 128 + ((q ^ (crow & 7)) << 4);
+      for (int cb = 0; cb < P.nCB; ++cb) {
+        float col[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (cval != 0u) {
           const int cofs = g * P.Cgp + cb * kChunk;
           uint4 graw[sizeof(G) / 2];
 #pragma unroll
@@ -136,13 +151,16 @@ __global__ void __launch_bounds__(kThreads) dcn_bwd_scatter_kernel(const __grid_
             float v[8];
             unpack_slice<T>(raw[c], v);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) S[c] = fmaf(gc[e], v[e], S[c]);
+            for (int e = 0; e < 8; ++e) {
+              S[c] = fmaf(gc[e], v[e], S[c]);
+              col[e] = fmaf(wc[c], v[e], col[e]);
+            }
           }
           if (!(a.dbg & 2)) {
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
               if (cval & (1u << c)) {
-                const float sk = bw[c] * m;
+                const float sk = wc[c];
                 float* dst = a.gx_nhwc + (size_t)(unsigned)((gidx + d[c]) * P.CS + cofs + 4 * q);
                 const float2 s0 = mul2(make_float2(gc[0], gc[1]), sk);
                 const float2 s1 = mul2(make_float2(gc[2], gc[3]), sk);
@@ -152,6 +170,29 @@ __global__ void __launch_bounds__(kThreads) dcn_bwd_scatter_kernel(const __grid_
                 red_add_v4(dst + 32, s2.x, s2.y, s3.x, s3.y);
               }
             }
+          }
+        }
+        if (cdst != nullptr) {
+          // column block of (unit tg * nCC + channel chunk, 64-channel block inside it)
+          const int c64 = cb * kChunk;
+          const int atom = (tg * P.nCC + c64 / P.NC) * nblk + (c64 % P.NC) / kChunk;
+          uint8_t* dst = cdst + (size_t)atom * 8192u;
+          if constexpr (OpOf<T>::kSplit) {
+            uint4 hi, lo;
+            split2(col[0], col[1], hi.x, lo.x);
+            split2(col[2], col[3], hi.y, lo.y);
+            split2(col[4], col[5], hi.z, lo.z);
+            split2(col[6], col[7], hi.w, lo.w);
+            *reinterpret_cast<uint4*>(dst) = hi;
+            *reinterpret_cast<uint4*>(dst + (size_t)natoms * 8192u) = lo;
+          } else {
+            constexpr int kBF = OpOf<T>::kBF16;
+            uint4 u;
+            u.x = pack2<kBF>(col[0], col[1]);
+            u.y = pack2<kBF>(col[2], col[3]);
+            u.z = pack2<kBF>(col[4], col[5]);
+            u.w = pack2<kBF>(col[6], col[7]);
+            *reinterpret_cast<uint4*>(dst) = u;
           }
         }
       }
@@ -187,7 +228,7 @@ __global__ void __launch_bounds__(kThreads) dcn_bwd_scatter_kernel(const __grid_
 
 int launch_backward_scatter(const BwdDataArgs& a, cudaStream_t stream) {
   const Plan& P = a.plan;
-  const long long nitems = (long long)(a.npix + 31) / 32 * (P.K2 * P.dg);
+  const long long nitems = (long long)(a.npix + 63) / 64 * 2 * (P.K2 * P.dg);
   long long blocks = (nitems + 7) / 8;
   const long long cap = (long long)a.num_sms * 16;
   if (blocks > cap) blocks = cap;

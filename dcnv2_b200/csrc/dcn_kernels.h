@@ -48,22 +48,22 @@ struct BwdDataArgs {
   int dbg;              // experiment switches (DCN_DEBUG_SKIP); 0 in normal use
   int a_slots;          // grad_out chunk slots in smem (set by the launcher)
   int vec_gout;         // grad_output 16-byte aligned (vector loads allowed when HoWo % 8 == 0)
+  uint8_t* cols;        // sampled columns of the chunk for the weight gradient, written by the
+                        // scatter: [npix/64][nsplit][nU*NC/64] 8 KB blocks of 64 pixels x 64
+                        // channels (pixel rows of 128 B, SW128 swizzled; MN-major UMMA B tiles)
 };
 
 struct BwdWeightArgs {
   Plan plan;
   unsigned long long* ts;  // optional pipeline timestamps of CTA 0 (DCN_DEBUG_TS), else null
-  const void* xt;
-  const void* offset;
-  const void* mask;
-  const void* gout;
+  const uint8_t* cols;  // sampled columns of the chunk (BwdDataArgs::cols)
+  int ks0, nks;         // the chunk's first 64-pixel block and its number of blocks
   const uint8_t* gpk;   // packed grad_output blocks (as above)
   float* gw;            // fp32 [Co][K2][dg][Cgp], zero-initialised, accumulated
   int* err;
   int stages;
   int num_sms;
   int dbg;              // experiment switches (DCN_DEBUG_SKIP); 0 in normal use
-  int vec_gout;
 };
 
 // Packing / finishing kernels (dcn_pack.cu)

@@ -42,9 +42,9 @@ struct Plan {
   int wg_nsplit_px;   // CTAs along the pixel reduction
   int wg_ksteps;      // 64-pixel K steps in total (ceil(totalP/64))
   // workspace layout (bytes)
-  size_t off_status, off_x, off_wf, off_wd, off_go, off_gcol, off_gx, off_gw, off_gb;
+  size_t off_status, off_x, off_wf, off_wd, off_go, off_gcol, off_cols, off_gx, off_gw, off_gb;
   int nPB;               // 64-pixel blocks of the packed grad_output
-  int gcol_chunk;        // pixels per backward-data chunk (multiple of 128)
+  int gcol_chunk;        // pixels per backward chunk (multiple of 128)
   size_t fwd_bytes, bwd_bytes;
   size_t wf_tile_bytes;   // one forward weight tile (NT rows x 128 B x nsplit)
   size_t wd_tile_bytes;   // one backward-data weight tile (gNC rows x 128 B x nsplit)

@@ -101,3 +101,43 @@ def test_golden_vectors_fp32(path):
     assert rel_err(y.cpu().numpy(), z["y"]) <= 1e-3
     for name, g in zip(NAMES, grads):
         assert rel_err(g.cpu().numpy(), z[name]) <= 1e-4, name
+
+
+_CHUNKED_SCRIPT = r"""
+import sys, numpy as np, torch
+sys.path.insert(0, sys.argv[1])
+from dcn_cases import Case, make_inputs
+from dcnv2_b200 import _C
+c = Case("chunked", 3, 40, 37, 29, 72, 3, 3, off_std=2.0)
+dt = {"bf16": torch.bfloat16, "fp32": torch.float32}[sys.argv[3]]
+x, w, b, off, m, gy = [t.to(dt).cuda() for t in make_inputs(c, seed=3)]
+g = _C.dcn_v2_backward(x, w, m, off, b, gy, 1, 1, 1, 1)
+torch.cuda.synchronize()
+np.savez(sys.argv[2], *[t.float().cpu().numpy() for t in g])
+"""
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", ["fp32", "bf16"])
+def test_backward_in_pixel_chunks(tmp_path, dtype):
+    """A 1 MB chunk budget (DCN_GCOL_MB=1) splits the backward of a 3219-pixel
+    problem into chunks of 384 (bf16) or 128 (fp32) pixels, the last one ragged
+    (not a multiple of 64):
+    every gradient still matches the float64 oracle."""
+    import os
+    import subprocess
+    import sys
+    from dcn_cases import Case
+    c = Case("chunked", 3, 40, 37, 29, 72, 3, 3, off_std=2.0)
+    out = tmp_path / "g.npz"
+    env = dict(os.environ, DCN_GCOL_MB="1")
+    here = os.path.dirname(os.path.abspath(__file__))
+    subprocess.run([sys.executable, "-c", _CHUNKED_SCRIPT, here, str(out), dtype], env=env,
+                   check=True, cwd=os.path.dirname(here), timeout=300)
+    z = np.load(out)
+    tdt = {"bf16": torch.bfloat16, "fp32": torch.float32}[dtype]
+    x, w, b, off, m, gy = [t.to(tdt).double().numpy() for t in make_inputs(c, seed=3)]
+    ref = oracle.backward(x, w, off, m, gy, 1, 1, 1, 1)
+    tol = 1e-4 if dtype == "fp32" else 1e-2
+    for i, name in enumerate(NAMES):
+        assert rel_err(z[f"arr_{i}"], ref[i]) <= tol, name
