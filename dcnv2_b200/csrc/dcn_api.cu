@@ -135,9 +135,12 @@ int make_plan(const dcn_desc* d, Plan* p, int num_sms) {
   p->nU = p->K2 * d->dg * p->nCC;
   {
     const int nTG = p->K2 * d->dg;
-    p->gT = p->nCC == 1 ? 256 / p->NC : 1;
-    if (p->gT > nTG) p->gT = nTG;
-    if (p->gT < 1) p->gT = 1;
+    // (tap, group)s per unit: at most 256 columns, balanced over the units
+    int gmax = p->nCC == 1 ? 256 / p->NC : 1;
+    if (gmax > nTG) gmax = nTG;
+    if (gmax < 1) gmax = 1;
+    const int nset = ceil_div(nTG, gmax);
+    p->gT = ceil_div(nTG, nset);
     p->gNC = p->gT * p->NC;
     p->gnU = ceil_div(nTG, p->gT) * p->nCC;
   }

@@ -13,43 +13,70 @@ namespace dcn {
 namespace {
 
 // [B][C][H*W] -> [B][H*W][dg][Cgp] (channel order of perm_logical inside each
-// 64-channel block); padded channels are written as zero.  One
-// CTA moves a 64-pixel x 64-channel block: 16-byte loads along pixels (when
-// `vec`: H*W % 8 == 0 and x 16-byte aligned), 16-byte stores along channels.
+// 64-channel block); padded channels are written as zero.  A CTA moves 64-pixel
+// x 64-channel blocks in a grid-stride loop: 16-byte loads along pixels (when
+// `vec`: H*W % 8 == 0 and x 16-byte aligned), 16-byte stores along channels;
+// the next block's loads are issued before the current block is stored.
 template <typename T>
 __global__ void __launch_bounds__(256) pack_input_kernel(const T* __restrict__ x,
                                                          T* __restrict__ xt, int C, int HW,
-                                                         int Cg, int Cgp, int CS, int vec) {
+                                                         int Cg, int Cgp, int CS, int vec,
+                                                         int npb, int ncb, int nblocks) {
   constexpr int EPV = 16 / (int)sizeof(T);           // elements per 16-byte vector
+  constexpr int kItems = 64 * (64 / EPV) / 256;       // 16-byte loads per thread and block
   __shared__ __align__(16) T tile[64][64 + EPV];      // [channel][pixel]
-  const int b = blockIdx.z;
-  const int d0 = blockIdx.y * 64;                     // destination channel block
-  const int p0 = blockIdx.x * 64;
-  const int g = d0 / Cgp, cb = d0 - g * Cgp;
-  const T* xb = x + (size_t)b * C * HW;
   const int tid = threadIdx.x;
-  for (int item = tid; item < 64 * (64 / EPV); item += 256) {
-    const int c = item / (64 / EPV), pv = item - c * (64 / EPV);
-    const int cc = cb + c, p = p0 + pv * EPV;
-    T* dst = &tile[c][pv * EPV];
-    if (cc < Cg && vec && p + EPV <= HW) {
-      *reinterpret_cast<uint4*>(dst) =
-          ldg_nc_v4(xb + (size_t)(g * Cg + cc) * HW + p);
-    } else {
-      for (int e = 0; e < EPV; ++e)
-        dst[e] = (cc < Cg && p + e < HW) ? xb[(size_t)(g * Cg + cc) * HW + p + e] : Elem<T>::from_f(0.f);
-    }
-  }
-  __syncthreads();
-  T* xo = xt + (size_t)b * HW * CS + d0;
-  for (int item = tid; item < 64 * (64 / EPV); item += 256) {
-    const int pl = item / (64 / EPV), cv = item - pl * (64 / EPV);
-    const int p = p0 + pl;
-    if (p >= HW) continue;
-    alignas(16) T v[EPV];
+  uint4 raw[kItems];
+  auto issue = [&](int blk) {
+    if (!vec || blk >= nblocks) return;
+    const int pbk = blk % npb, rest = blk / npb;
+    const int d0 = (rest % ncb) * 64, b = rest / ncb;
+    const int g = d0 / Cgp, cb = d0 - g * Cgp;
+    const T* xb = x + (size_t)b * C * HW;
 #pragma unroll
-    for (int e = 0; e < EPV; ++e) v[e] = tile[perm_logical(cv * EPV + e)][pl];
-    *reinterpret_cast<uint4*>(xo + (size_t)p * CS + cv * EPV) = *reinterpret_cast<const uint4*>(v);
+    for (int k = 0; k < kItems; ++k) {
+      const int item = tid + 256 * k;
+      const int c = item / (64 / EPV), pv = item - c * (64 / EPV);
+      const int cc = cb + c, p = pbk * 64 + pv * EPV;
+      raw[k] = (cc < Cg && p + EPV <= HW) ? ldg_nc_v4(xb + (size_t)(g * Cg + cc) * HW + p)
+                                          : make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+  issue(blockIdx.x);
+  for (int blk = blockIdx.x; blk < nblocks; blk += gridDim.x) {
+    const int pbk = blk % npb, rest = blk / npb;
+    const int d0 = (rest % ncb) * 64, b = rest / ncb;
+    const int p0 = pbk * 64;
+    const int g = d0 / Cgp, cb = d0 - g * Cgp;
+    const T* xb = x + (size_t)b * C * HW;
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) {
+      const int item = tid + 256 * k;
+      const int c = item / (64 / EPV), pv = item - c * (64 / EPV);
+      const int cc = cb + c, p = p0 + pv * EPV;
+      T* dst = &tile[c][pv * EPV];
+      if (vec && (cc >= Cg || p + EPV <= HW)) {
+        *reinterpret_cast<uint4*>(dst) = raw[k];
+      } else {
+        for (int e = 0; e < EPV; ++e)
+          dst[e] = (cc < Cg && p + e < HW) ? xb[(size_t)(g * Cg + cc) * HW + p + e] : Elem<T>::from_f(0.f);
+      }
+    }
+    issue(blk + gridDim.x);
+    __syncthreads();
+    T* xo = xt + (size_t)b * HW * CS + d0;
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) {
+      const int item = tid + 256 * k;
+      const int pl = item / (64 / EPV), cv = item - pl * (64 / EPV);
+      const int p = p0 + pl;
+      if (p >= HW) continue;
+      alignas(16) T v[EPV];
+#pragma unroll
+      for (int e = 0; e < EPV; ++e) v[e] = tile[perm_logical(cv * EPV + e)][pl];
+      *reinterpret_cast<uint4*>(xo + (size_t)p * CS + cv * EPV) = *reinterpret_cast<const uint4*>(v);
+    }
   }
 }
 
@@ -162,6 +189,16 @@ __global__ void __launch_bounds__(256) pack_gout_kernel(const T* __restrict__ go
   const int nPB = (int)((P.totalP + 63) / 64);
   const size_t blk_bytes = (size_t)P.nsplit * 8192;
   float bsum[2] = {0.f, 0.f};
+  // the next block's grad_output rows are loaded while this block is stored
+  GoutRaw<T> raw[2];
+  auto issue = [&](int pb) {
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int item = tid + 256 * k;
+      if (vec && pb < nPB) gout_raw_load<T>(gout, P, pb * 64 + (item & 7) * 8, ko * kChunk + (item >> 3), raw[k]);
+    }
+  };
+  issue(blockIdx.x);
   for (int pb = blockIdx.x; pb < nPB; pb += gridDim.x) {
     __syncthreads();
 #pragma unroll
@@ -171,9 +208,7 @@ __global__ void __launch_bounds__(256) pack_gout_kernel(const T* __restrict__ go
       float v[8];
       const int co = ko * kChunk + col;
       if (vec) {
-        GoutRaw<T> raw;
-        gout_raw_load<T>(gout, P, pb * 64 + ch * 8, co, raw);
-        gout_raw_to_f<T>(raw, v);
+        gout_raw_to_f<T>(raw[k], v);
       } else {
         load8_gout<T>(gout, P, pb * 64 + ch * 8, co, false, v);
       }
@@ -181,6 +216,7 @@ __global__ void __launch_bounds__(256) pack_gout_kernel(const T* __restrict__ go
 #pragma unroll
       for (int e = 0; e < 8; ++e) tile[col][ch * 8 + e] = v[e];
     }
+    issue(pb + gridDim.x);
     __syncthreads();
     uint8_t* blk = gpk + ((size_t)pb * P.nKo + ko) * blk_bytes;
 #pragma unroll
@@ -305,11 +341,14 @@ int grid_for(long long n, int threads) {
 int launch_pack_input(const Plan& P, const void* x, void* xt, cudaStream_t s) {
   const int HW = P.H * P.W;
   const int vec = (HW % 8 == 0) && (((uintptr_t)x & 15u) == 0);
-  dim3 grid(ceil_div(HW, 64), P.CS / 64, P.B);
+  const int npb = ceil_div(HW, 64), ncb = P.CS / 64;
+  const long long nblocks = (long long)npb * ncb * P.B;
+  if (nblocks >= (1LL << 31)) return DCN_E_UNSUPPORTED;
+  const int grid = (int)(nblocks < 148LL * 8 ? nblocks : 148LL * 8);
   return dispatch(P.dtype, [&](auto tag) {
     using T = decltype(tag);
     pack_input_kernel<T><<<grid, 256, 0, s>>>(static_cast<const T*>(x), static_cast<T*>(xt), P.C,
-                                              HW, P.Cg, P.Cgp, P.CS, vec);
+                                              HW, P.Cg, P.Cgp, P.CS, vec, npb, ncb, (int)nblocks);
   });
 }
 
