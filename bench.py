@@ -342,11 +342,14 @@ def main():
     else:
         # scatter: read gcol (P*K2*C), x (B*C*H*W), offset+mask (3*K2*P); read+write the
         # fp32 grad_input accumulator (2 * 4*B*C*H*W); write grad_offset+grad_mask (3*K2*P)
+        # and the sampled columns for the weight gradient (P*K2*C operands, hi+lo for f32)
         P = B * Ho * Wo
-        nbytes = (P * K2 * C * esz + B * C * H * W * esz + 6 * K2 * P * esz + 8 * B * C * H * W)
+        nsplit = 2 if esz == 4 else 1
+        nbytes = (P * K2 * C * esz + B * C * H * W * esz + 6 * K2 * P * esz + 8 * B * C * H * W
+                  + P * K2 * C * 2 * nsplit)
         nbytes /= n_dom / args.steps  # per launch (the scatter may run in chunks)
         work, bound, unit, peak = nbytes, "hbm", "GB/s", peaks["hbm_gbs"]
-        basis = f"algorithmic bytes {nbytes:.4g} per launch (gcol, x, offset/mask, fp32 grad_input acc, outputs)"
+        basis = f"algorithmic bytes {nbytes:.4g} per launch (gcol, x, offset/mask, fp32 grad_input acc, outputs, columns)"
         achieved = work / (per_launch_ms * 1e-3) / 1e9
     traffic = load_traffic(dom, args.workload, args.dtype)
     # kernels of this library in the timed region (the accumulator memset is a runtime call)
