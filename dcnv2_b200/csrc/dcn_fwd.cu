@@ -48,7 +48,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const int S = a.stages;
 
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t bars[2 * kMaxStages + 7];
+  __shared__ __align__(8) uint64_t bars[2 * kMaxStages + 11];
   __shared__ uint32_t tmem_slot;
   __shared__ __align__(16) uint8_t epi_stage[kEpiWarps][16 * 32 * 2];
   __shared__ volatile int abort_flag;
@@ -61,10 +61,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const uint32_t drain = smem_u32(&bars[2 * kMaxStages + 4]);
   const uint32_t geof = smem_u32(&bars[2 * kMaxStages + 5]);  // geometry window written
   const uint32_t geoe = smem_u32(&bars[2 * kMaxStages + 6]);  // geometry window consumed
-  // geometry window after the stage ring: [kGeoTaps][128] corner weights and indices
+  const uint32_t gready0 = smem_u32(&bars[2 * kMaxStages + 7]);  // geometry window built (x2)
+  const uint32_t gfree0 = smem_u32(&bars[2 * kMaxStages + 9]);   // geometry window released (x2)
+  // geometry windows after the stage ring: NB x [kGeoTaps][128] corner weights
+  // and indices, then the bias.  NB = 2: the epilogue warps build the window of
+  // tile i+1 while the producers gather tile i (every (tap, group) of a tile
+  // fits one window); NB = 1: the producers build each window themselves.
+  const int NB = a.geo_bufs;
   float4* sgeo_w = reinterpret_cast<float4*>(smem_raw + ((sbase - smem_u32(smem_raw)) + S * stageBytes));
-  int* sgeo_idx = reinterpret_cast<int*>(sgeo_w + kGeoTaps * kTileM);
-  float* sbias = reinterpret_cast<float*>(sgeo_idx + kGeoTaps * kTileM);  // [Co]
+  int* sgeo_idx = reinterpret_cast<int*>(sgeo_w + NB * kGeoTaps * kTileM);
+  float* sbias = reinterpret_cast<float*>(sgeo_idx + NB * kGeoTaps * kTileM);  // [Co]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
@@ -79,6 +85,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     mbar_init(drain, 1);
     mbar_init(geof, kProdThreads / 32);
     mbar_init(geoe, kProdThreads / 32);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(gready0 + 8 * i, kEpiWarps);
+      mbar_init(gfree0 + 8 * i, kProdThreads / 32);
+    }
     abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -97,6 +107,54 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const int HoWo = P.HoWo;
   if (warp == 0) DCN_TS(1000);
 
+  // Builds geometry window slot `buf` for pixel tile pt and (tap, group)s
+  // tg0 .. tg0 + wt - 1 with 256 threads (this one is thread gt).  Thread gt
+  // owns row gt % 128 and slots gt / 128 + 2k: the row's coordinates are
+  // computed once, and every offset / mask load of the window is issued before
+  // the first one is used, so their latencies overlap.
+  auto build_geometry = [&](int pt, int tg0, int wt, int buf, int gt) {
+    constexpr int KI = (kGeoTaps * kTileM + 255) / 256;
+    const T* __restrict__ off = reinterpret_cast<const T*>(a.offset);
+    const T* __restrict__ msk = reinterpret_cast<const T*>(a.mask);
+    const int HW = P.H * P.W;
+    const int row = gt & (kTileM - 1), slot0 = gt >> 7;
+    const int pix = pt * kTileM + row;
+    const bool pv = pix < P.totalP && !(a.dbg & 1);
+    const int b = pv ? pix / HoWo : 0, p = pv ? pix - b * HoWo : 0;
+    const int ho = p / P.Wo, wo = p - ho * P.Wo;
+    uint32_t rh[KI], rw[KI], rm[KI];
+#pragma unroll
+    for (int k = 0; k < KI; ++k) {
+      const int slot = slot0 + 2 * k;
+      rh[k] = rw[k] = rm[k] = 0u;
+      if (pv && slot < wt) {
+        const int tgi = tg0 + slot;
+        const int t = tgi / P.dg, gi = tgi - t * P.dg;
+        const int ob = ((b * P.dg + gi) * 2 * P.K2 + 2 * t) * HoWo + p;
+        rh[k] = ldg_raw<T>(off + ob);
+        rw[k] = ldg_raw<T>(off + ob + HoWo);
+        rm[k] = ldg_raw<T>(msk + ((b * P.dg + gi) * P.K2 + t) * HoWo + p);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < KI; ++k) {
+      const int slot = slot0 + 2 * k;
+      if (slot < wt) {
+        PixGeo r = zero_pixgeo();
+        if (pv) {
+          const int t = (tg0 + slot) / P.dg;
+          const int i = t / P.kw, j = t - i * P.kw;
+          const float hs = (float)(ho * P.sh - P.ph + i * P.dh) + raw_to_f<T>(rh[k]);
+          const float ws = (float)(wo * P.sw - P.pw + j * P.dw) + raw_to_f<T>(rw[k]);
+          r = make_pixgeo(b * HW, hs, ws, raw_to_f<T>(rm[k]), P.H, P.W);
+        }
+        const int e = (buf * kGeoTaps + slot) * kTileM + row;
+        sgeo_idx[e] = r.gidx;
+        sgeo_w[e] = make_float4(r.w[0], r.w[1], r.w[2], r.w[3]);
+      }
+    }
+  };
+
   // Roles by warpgroup; setmaxnreg at the top of each branch (one instruction
   // per warpgroup).  Launch: 640 threads x 96 registers; after the split
   // producers 2 x 4 warps x 160, epilogue 2 x 4 warps x 64, control 4 warps x 32
@@ -112,10 +170,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     constexpr int BATCH = sizeof(T) == 4 ? 2 : 4;
     const int lp = lane / LPP, q = lane % LPP;
     const T* __restrict__ xt = reinterpret_cast<const T*>(a.xt);
-    const T* __restrict__ off = reinterpret_cast<const T*>(a.offset);
-    const T* __restrict__ msk = reinterpret_cast<const T*>(a.mask);
-    const int HW = P.H * P.W;
-    uint32_t kidx = 0, gcnt = 0;
+    uint32_t kidx = 0, gcnt = 0, gbuf = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < nTiles && ok; tile += gridDim.x) {
       const int pt = tile / P.nCoT;
@@ -134,38 +189,29 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const int g = tg % P.dg;
         const int tl = tg % nwin_t;                 // tap slot inside the window
         if (cb == 0 && tl == 0) {
-          __syncwarp();
-          if (lane == 0) mbar_arrive(geoe);
-          if (!mbar_wait(geoe, gcnt & 1u, a.err, &abort_flag)) { ok = false; break; }
-          const int wt = min(nwin_t, nTG - tg);     // taps in this window
-          for (int item = tid; item < wt * kTileM; item += kProdThreads) {
-            const int slot = item / kTileM, row = item - slot * kTileM;
-            const int tgi = tg + slot;
-            const int t = tgi / P.dg, gi = tgi - t * P.dg;
-            const int pix = pt * kTileM + row;
-            PixGeo r = zero_pixgeo();
-            if (pix < P.totalP && !(a.dbg & 1)) {
-              const int b = pix / HoWo, p = pix - b * HoWo;
-              const int ho = p / P.Wo, wo = p - ho * P.Wo;
-              const int i = t / P.kw, j = t - i * P.kw;
-              const int ob = ((b * P.dg + gi) * 2 * P.K2 + 2 * t) * HoWo + p;
-              const float hs = (float)(ho * P.sh - P.ph + i * P.dh) + ldf(off + ob);
-              const float ws = (float)(wo * P.sw - P.pw + j * P.dw) + ldf(off + ob + HoWo);
-              const float m = ldf(msk + ((b * P.dg + gi) * P.K2 + t) * HoWo + p);
-              r = make_pixgeo(b * HW, hs, ws, m, P.H, P.W);
-            }
-            sgeo_idx[item] = r.gidx;
-            sgeo_w[item] = make_float4(r.w[0], r.w[1], r.w[2], r.w[3]);
+          if (NB == 2) {
+            // window built by the epilogue warps: release the previous one, wait for this one
+            __syncwarp();
+            if (gcnt > 0 && lane == 0) mbar_arrive(gfree0 + 8 * ((gcnt - 1) & 1u));
+            if (!mbar_wait(gready0 + 8 * (gcnt & 1u), (gcnt >> 1) & 1u, a.err, &abort_flag)) { ok = false; break; }
+            gbuf = gcnt & 1u;
+          } else {
+            // built here by all producer threads; two bounded handoffs per window
+            __syncwarp();
+            if (lane == 0) mbar_arrive(geoe);
+            if (!mbar_wait(geoe, gcnt & 1u, a.err, &abort_flag)) { ok = false; break; }
+            build_geometry(pt, tg, min(nwin_t, nTG - tg), 0, tid);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(geof);
+            if (!mbar_wait(geof, gcnt & 1u, a.err, &abort_flag)) { ok = false; break; }
+            gbuf = 0;
           }
-          __syncwarp();
-          if (lane == 0) mbar_arrive(geof);
-          if (!mbar_wait(geof, gcnt & 1u, a.err, &abort_flag)) { ok = false; break; }
           ++gcnt;
         }
         if (cb == 0) {
 #pragma unroll
           for (int it = 0; it < ITER; ++it) {
-            const int e = tl * kTileM + warp * 16 + it * PPI + lp;
+            const int e = (gbuf * kGeoTaps + tl) * kTileM + warp * 16 + it * PPI + lp;
             const float4 w4 = sgeo_w[e];
             geo[it].gidx = sgeo_idx[e];
             geo[it].w[0] = w4.x;
@@ -207,9 +253,24 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const int row = q * 32 + lane;
     T* __restrict__ y = reinterpret_cast<T*>(a.out);
     int it = 0;
+    int gnext = 0;                                  // next geometry window to build (NB == 2)
     for (int tile = blockIdx.x; tile < nTiles; tile += gridDim.x, ++it) {
       const int pt = tile / P.nCoT, ct = tile - pt * P.nCoT;
       const int ab = it & 1;
+      if (NB == 2) {
+        // windows of this tile and the next one (one window per tile): the slot
+        // of window w is free once the producers started window w - 1
+        bool gok = true;
+        for (; gnext <= it + 1 && blockIdx.x + gnext * (int)gridDim.x < nTiles; ++gnext) {
+          const int gb = gnext & 1;
+          if (!mbar_wait(gfree0 + 8 * gb, ((gnext >> 1) & 1) ^ 1, a.err, &abort_flag)) { gok = false; break; }
+          const int gpt = (blockIdx.x + gnext * (int)gridDim.x) / P.nCoT;
+          build_geometry(gpt, 0, P.K2 * P.dg, gb, tid - kEpiWarp0 * 32);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(gready0 + 8 * gb);
+        }
+        if (!gok) break;
+      }
       if (!mbar_wait(accf0 + 8 * ab, (it >> 1) & 1, a.err, &abort_flag)) break;
       if (warp == kEpiWarp0) DCN_TS(800 + 2 * it);
       tc_fence_after();
@@ -345,13 +406,19 @@ int launch_forward(const FwdArgs& a, cudaStream_t stream) {
   if (P.Co > kMaxCo) return DCN_E_UNSUPPORTED;
   const int NS = P.nsplit;
   const size_t stageBytes = (size_t)NS * (128 * 128 + (size_t)P.NT * 128);
-  const size_t geoBytes = (size_t)kGeoTaps * kTileM * (sizeof(float4) + sizeof(int)) +
-                          (size_t)P.nCoT * P.NT * sizeof(float);   // geometry window + bias
+  // two geometry windows built by the epilogue warps when every (tap, group) of
+  // a tile fits one window and two stages still fit, else one built by the producers
+  const size_t geoWin = (size_t)kGeoTaps * kTileM * (sizeof(float4) + sizeof(int));
+  const size_t biasBytes = (size_t)P.nCoT * P.NT * sizeof(float);
+  int NB = (P.K2 * P.dg <= kGeoTaps && P.nCoT == 1) ? 2 : 1;
+  if (NB == 2 && (kFwdSmemBudget - 1024 - 2 * geoWin - biasBytes) / stageBytes < 2) NB = 1;
+  const size_t geoBytes = NB * geoWin + biasBytes;
   int S = (int)((kFwdSmemBudget - 1024 - geoBytes) / stageBytes);
   if (S > kMaxStages) S = kMaxStages;
   if (S < 2) return DCN_E_UNSUPPORTED;
   FwdArgs args = a;
   args.stages = S;
+  args.geo_bufs = NB;
   const size_t smem = 1024 + (size_t)S * stageBytes + geoBytes;
   const int nTiles = P.nPT * P.nCoT;
   int grid = nTiles < a.num_sms ? nTiles : a.num_sms;

@@ -24,6 +24,7 @@ struct FwdArgs {
   int vec_out;          // out is 16-byte aligned
   int* err;             // device error word
   int stages;
+  int geo_bufs;         // geometry windows: 2 built by the epilogue warps, 1 by the producers
   int num_sms;
   int dbg;              // experiment switches (DCN_DEBUG_SKIP); 0 in normal use
 };
