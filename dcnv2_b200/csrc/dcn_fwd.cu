@@ -287,28 +287,37 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       constexpr int EPV = 16 / (int)sizeof(T);       // elements per 16-byte vector
       constexpr int VPR = 32 / EPV;                  // vectors per 32-pixel row
       constexpr int JH = sizeof(T) == 4 ? 8 : 16;    // columns staged per pass
+      // this lane always stores run lane % VPR of the warp's 32 pixels (a run
+      // never crosses an image since HoWo % 8 == 0): its output offset is fixed
+      const int cvl = lane % VPR;
+      const int rpl = wpix0 + cvl * EPV;
+      const int rbl = vec ? rpl / HoWo : 0;
+      T* yrun = y + (size_t)rbl * P.Co * HoWo + (rpl - rbl * HoWo);
       for (int c0 = 16 * chalf; c0 < NT; c0 += 32) {
         float v[16];
         tmem_ld16(tbase + c0, v);
         if (vec) {
+          float bz[16];
+#pragma unroll
+          for (int j = 0; j < 16; j += 4) {
+            const float4 b4 = *reinterpret_cast<const float4*>(sbias + ct * NT + c0 + j);
+            bz[j] = b4.x; bz[j + 1] = b4.y; bz[j + 2] = b4.z; bz[j + 3] = b4.w;
+          }
           // stage [JH co][32 px] (JH = 16 columns for 16-bit outputs, 8 per pass for
           // f32 so the stage stays 1 KB a warp) then store 16-byte runs of pixels per co row
 #pragma unroll
           for (int h = 0; h < 16 / JH; ++h) {
 #pragma unroll
             for (int j = 0; j < JH; ++j)
-              stg[j * 32 + lane] = Elem<T>::from_f(v[h * JH + j] + sbias[ct * NT + c0 + h * JH + j]);
+              stg[j * 32 + lane] = Elem<T>::from_f(v[h * JH + j] + bz[h * JH + j]);
             __syncwarp();
 #pragma unroll
             for (int k = 0; k < JH * VPR / 32; ++k) {
-              const int idx = lane + 32 * k;
-              const int j = idx / VPR, cv = idx - j * VPR;
+              const int j = lane / VPR + k * (32 / VPR);
               const int co = ct * NT + c0 + h * JH + j;
               if (co < P.Co && !(a.dbg & 2)) {
-                const uint4 val = *reinterpret_cast<const uint4*>(stg + j * 32 + cv * EPV);
-                const int rp = wpix0 + cv * EPV;   // a run never crosses an image (HoWo % 8 == 0)
-                const int rb = (int)(rp / HoWo), rpp = (int)(rp - rb * HoWo);
-                *reinterpret_cast<uint4*>(y + ((size_t)rb * P.Co + co) * HoWo + rpp) = val;
+                const uint4 val = *reinterpret_cast<const uint4*>(stg + j * 32 + cvl * EPV);
+                *reinterpret_cast<uint4*>(yrun + (size_t)co * HoWo) = val;
               }
             }
             __syncwarp();
