@@ -204,13 +204,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       // One thread bulk-copies the two pre-packed 64-pixel blocks of each Co
       // chunk (K-major, 128-byte swizzle; f32: hi and lo) into the A ring.
       if (warp == 0 && lane == 0) {
-        uint32_t aseq = 0;
+        int r = 0;                                  // A ring slot and its phase
+        uint32_t ph = 0;
         bool ok = true;
         const uint32_t blk = NS * 8192u;
         for (int tile = r0; tile < nTiles && ok; tile += cpu) {
-          for (int ko = 0; ko < P.nKo; ++ko, ++aseq) {
-            const int r = aseq % RA;
-            const uint32_t ph = (aseq / RA) & 1u;
+          for (int ko = 0; ko < P.nKo; ++ko, (++r == RA ? (r = 0, ph ^= 1u) : 0u)) {
             if (!mbar_wait(aempty0 + 8 * r, ph ^ 1u, a.err, &abort_flag)) { ok = false; break; }
             const uint32_t at = abase + (uint32_t)r * aSlot;
             const int pb0 = a.pix0 / 64 + tile * 2;
@@ -227,12 +226,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == kTmaWarp) {
       // ---------------------------------------------- W^T tiles of the unit
       if (lane == 0) {
-        uint32_t kidx = 0;
+        int ws = 0;                                 // W^T ring stage and its phase
+        uint32_t wph = 0;
         bool ok = true;
         for (int tile = r0; tile < nTiles && ok; tile += cpu) {
-          for (int ko = 0; ko < P.nKo; ++ko, ++kidx) {
-            const int s = wres ? ko : (int)(kidx % S);
-            const uint32_t ph = wres ? 0u : (kidx / S) & 1u;
+          for (int ko = 0; ko < P.nKo; ++ko) {
+            const int s = wres ? ko : ws;
+            const uint32_t ph = wres ? 0u : wph;
+            if (++ws == S) { ws = 0; wph ^= 1u; }
             if (wres && tile != r0) break;        // resident: loaded once
             if (!wres && !mbar_wait(empty0 + 8 * s, ph ^ 1u, a.err, &abort_flag)) { ok = false; break; }
             const uint32_t bt = sbase + s * stageBytes;
@@ -247,18 +248,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---------------------------------------------- MMA issuer
       if (lane == 0) {
         const uint32_t idesc = make_idesc(OpOf<T>::kBF16, 0, 0, kTileM, NC);
-        uint32_t kidx = 0, aseq = 0, it = 0;
+        uint32_t it = 0;
+        int ar = 0, ms = 0;                         // A slot / W^T stage and their phases
+        uint32_t aph = 0, mph = 0;
         bool ok = true;
         for (int tile = r0; tile < nTiles && ok; tile += cpu, ++it) {
           const int ab = it & 1;
           if (!mbar_wait(acce0 + 8 * ab, ((it >> 1) & 1) ^ 1, a.err, &abort_flag)) { ok = false; break; }
           tc_fence_after();
           const uint32_t dt = tmem_base + (uint32_t)(ab * NC);
-          for (int ko = 0; ko < P.nKo; ++ko, ++kidx, ++aseq) {
-            const int r = aseq % RA;
-            if (!mbar_wait(afull0 + 8 * r, (aseq / RA) & 1u, a.err, &abort_flag)) { ok = false; break; }
-            const int s = wres ? ko : (int)(kidx % S);
-            const uint32_t ph = wres ? 0u : (kidx / S) & 1u;
+          for (int ko = 0; ko < P.nKo; ++ko) {
+            const int r = ar;
+            const uint32_t rph = aph;
+            if (++ar == RA) { ar = 0; aph ^= 1u; }
+            const int s = wres ? ko : ms;
+            const uint32_t ph = wres ? 0u : mph;
+            if (++ms == S) { ms = 0; mph ^= 1u; }
+            if (!mbar_wait(afull0 + 8 * r, rph, a.err, &abort_flag)) { ok = false; break; }
             if ((!wres || it == 0) && !mbar_wait(full0 + 8 * s, ph, a.err, &abort_flag)) { ok = false; break; }
             DCN_TS(700 + 4 * it + (ko & 3));
             tc_fence_after();

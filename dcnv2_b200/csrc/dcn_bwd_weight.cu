@@ -104,10 +104,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     // the chunk's column buffer and form the B tile in one copy (per hi/lo).
     if (lane == 0) {
       const uint32_t blk = NS * 8192u;
+      int ls = 0;                                   // ring stage and its phase
+      uint32_t lph = 0;
       for (int kl = kl0; kl < kl1; ++kl) {
         const uint32_t kidx = kl - kl0;
-        const int s = kidx % S;
-        const uint32_t ph = (kidx / S) & 1u;
+        const int s = ls;
+        const uint32_t ph = lph;
+        if (++ls == S) { ls = 0; lph ^= 1u; }
         if (!mbar_wait(empty0 + 8 * s, ph ^ 1u, a.err, &abort_flag)) break;
         DCN_TS(256 + 2 * kidx);
         const uint32_t at = sbase + s * stageBytes;
@@ -138,10 +141,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
       bool ok = true;
+      int ms = 0;                                   // ring stage and its phase
+      uint32_t mph = 0;
       for (int kl = kl0; kl < kl1; ++kl) {
         const uint32_t kidx = kl - kl0;
-        const int s = kidx % S;
-        const uint32_t ph = (kidx / S) & 1u;
+        const int s = ms;
+        const uint32_t ph = mph;
+        if (++ms == S) { ms = 0; mph ^= 1u; }
         if (!mbar_wait(full0 + 8 * s, ph, a.err, &abort_flag)) { ok = false; break; }
         DCN_TS(512 + 2 * kidx);
         tc_fence_after();

@@ -171,6 +171,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const int lp = lane / LPP, q = lane % LPP;
     const T* __restrict__ xt = reinterpret_cast<const T*>(a.xt);
     uint32_t kidx = 0, gcnt = 0, gbuf = 0;
+    int rs = 0;                                   // ring stage of step kidx and its phase
+    uint32_t rph = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < nTiles && ok; tile += gridDim.x) {
       const int pt = tile / P.nCoT;
@@ -183,11 +185,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const int nTG = P.K2 * P.dg;
       const int nwin_t = nTG < kGeoTaps ? nTG : kGeoTaps;
       PixGeo geo[ITER];
+      // (tap, group) tg, channel block cb, group g, tap slot tl of step kc, kept
+      // as counters (no divisions in the step loop)
+      int tg = 0, cb = 0, g = 0, tl = 0;
       for (int kc = 0; kc < P.nK && ok; ++kc, ++kidx) {
-        const int tg = kc / P.nCB;
-        const int cb = kc - tg * P.nCB;
-        const int g = tg % P.dg;
-        const int tl = tg % nwin_t;                 // tap slot inside the window
         if (cb == 0 && tl == 0) {
           if (NB == 2) {
             // window built by the epilogue warps: release the previous one, wait for this one
@@ -221,8 +222,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           }
         }
         if (warp == 0) DCN_TS(4 * kidx);
-        const int s = kidx % S;
-        const uint32_t ph = (kidx / S) & 1u;
+        const int s = rs;
+        const uint32_t ph = rph;
+        if (++rs == S) { rs = 0; rph ^= 1u; }
         const uint32_t atile = sbase + s * stageBytes;
         const int cofs = g * P.Cgp + cb * kChunk + q * CPL;
         uint4 v[BATCH][4][GS::kLD];
@@ -243,6 +245,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(full0 + 8 * s);
         if (warp == 0) DCN_TS(4 * kidx + 3);
+        if (++cb == P.nCB) {
+          cb = 0;
+          ++tg;
+          if (++g == P.dg) g = 0;
+          if (++tl == nwin_t) tl = 0;
+        }
       }
     }
   } else if (warp < kTmaWarp) {
@@ -340,14 +348,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     if (warp == kTmaWarp) {
     // ------------------------------------------------ weight tiles (bulk copy)
     if (lane == 0) {
-      uint32_t kidx = 0;
+      int s = 0;
+      uint32_t ph = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < nTiles && ok; tile += gridDim.x) {
         const int ct = tile % P.nCoT;
         const uint8_t* wsrc = a.wpk + (size_t)ct * P.nK * P.wf_tile_bytes;
-        for (int kc = 0; kc < P.nK; ++kc, ++kidx) {
-          const int s = kidx % S;
-          const uint32_t ph = (kidx / S) & 1u;
+        for (int kc = 0; kc < P.nK; ++kc, (++s == S ? (s = 0, ph ^= 1u) : 0u)) {
           if (!mbar_wait(empty0 + 8 * s, ph ^ 1u, a.err, &abort_flag)) { ok = false; break; }
           const uint32_t btile = sbase + s * stageBytes + NS * kATile;
           mbar_arrive_expect_tx(full0 + 8 * s, NS * bTile);
@@ -360,6 +367,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     if (warp == kMmaWarp && lane == 0) {
       const uint32_t idesc = make_idesc(OpOf<T>::kBF16, 0, 0, kTileM, NT);
       uint32_t kidx = 0;
+      int ms = 0;
+      uint32_t mph = 0;
       int it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < nTiles && ok; tile += gridDim.x, ++it) {
@@ -368,8 +377,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         tc_fence_after();
         const uint32_t dt = tmem_base + (uint32_t)(ab * NT);
         for (int kc = 0; kc < P.nK; ++kc, ++kidx) {
-          const int s = kidx % S;
-          const uint32_t ph = (kidx / S) & 1u;
+          const int s = ms;
+          const uint32_t ph = mph;
+          if (++ms == S) { ms = 0; mph ^= 1u; }
           if (!mbar_wait(full0 + 8 * s, ph, a.err, &abort_flag)) { ok = false; break; }
           DCN_TS(512 + 2 * kidx);
           tc_fence_after();
