@@ -182,6 +182,11 @@ int make_plan(const dcn_desc* d, Plan* p, int num_sms) {
   p->off_gw = off; off = align_up(off + (size_t)d->Co * p->K2 * p->CS * 4, kWsAlign);
   p->off_gb = off; off = align_up(off + (size_t)d->Co * 4, kWsAlign);
   p->bwd_bytes = off;
+  p->fd_howo = make_fastdiv((uint32_t)p->HoWo);
+  p->fd_wo = make_fastdiv((uint32_t)p->Wo);
+  p->fd_kw = make_fastdiv((uint32_t)p->kw);
+  p->fd_dg = make_fastdiv((uint32_t)p->dg);
+  p->fd_ntg = make_fastdiv((uint32_t)(p->K2 * p->dg));
   return DCN_OK;
 }
 

@@ -70,13 +70,13 @@ __global__ void __launch_bounds__(kThreads, 3) dcn_bwd_scatter_kernel(const __gr
   const int nwarps = (int)((gridDim.x * kThreads) >> 5);
 
   for (int item = warp0; item < nitems; item += nwarps) {
-    const int grp = item / nTG;
+    const int grp = fdiv(item, P.fd_ntg);
     const int tg = item - grp * nTG;
-    const int t = tg / P.dg, g = tg - t * P.dg;
+    const int t = fdiv(tg, P.fd_dg), g = tg - t * P.dg;
     // ---- geometry of pixel (group base + lane), computed once per lane
     const int mpix = a.pix0 + grp * 32 + lane;
     const bool mpv = mpix < pend;
-    const int mb = mpv ? mpix / HoWo : 0;
+    const int mb = mpv ? fdiv(mpix, P.fd_howo) : 0;
     const int mp = mpv ? mpix - mb * HoWo : 0;
     const int obase = ((mb * P.dg + g) * 2 * P.K2 + 2 * t) * HoWo + mp;
     const int mbase = ((mb * P.dg + g) * P.K2 + t) * HoWo + mp;
@@ -84,8 +84,8 @@ __global__ void __launch_bounds__(kThreads, 3) dcn_bwd_scatter_kernel(const __gr
     int mgidx = 0;
     uint32_t mval = 0u;
     if (mpv) {
-      const int i = t / P.kw, j = t - i * P.kw;
-      const int ho = mp / P.Wo, wo = mp - ho * P.Wo;
+      const int i = fdiv(t, P.fd_kw), j = t - i * P.kw;
+      const int ho = fdiv(mp, P.fd_wo), wo = mp - ho * P.Wo;
       const float h = (float)(ho * P.sh - P.ph + i * P.dh) + ldf(off + obase);
       const float w = (float)(wo * P.sw - P.pw + j * P.dw) + ldf(off + obase + HoWo);
       mm = ldf(msk + mbase);
@@ -122,7 +122,8 @@ __global__ void __launch_bounds__(kThreads, 3) dcn_bwd_scatter_kernel(const __gr
       uint8_t* cdst = a.cols == nullptr ? nullptr
                       : a.cols + ((size_t)(unsigned)(pl >> 6) * P.nsplit * natoms) * 8192u +
                             crow * 128 + ((q ^ (crow & 7)) << 4);
-      for (int cb = 0; cb < P.nCB; ++cb) {
+      int cch = 0, cblk = 0;                       // channel chunk of the unit, 64-block inside it
+      for (int cb = 0; cb < P.nCB; ++cb, (++cblk == nblk ? (cblk = 0, ++cch) : 0)) {
         float col[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         if (cval != 0u) {
           const int cofs = g * P.Cgp + cb * kChunk;
@@ -174,8 +175,7 @@ __global__ void __launch_bounds__(kThreads, 3) dcn_bwd_scatter_kernel(const __gr
         }
         if (cdst != nullptr) {
           // column block of (unit tg * nCC + channel chunk, 64-channel block inside it)
-          const int c64 = cb * kChunk;
-          const int atom = (tg * P.nCC + c64 / P.NC) * nblk + (c64 % P.NC) / kChunk;
+          const int atom = (tg * P.nCC + cch) * nblk + cblk;
           uint8_t* dst = cdst + (size_t)atom * 8192u;
           if constexpr (OpOf<T>::kSplit) {
             uint4 hi, lo;

@@ -11,12 +11,18 @@
 #include <stdint.h>
 
 #include "dcn_b200.h"
+#include "dcn_plan.h"
 
 #ifndef DCN_WAIT_TIMEOUT_NS
 #define DCN_WAIT_TIMEOUT_NS 4000000000ull  // 4 s: far above any legitimate wait
 #endif
 
 namespace dcn {
+
+// n / f.d for 0 <= n < 2^31 (see FastDiv)
+__device__ __forceinline__ int fdiv(int n, const FastDiv& f) {
+  return f.d == 1 ? n : (int)(__umulhi((uint32_t)n, f.m) >> f.sh);
+}
 
 // ---------------------------------------------------------------- basics
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

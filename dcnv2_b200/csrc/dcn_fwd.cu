@@ -120,8 +120,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const int row = gt & (kTileM - 1), slot0 = gt >> 7;
     const int pix = pt * kTileM + row;
     const bool pv = pix < P.totalP && !(a.dbg & 1);
-    const int b = pv ? pix / HoWo : 0, p = pv ? pix - b * HoWo : 0;
-    const int ho = p / P.Wo, wo = p - ho * P.Wo;
+    const int b = pv ? fdiv(pix, P.fd_howo) : 0, p = pv ? pix - b * HoWo : 0;
+    const int ho = fdiv(p, P.fd_wo), wo = p - ho * P.Wo;
     uint32_t rh[KI], rw[KI], rm[KI];
 #pragma unroll
     for (int k = 0; k < KI; ++k) {
@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       rh[k] = rw[k] = rm[k] = 0u;
       if (pv && slot < wt) {
         const int tgi = tg0 + slot;
-        const int t = tgi / P.dg, gi = tgi - t * P.dg;
+        const int t = fdiv(tgi, P.fd_dg), gi = tgi - t * P.dg;
         const int ob = ((b * P.dg + gi) * 2 * P.K2 + 2 * t) * HoWo + p;
         rh[k] = ldg_raw<T>(off + ob);
         rw[k] = ldg_raw<T>(off + ob + HoWo);
@@ -142,8 +142,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       if (slot < wt) {
         PixGeo r = zero_pixgeo();
         if (pv) {
-          const int t = (tg0 + slot) / P.dg;
-          const int i = t / P.kw, j = t - i * P.kw;
+          const int t = fdiv(tg0 + slot, P.fd_dg);
+          const int i = fdiv(t, P.fd_kw), j = t - i * P.kw;
           const float hs = (float)(ho * P.sh - P.ph + i * P.dh) + raw_to_f<T>(rh[k]);
           const float ws = (float)(wo * P.sw - P.pw + j * P.dw) + raw_to_f<T>(rw[k]);
           r = make_pixgeo(b * HW, hs, ws, raw_to_f<T>(rm[k]), P.H, P.W);

@@ -12,6 +12,24 @@ constexpr int kChunk = 64;    // 16-bit elements per 128-byte swizzle row (one K
 constexpr size_t kWsAlign = 256;
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Division by a run-time constant d >= 1 for numerators 0 <= n < 2^31 with one
+// multiply-high and a shift: m = ceil(2^(31+s) / d), s = ceil(log2 d), then
+// n / d = umulhi(n, m) >> (s - 1).  Exact: with m = (2^(31+s) + e) / d,
+// 0 <= e < d, the error term n e / (d 2^(31+s)) stays below 2^-s <= 1/d.
+struct FastDiv {
+  uint32_t d, m, sh;
+};
+
+inline FastDiv make_fastdiv(uint32_t d) {
+  FastDiv f;
+  f.d = d ? d : 1;
+  uint32_t s = 0;
+  while ((1ull << s) < f.d) ++s;
+  f.m = f.d == 1 ? 0u : (uint32_t)(((1ull << (31 + s)) + f.d - 1) / f.d);
+  f.sh = s ? s - 1 : 0;
+  return f;
+}
 inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
 
 struct Plan {
@@ -48,6 +66,8 @@ struct Plan {
   size_t fwd_bytes, bwd_bytes;
   size_t wf_tile_bytes;   // one forward weight tile (NT rows x 128 B x nsplit)
   size_t wd_tile_bytes;   // one backward-data weight tile (gNC rows x 128 B x nsplit)
+  // divisors of the index arithmetic in the kernels
+  FastDiv fd_howo, fd_wo, fd_kw, fd_dg, fd_ntg;
 };
 
 // Fills `p` from `d`; returns DCN_OK or DCN_E_INVALID / DCN_E_UNSUPPORTED.
