@@ -27,8 +27,14 @@ import time
 
 import numpy as np
 
-# NCCL prints its version on stdout by default; the bench's stdout is one JSON line
+# The bench's stdout is one JSON line.  Whatever the libraries print (NCCL's
+# version banner, warnings) goes to stderr: file descriptor 1 is pointed at
+# stderr and the JSON line is written to a duplicate of the original stdout.
 os.environ.setdefault("NCCL_DEBUG", "WARN")
+os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+sys.stdout.flush()
+_JSON_OUT = os.fdopen(os.dup(1), "w")
+os.dup2(2, 1)
 import torch  # noqa: E402
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -143,9 +149,18 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def host_threads():
+    """Host threads this process may use (torchrun sets OMP_NUM_THREADS=1 for its workers)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
 def cpu_port_step(wl, B_sample):
     """One forward+backward of the C port of the reference path (float32, OpenMP)."""
     import oracle
+    oracle.set_threads(host_threads())
     x, w, b, off, m, gy = [t.numpy() for t in make_inputs(wl, None, None, 0)]
     _, C, H, W, Co, k, s, p, d, dg, _ = wl
     sl = slice(0, B_sample)
@@ -201,7 +216,7 @@ def run_reference(args, wl, rank):
         "e2e": {"value": val, "unit": "TFLOP/s (README formula, fwd+bwd)",
                 "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    print(json.dumps(line), file=_JSON_OUT, flush=True)
 
 
 def config_of(args, wl):
@@ -376,7 +391,7 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(wl)
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        print(json.dumps(line), file=_JSON_OUT, flush=True)
     if world > 1:
         dist.destroy_process_group()
 

@@ -49,12 +49,19 @@ def _load():
         g.argtypes = [p, p, p, p, p, p, p, p, p, p, ip]
         g.restype = None
     lib.dcn_oracle_num_threads.restype = ctypes.c_int
+    lib.dcn_oracle_set_threads.argtypes = [ctypes.c_int]
+    lib.dcn_oracle_set_threads.restype = None
     _lib = lib
     return lib
 
 
 def num_threads() -> int:
     return int(_load().dcn_oracle_num_threads())
+
+
+def set_threads(n: int) -> None:
+    """Threads of the float32 CPU port (OpenMP)."""
+    _load().dcn_oracle_set_threads(int(n))
 
 
 def out_size(n: int, k: int, s: int, p: int, d: int) -> int:

@@ -56,6 +56,15 @@ int dcn_oracle_num_threads(void) {
 #endif
 }
 
+/* threads of the CPU legs of the benchmark (a launcher may have set OMP_NUM_THREADS=1) */
+void dcn_oracle_set_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
 #define DCN_ORACLE_DEFINE(T, SFX)                                                              \
 /* bilinear value at (h, w) of one HxW plane; corners outside are 0 (com.cu:119-148) */       \
 static T bilinear_##SFX(const T *im, int H, int W, T h, T w) {                                 \
