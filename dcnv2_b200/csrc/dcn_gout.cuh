@@ -18,7 +18,7 @@ __device__ __forceinline__ void load8_gout(const T* __restrict__ gout, const Pla
     return;
   }
   if (vec) {
-    const int b = (int)(pix0 / P.HoWo);
+    const int b = fdiv(pix0, P.fd_howo);
     const int p = (int)(pix0 - b * P.HoWo);
     const T* src = gout + ((size_t)b * P.Co + co) * P.HoWo + p;
     if constexpr (std::is_same<T, float>::value) {
@@ -36,7 +36,7 @@ __device__ __forceinline__ void load8_gout(const T* __restrict__ gout, const Pla
       const int pix = pix0 + e;
       v[e] = 0.f;
       if (pix < P.totalP) {
-        const int b = (int)(pix / P.HoWo);
+        const int b = fdiv(pix, P.fd_howo);
         const int p = (int)(pix - b * P.HoWo);
         v[e] = ldf(gout + ((size_t)b * P.Co + co) * P.HoWo + p);
       }
@@ -68,7 +68,7 @@ __device__ __forceinline__ void gout_raw_load(const T* __restrict__ gout, const 
     for (int k = 0; k < (int)(sizeof(T) / 2); ++k) g.r[k] = make_uint4(0u, 0u, 0u, 0u);
     return;
   }
-  const int b = (int)(pix0 / P.HoWo);
+  const int b = fdiv(pix0, P.fd_howo);
   const int p = (int)(pix0 - b * P.HoWo);
   const T* src = gout + ((size_t)b * P.Co + co) * P.HoWo + p;
 #pragma unroll

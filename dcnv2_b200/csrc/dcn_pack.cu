@@ -320,6 +320,54 @@ __global__ void finish_grad_weight_kernel(const float* __restrict__ gw, const fl
   }
 }
 
+// ---------------------------------------------------------------------------
+// Register-transpose input pack for 16-bit tensors (H*W % 8 == 0, 16-byte
+// aligned): a thread moves an 8 x 8 block (eight 16-byte loads, 32 byte
+// permutes, eight 16-byte stores) without shared memory.
+
+// word k of pixel e of an 8 x 8 16-bit block whose rows 2k, 2k+1 are ra, rb
+__device__ __forceinline__ uint32_t tr_word(const uint4& ra, const uint4& rb, int e) {
+  const uint32_t wa = e < 2 ? ra.x : e < 4 ? ra.y : e < 6 ? ra.z : ra.w;
+  const uint32_t wb = e < 2 ? rb.x : e < 4 ? rb.y : e < 6 ? rb.z : rb.w;
+  return __byte_perm(wa, wb, (e & 1) ? 0x7632 : 0x5410);
+}
+
+__device__ __forceinline__ void transpose8x8_b16(const uint4 (&row)[8], uint4 (&col)[8]) {
+#pragma unroll
+  for (int e = 0; e < 8; ++e)
+    col[e] = make_uint4(tr_word(row[0], row[1], e), tr_word(row[2], row[3], e), tr_word(row[4], row[5], e),
+                        tr_word(row[6], row[7], e));
+}
+
+// x [B][C][HW] -> xt [B][HW][dg][Cgp] (perm_logical order).  Thread: 16-byte
+// chunk q of a 64-channel block and 8 pixels; q varies fastest so that the
+// eight chunks of a pixel's 128-byte line are stored by one warp instruction.
+template <typename T>
+__global__ void __launch_bounds__(256) pack_input_rt_kernel(const T* __restrict__ x, T* __restrict__ xt,
+                                                            int C, int HW, int Cg, int Cgp, int CS,
+                                                            long long nthr) {
+  const int np8 = HW >> 3, nblk = CS >> 6;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < nthr;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int q = (int)(idx & 7);
+    const long long r1 = idx >> 3;
+    const int p8 = (int)(r1 % np8);
+    const long long r2 = r1 / np8;
+    const int blk = (int)(r2 % nblk), b = (int)(r2 / nblk);
+    const int d0 = blk * 64, g = d0 / Cgp, cb = d0 - g * Cgp;
+    uint4 row[8], col[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const int cc = cb + (r < 4 ? 4 * q + r : 32 + 4 * q + r - 4);   // logical channel of position 8q + r
+      row[r] = cc < Cg ? ldg_nc_v4(x + ((size_t)b * C + g * Cg + cc) * HW + p8 * 8) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    transpose8x8_b16(row, col);
+    T* o = xt + ((size_t)b * HW + p8 * 8) * CS + d0 + q * 8;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) *reinterpret_cast<uint4*>(o + (size_t)e * CS) = col[e];
+  }
+}
+
 template <typename F>
 int dispatch(int dtype, F&& f) {
   switch (dtype) {
@@ -345,6 +393,15 @@ int launch_pack_input(const Plan& P, const void* x, void* xt, cudaStream_t s) {
   const long long nblocks = (long long)npb * ncb * P.B;
   if (nblocks >= (1LL << 31)) return DCN_E_UNSUPPORTED;
   const int grid = (int)(nblocks < 148LL * 8 ? nblocks : 148LL * 8);
+  if (vec && P.esz == 2) {
+    const long long nthr = (long long)P.B * (HW / 8) * (P.CS / 64) * 8;
+    return dispatch(P.dtype, [&](auto tag) {
+      using T = decltype(tag);
+      if constexpr (sizeof(T) == 2)
+        pack_input_rt_kernel<T><<<grid_for(nthr, 256), 256, 0, s>>>(static_cast<const T*>(x), static_cast<T*>(xt),
+                                                                     P.C, HW, P.Cg, P.Cgp, P.CS, nthr);
+    });
+  }
   return dispatch(P.dtype, [&](auto tag) {
     using T = decltype(tag);
     pack_input_kernel<T><<<grid, 256, 0, s>>>(static_cast<const T*>(x), static_cast<T*>(xt), P.C,
