@@ -45,6 +45,13 @@ WORKLOADS = {
     "readme": (8, 64, 128, 128, 256, 3, 1, 1, 1, 1, 1.5),
     # the README layer at batch 2: the small case for ncu captures
     "readme_b2": (2, 64, 128, 128, 256, 3, 1, 1, 1, 1, 1.5),
+    # the other layer shapes of the benchmark configurations (run with --dtype
+    # of the configuration: fp16 for the ResNet-50 stages, bf16 for c512_dg4)
+    "resnet_s1": (16, 128, 64, 64, 128, 3, 1, 1, 1, 1, 1.5),
+    "resnet_s2": (16, 256, 32, 32, 256, 3, 1, 1, 1, 1, 1.5),
+    "resnet_s3": (16, 512, 16, 16, 512, 3, 1, 1, 1, 1, 1.5),
+    "c512_dg4": (32, 512, 32, 32, 512, 3, 1, 1, 1, 4, 2.0),
+    "edge_k5": (4, 96, 97, 131, 160, 5, 2, 4, 2, 2, 8.0),
 }
 DTYPES = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}

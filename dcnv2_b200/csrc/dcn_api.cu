@@ -127,6 +127,7 @@ int make_plan(const dcn_desc* d, Plan* p, int num_sms) {
   p->nCoT = ceil_div(d->Co, 256);
   p->NT = ceil_div(ceil_div(d->Co, p->nCoT), 16) * 16;
   p->nPT = (int)((p->totalP + kTileM - 1) / kTileM);
+
   // backward data
   p->Cop = ceil_div(d->Co, kChunk) * kChunk;
   p->nKo = p->Cop / kChunk;
@@ -213,12 +214,12 @@ int dcn_output_size(const dcn_desc* d, int32_t* Ho, int32_t* Wo) {
 
 size_t dcn_forward_workspace_size(const dcn_desc* d) {
   Plan p;
-  return make_plan(d, &p, 148) == DCN_OK ? p.fwd_bytes : 0;
+  return make_plan(d, &p, device_sms()) == DCN_OK ? p.fwd_bytes : 0;
 }
 
 size_t dcn_backward_workspace_size(const dcn_desc* d) {
   Plan p;
-  return make_plan(d, &p, 148) == DCN_OK ? p.bwd_bytes : 0;
+  return make_plan(d, &p, device_sms()) == DCN_OK ? p.bwd_bytes : 0;
 }
 
 int dcn_forward(const dcn_desc* d, const void* input, const void* weight, const void* mask,

@@ -429,7 +429,7 @@ int launch_forward(const FwdArgs& a, cudaStream_t stream) {
   // a tile fits one window and two stages still fit, else one built by the producers
   const size_t geoWin = (size_t)kGeoTaps * kTileM * (sizeof(float4) + sizeof(int));
   const size_t biasBytes = (size_t)P.nCoT * P.NT * sizeof(float);
-  int NB = (P.K2 * P.dg <= kGeoTaps && P.nCoT == 1) ? 2 : 1;
+  int NB = P.K2 * P.dg <= kGeoTaps ? 2 : 1;
   if (NB == 2 && (kFwdSmemBudget - 1024 - 2 * geoWin - biasBytes) / stageBytes < 2) NB = 1;
   const size_t geoBytes = NB * geoWin + biasBytes;
   int S = (int)((kFwdSmemBudget - 1024 - geoBytes) / stageBytes);
