@@ -35,6 +35,16 @@ namespace {
 
 constexpr int kThreads = 256;
 
+// {a.x * b.x + c.x, a.y * b.y + c.y} (sm_100 packed f32x2)
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  unsigned long long r;
+  asm("{\n\t.reg .b64 x, y, z;\n\tmov.b64 x, {%1, %2};\n\tmov.b64 y, {%3, %4};\n\t"
+      "mov.b64 z, {%5, %6};\n\tfma.rn.f32x2 %0, x, y, z;\n\t}"
+      : "=l"(r)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return make_float2(__uint_as_float((uint32_t)r), __uint_as_float((uint32_t)(r >> 32)));
+}
+
 // 2 x f32 packed multiply (sm_100): {a.x * s, a.y * s}
 __device__ __forceinline__ float2 mul2(float2 a, float s) {
   unsigned long long r;
@@ -151,11 +161,16 @@ __global__ void __launch_bounds__(kThreads, 3) dcn_bwd_scatter_kernel(const __gr
           for (int c = 0; c < 4; ++c) {
             float v[8];
             unpack_slice<T>(raw[c], v);
+            float2 sp = make_float2(0.f, 0.f);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              S[c] = fmaf(gc[e], v[e], S[c]);
-              col[e] = fmaf(wc[c], v[e], col[e]);
+            for (int e = 0; e < 8; e += 2) {
+              const float2 ve = make_float2(v[e], v[e + 1]);
+              sp = fma2(make_float2(gc[e], gc[e + 1]), ve, sp);
+              const float2 ce = fma2(ve, make_float2(wc[c], wc[c]), make_float2(col[e], col[e + 1]));
+              col[e] = ce.x;
+              col[e + 1] = ce.y;
             }
+            S[c] += sp.x + sp.y;
           }
           if (!(a.dbg & 2)) {
 #pragma unroll
