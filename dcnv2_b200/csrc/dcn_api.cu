@@ -1,5 +1,6 @@
 // C ABI of libdcn_b200 (declared in include/dcn_b200.h): problem planning,
 // workspace layout and the launch sequences of forward and backward.
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -33,6 +34,33 @@ long long gcol_budget_mb() {
     return e ? atoll(e) : 1024LL;
   }();
   return v;
+}
+
+// Study switch: DCN_GOUT_PACKED=1 keeps the packed grad_output copy even where
+// the GEMMs could read grad_output directly.
+bool gout_packed_forced() {
+  static bool v = [] {
+    const char* e = getenv("DCN_GOUT_PACKED");
+    return e != nullptr && atoi(e) != 0;
+  }();
+  return v;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// The driver's tensor-map encoder, looked up once through the runtime.
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return (EncodeTiledFn) nullptr;
+    return reinterpret_cast<EncodeTiledFn>(f);
+  }();
+  return fn;
 }
 
 int device_sms() {
@@ -87,6 +115,25 @@ void plan_weight_grad(Plan* p, int num_sms) {
 }
 
 }  // namespace
+
+bool make_gout_tmap(const Plan& P, const void* gout, TmaDesc* out) {
+  static_assert(sizeof(CUtensorMap) == sizeof(TmaDesc), "tensor map size");
+  EncodeTiledFn fn = encode_tiled();
+  if (!fn || !gout || P.esz != 2 || (P.HoWo % 64) != 0) return false;
+  const cuuint64_t dims[3] = {(cuuint64_t)P.HoWo, (cuuint64_t)P.Co, (cuuint64_t)P.B};
+  const cuuint64_t strides[2] = {(cuuint64_t)P.HoWo * 2u, (cuuint64_t)P.Co * P.HoWo * 2u};
+  const cuuint32_t box[3] = {64u, 64u, 1u};
+  const cuuint32_t estr[3] = {1u, 1u, 1u};
+  const CUtensorMapDataType dt =
+      P.dtype == DCN_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUtensorMap m;
+  const CUresult r = fn(&m, dt, 3, const_cast<void*>(gout), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return false;
+  memcpy(out, &m, sizeof(m));
+  return true;
+}
 
 int make_plan(const dcn_desc* d, Plan* p, int num_sms) {
   if (d == nullptr || p == nullptr) return DCN_E_NULLPTR;
@@ -320,15 +367,20 @@ int dcn_backward(const dcn_desc* d, const void* input, const void* weight, const
     TraceScope ts(TR_PACK_WEIGHT_BWD, s);
     if ((rc = launch_pack_weight_bwd(P, weight, ws + P.off_wd, s)) != DCN_OK) return rc;
   }
-  {
+  // 16-bit grad_output whose 64-pixel blocks never straddle two images is read
+  // by the GEMMs directly (TMA tiles of 64 pixels x 64 Co); otherwise it is
+  // packed into swizzled blocks first (and f32 is split into bf16 hi/lo).
+  BwdDataArgs a;
+  memset(&a, 0, sizeof(a));
+  a.gdirect = P.esz == 2 && aligned16(grad_output) && !gout_packed_forced() &&
+              make_gout_tmap(P, grad_output, &a.gmap);
+  if (!a.gdirect) {
     TraceScope ts(TR_PACK_GRAD_OUTPUT, s);
     const int vec = aligned16(grad_output) && (P.HoWo % 8 == 0);
     if ((rc = launch_pack_gout(P, grad_output, ws + P.off_go, d->has_bias ? gb : nullptr, vec, s)) !=
         DCN_OK)
       return rc;
   }
-  BwdDataArgs a;
-  memset(&a, 0, sizeof(a));
   a.plan = P;
   a.xt = ws + P.off_x;
   a.offset = offset;
@@ -354,6 +406,9 @@ int dcn_backward(const dcn_desc* d, const void* input, const void* weight, const
   BwdWeightArgs w;
   memset(&w, 0, sizeof(w));
   w.plan = P;
+  w.gmap = a.gmap;
+  w.gdirect = a.gdirect;
+  w.gb = (a.gdirect && d->has_bias) ? gb : nullptr;
   w.cols = a.cols;
   w.gpk = ws + P.off_go;
   w.gw = gw;

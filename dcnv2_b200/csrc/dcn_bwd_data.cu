@@ -15,8 +15,10 @@
 // time, so the grad_out reads of the other units hit L2.
 //
 // CTA roles (512 threads):
-//   warp 0      bulk copies of pre-packed grad_out chunks (128 pixels x 64 Co,
-//               K-major SW128) into the A ring (warps 1-3 idle)
+//   warp 0      copies of grad_out chunks (128 pixels x 64 Co, SW128) into the
+//               A ring (warps 1-3 idle): TMA tiles read from grad_output itself
+//               (16-bit types; MN-major) or bulk copies of pre-packed blocks
+//               (K-major; f32 as bf16 hi/lo)
 //   warps 4-11  epilogue: TMEM -> registers -> shared-memory transpose -> global
 //               stores of whole 64- or 128-byte row segments
 //   warp 12     bulk copies of the unit's pre-packed W^T tiles (K-major SW128)
@@ -208,6 +210,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t ph = 0;
         bool ok = true;
         const uint32_t blk = NS * 8192u;
+        const bool gdirect = NS == 1 && a.gdirect;
+        const int nPBi = P.HoWo / 64;              // 64-pixel blocks per image (gdirect)
         for (int tile = r0; tile < nTiles && ok; tile += cpu) {
           for (int ko = 0; ko < P.nKo; ++ko, (++r == RA ? (r = 0, ph ^= 1u) : 0u)) {
             if (!mbar_wait(aempty0 + 8 * r, ph ^ 1u, a.err, &abort_flag)) { ok = false; break; }
@@ -216,9 +220,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int nb = (pb0 + 1 < P.nPB) ? 2 : 1;
             mbar_arrive_expect_tx(afull0 + 8 * r, (uint32_t)nb * blk);
             for (int h = 0; h < nb; ++h) {
-              const uint8_t* src = a.gpk + ((size_t)(pb0 + h) * P.nKo + ko) * blk;
-              bulk_g2s(at + h * 8192u, src, 8192u, afull0 + 8 * r);
-              if constexpr (NS == 2) bulk_g2s(at + kATile + h * 8192u, src + 8192, 8192u, afull0 + 8 * r);
+              if (gdirect) {
+                // 64 pixels x 64 Co straight from grad_output (one image: HoWo % 64 == 0);
+                // pixels contiguous, so the tile is MN-major; Co past the end reads zeros
+                const int pbi = pb0 + h, b = pbi / nPBi;
+                tma_load_3d(at + h * 8192u, &a.gmap, (pbi - b * nPBi) * 64, ko * 64, b, afull0 + 8 * r);
+              } else {
+                const uint8_t* src = a.gpk + ((size_t)(pb0 + h) * P.nKo + ko) * blk;
+                bulk_g2s(at + h * 8192u, src, 8192u, afull0 + 8 * r);
+                if constexpr (NS == 2) bulk_g2s(at + kATile + h * 8192u, src + 8192, 8192u, afull0 + 8 * r);
+              }
             }
           }
         }
@@ -247,7 +258,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == kMmaWarp) {
       // ---------------------------------------------- MMA issuer
       if (lane == 0) {
-        const uint32_t idesc = make_idesc(OpOf<T>::kBF16, 0, 0, kTileM, NC);
+        // A: packed grad_out chunks are K-major (Co contiguous per pixel row);
+        // tiles read from grad_output directly are MN-major (pixels contiguous
+        // per Co row, the two 64-pixel halves 8 KB apart)
+        const bool gdirect = NS == 1 && a.gdirect;
+        const uint32_t idesc = make_idesc(OpOf<T>::kBF16, gdirect ? 1 : 0, 0, kTileM, NC);
         uint32_t it = 0;
         int ar = 0, ms = 0;                         // A slot / W^T stage and their phases
         uint32_t aph = 0, mph = 0;
@@ -272,7 +287,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t bt = sbase + s * stageBytes;
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t ad = sw128_desc(at + kk * 32, 16, 1024);
+              const uint64_t ad = gdirect ? sw128_desc(at + kk * 2048, 8192, 1024)
+                                          : sw128_desc(at + kk * 32, 16, 1024);
               const uint64_t bd = sw128_desc(bt + kk * 32, 16, 1024);
               if (!(a.dbg & 4)) umma_f16(dt, ad, bd, idesc, (ko | kk) != 0);
               if constexpr (NS == 2) {

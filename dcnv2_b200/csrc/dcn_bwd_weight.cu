@@ -8,13 +8,17 @@
 //       units, K = pixels (64 per pipeline stage); all of a CTA's Co tiles and
 //       units are kept in TMEM at once.
 //
-// Both operands arrive pre-packed as MN-major SW128 blocks of 64 pixels: the
-// grad_out blocks from pack_gout_kernel and the sampled columns from the
-// backward scatter kernel, which already holds every bilinear corner.  The
+// The B operand (sampled columns) arrives as MN-major SW128 blocks of 64 pixels
+// written by the backward scatter kernel, which already holds every bilinear
+// corner.  The A operand is read from grad_output itself by TMA for 16-bit
+// types (64 pixels x 64 Co boxes, K-major) or arrives as MN-major blocks
+// pre-packed by pack_gout_kernel (f32 as bf16 hi/lo, and shapes whose 64-pixel
+// blocks straddle images).  The
 // kernel is therefore a plain streaming GEMM: one thread bulk-copies both
 // operands into a ring of stages, one thread issues the MMAs, and at the end
 // four warps add the fp32 partial sums into a zeroed fp32 buffer with vector
-// red.add (the pixel reduction is split over CTAs).  grad_bias is summed while
+// red.add (the pixel reduction is split over CTAs).  grad_bias is summed by the
+// epilogue warps from the A tiles while the GEMM runs (direct reads), else while
 // grad_output is packed.
 //
 // CTA roles (192 threads):
@@ -65,6 +69,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int ucount = min(ups, P.nU - u0);
   if (kl1 <= kl0 || mcount <= 0 || ucount <= 0) return;  // uniform for the CTA
   const int ntot = ucount * NC;
+  // grad_output read directly (16-bit): A tiles are K-major (pixels contiguous
+  // per Co row), and the CTAs of unit set 0 also sum grad_bias from them
+  const bool gdirect = NS == 1 && a.gdirect;
+  const bool bias = gdirect && a.gb != nullptr && set == 0;
 
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bars[2 * kMaxStages + 2];
@@ -81,7 +89,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(full0 + 8 * s, 1);
-      mbar_init(empty0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, bias ? 1 + 4 : 1);  // MMA commit (+ the 4 bias-summing warps)
     }
     mbar_init(accf, 1);
     mbar_init(drain, 1);
@@ -104,6 +112,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // the chunk's column buffer and form the B tile in one copy (per hi/lo).
     if (lane == 0) {
       const uint32_t blk = NS * 8192u;
+      const int nPBi = P.HoWo / 64;               // 64-pixel blocks per image (gdirect)
       int ls = 0;                                   // ring stage and its phase
       uint32_t lph = 0;
       for (int kl = kl0; kl < kl1; ++kl) {
@@ -122,10 +131,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (2 * (mt0 + m) + h < P.nKo) bytes += blk;
         mbar_arrive_expect_tx(full0 + 8 * s, bytes);
         const int ks = a.ks0 + kl;
+        const int kb = gdirect ? ks / nPBi : 0;
         for (int m = 0; m < mcount; ++m) {
           for (int h = 0; h < 2; ++h) {
             const int ko = 2 * (mt0 + m) + h;
             if (ko >= P.nKo) continue;
+            if (gdirect) {
+              // Co rows ko*64 .. +63 of 64-pixel block ks (Co past the end reads zeros)
+              tma_load_3d(at + m * kATile + h * 8192u, &a.gmap, (ks - kb * nPBi) * 64, ko * 64, kb,
+                          full0 + 8 * s);
+              continue;
+            }
             const uint8_t* src = a.gpk + ((size_t)ks * P.nKo + ko) * blk;
             bulk_g2s(at + m * kATile + h * 8192u, src, 8192u, full0 + 8 * s);
             if constexpr (NS == 2)
@@ -156,11 +172,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int m = 0; m < mcount; ++m) {
           for (int n0 = 0; n0 < ntot; n0 += 256) {
             const int N = min(256, ntot - n0);
-            const uint32_t idesc = make_idesc(OpOf<T>::kBF16, 1, 1, kTileM, N);
+            const uint32_t idesc = make_idesc(OpOf<T>::kBF16, gdirect ? 0 : 1, 1, kTileM, N);
             const uint32_t dt = tmem_base + (uint32_t)(m * ups * NC + n0);
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t ad = sw128_desc(at + m * kATile + kk * 2048, 8192, 1024);
+              const uint64_t ad = gdirect ? sw128_desc(at + m * kATile + kk * 32, 16, 1024)
+                                          : sw128_desc(at + m * kATile + kk * 2048, 8192, 1024);
               const uint64_t bd = sw128_desc(bt + (uint32_t)(n0 >> 6) * 8192u + kk * 2048, 8192, 1024);
               if (!(a.dbg & 4)) umma_f16(dt, ad, bd, idesc, (kl > kl0 || kk > 0) ? 1u : 0u);
               if constexpr (NS == 2) {
@@ -181,6 +198,45 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait_drain(drain, 0, a.err);
     }
   } else {
+    if (bias) {
+      // ---------------------------------------------- grad_bias from the A tiles
+      // Thread tid owns Co row tid of every M tile: per stage it adds the 64
+      // pixels of its 128-byte row (chunk order is irrelevant to the sum; lane
+      // i starts at chunk i % 8 so that eight rows hit eight bank groups).
+      float bsum[kMaxMT];
+#pragma unroll
+      for (int m = 0; m < kMaxMT; ++m) bsum[m] = 0.f;
+      int bs = 0;
+      uint32_t bph = 0;
+      bool ok = true;
+      for (int kl = kl0; kl < kl1; ++kl) {
+        const int s = bs;
+        const uint32_t ph = bph;
+        if (++bs == S) { bs = 0; bph ^= 1u; }
+        if (!mbar_wait(full0 + 8 * s, ph, a.err, &abort_flag)) { ok = false; break; }
+        const uint32_t at = sbase + s * stageBytes;
+#pragma unroll
+        for (int m = 0; m < kMaxMT; ++m) {
+          if (m < mcount) {
+            float acc = 0.f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const uint4 w = lds_v4(at + m * kATile + tid * 128u + (uint32_t)(((j + tid) & 7) << 4));
+              acc += sum8<T>(w);
+            }
+            bsum[m] += acc;
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty0 + 8 * s);
+      }
+      if (ok) {
+        for (int m = 0; m < mcount; ++m) {
+          const int co = (mt0 + m) * 128 + tid;
+          if (co < P.Co) atomicAdd(a.gb + co, bsum[m]);
+        }
+      }
+    }
     // ------------------------------------------------ epilogue: TMEM -> fp32 red.add
     if (mbar_wait(accf, 0, a.err, &abort_flag)) {
       if (warp == 0) DCN_TS(1001);

@@ -121,6 +121,19 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
       : "memory");
 }
 
+// 3-D tiled TMA load of a box (no multicast) into this CTA's shared memory,
+// completion as tx bytes on an mbarrier.  Coordinates are element indices,
+// innermost first; the innermost one times the element size must be a multiple
+// of 16 bytes.  Out-of-range elements of the box are filled with zeros.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int c0, int c1, int c2,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+          dst),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
+      : "memory");
+}
+
 // Warpgroup register re-allocation: every warp of a warpgroup executes the same
 // call; the block's register file (launch registers x threads) is redistributed.
 template <uint32_t N>
@@ -389,6 +402,22 @@ __device__ __forceinline__ uint4 lds_v4(uint32_t addr) {
                : "r"(addr)
                : "memory");
   return v;
+}
+
+// Sum of the elements held in 16 bytes (eight 16-bit values, or four f32), in fp32.
+template <typename T>
+__device__ __forceinline__ float sum8(const uint4& w) {
+  const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if constexpr (std::is_same<T, float>::value) {
+      s += __uint_as_float(u[i]);
+    } else {
+      s += raw_to_f<T>(u[i] & 0xffffu) + raw_to_f<T>(u[i] >> 16);
+    }
+  }
+  return s;
 }
 
 // Vector fp32 reduction into global memory (sm_90+).

@@ -12,6 +12,11 @@ constexpr size_t kFwdSmemBudget = 218 * 1024;  // dynamic smem of the forward ke
 constexpr size_t kBwdSmemBudget = 200 * 1024;
 constexpr size_t kBwdSmemLimit = 226 * 1024;  // backward-data ring + transpose buffer
 
+// Opaque 128-byte TMA tensor map (CUtensorMap), passed by value in kernel arguments.
+struct alignas(64) TmaDesc {
+  unsigned long long v[16];
+};
+
 struct FwdArgs {
   Plan plan;
   unsigned long long* ts;  // optional pipeline timestamps of CTA 0 (DCN_DEBUG_TS), else null
@@ -30,6 +35,9 @@ struct FwdArgs {
 };
 
 struct BwdDataArgs {
+  TmaDesc gmap;         // grad_output as [B][Co][HoWo], box 64 pixels x 64 Co, SW128 (gdirect)
+  int gdirect;          // A tiles loaded from grad_output by TMA (no packed copy); 16-bit types,
+                        // HoWo % 64 == 0, 16-byte aligned grad_output
   Plan plan;
   unsigned long long* ts;  // optional pipeline timestamps of CTA 0 (DCN_DEBUG_TS), else null
   const void* xt;       // packed NHWC input
@@ -55,6 +63,9 @@ struct BwdDataArgs {
 };
 
 struct BwdWeightArgs {
+  TmaDesc gmap;         // as BwdDataArgs::gmap
+  int gdirect;          // A tiles from grad_output by TMA; grad_bias then summed here
+  float* gb;            // fp32 [Co] grad_bias accumulator (gdirect and bias), else null
   Plan plan;
   unsigned long long* ts;  // optional pipeline timestamps of CTA 0 (DCN_DEBUG_TS), else null
   const uint8_t* cols;  // sampled columns of the chunk (BwdDataArgs::cols)
@@ -82,5 +93,9 @@ int launch_forward(const FwdArgs& a, cudaStream_t s);
 int launch_backward_data(const BwdDataArgs& a, cudaStream_t s);
 int launch_backward_scatter(const BwdDataArgs& a, cudaStream_t s);
 int launch_backward_weight(const BwdWeightArgs& a, cudaStream_t s);
+
+// Tensor map of grad_output [B][Co][HoWo] (16-bit) with a 64 x 64 box and the
+// 128-byte swizzle; false when the driver's encoder is unavailable or rejects it.
+bool make_gout_tmap(const Plan& p, const void* gout, TmaDesc* out);
 
 }  // namespace dcn

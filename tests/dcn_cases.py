@@ -73,4 +73,8 @@ SMALL = [
     Case("k1_nopad", 2, 64, 9, 9, 64, 1, 1, pad=0),
     Case("co512_c512", 1, 512, 6, 6, 512, 3, 3),
     Case("nobias", 1, 32, 7, 9, 48, 3, 2, bias=False),
+    # 64-pixel blocks inside one image (H*Wo % 64 == 0): for 16-bit types the
+    # GEMMs read grad_output directly and the weight-gradient kernel sums grad_bias
+    Case("direct_co100", 3, 32, 8, 16, 100, 3, 3),
+    Case("direct_co40", 2, 16, 8, 8, 40, 3, 3, off_std=2.0),
 ]

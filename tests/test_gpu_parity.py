@@ -108,7 +108,8 @@ import sys, numpy as np, torch
 sys.path.insert(0, sys.argv[1])
 from dcn_cases import Case, make_inputs
 from dcnv2_b200 import _C
-c = Case("chunked", 3, 40, 37, 29, 72, 3, 3, off_std=2.0)
+H, W = int(sys.argv[4]), int(sys.argv[5])
+c = Case("chunked", 3, 40, H, W, 72, 3, 3, off_std=2.0)
 dt = {"bf16": torch.bfloat16, "fp32": torch.float32}[sys.argv[3]]
 x, w, b, off, m, gy = [t.to(dt).cuda() for t in make_inputs(c, seed=3)]
 g = _C.dcn_v2_backward(x, w, m, off, b, gy, 1, 1, 1, 1)
@@ -118,21 +119,24 @@ np.savez(sys.argv[2], *[t.float().cpu().numpy() for t in g])
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("dtype", ["fp32", "bf16"])
-def test_backward_in_pixel_chunks(tmp_path, dtype):
+@pytest.mark.parametrize("dtype,hw", [("fp32", (37, 29)), ("bf16", (37, 29)), ("bf16", (32, 32))],
+                         ids=["fp32", "bf16", "bf16_direct"])
+def test_backward_in_pixel_chunks(tmp_path, dtype, hw):
     """A 1 MB chunk budget (DCN_GCOL_MB=1) splits the backward of a 3219-pixel
     problem into chunks of 384 (bf16) or 128 (fp32) pixels, the last one ragged
-    (not a multiple of 64):
+    (not a multiple of 64); at 32x32 (3072 pixels, bf16) the GEMMs read
+    grad_output directly and chunks cross image boundaries:
     every gradient still matches the float64 oracle."""
     import os
     import subprocess
     import sys
     from dcn_cases import Case
-    c = Case("chunked", 3, 40, 37, 29, 72, 3, 3, off_std=2.0)
+    c = Case("chunked", 3, 40, hw[0], hw[1], 72, 3, 3, off_std=2.0)
     out = tmp_path / "g.npz"
     env = dict(os.environ, DCN_GCOL_MB="1")
     here = os.path.dirname(os.path.abspath(__file__))
-    subprocess.run([sys.executable, "-c", _CHUNKED_SCRIPT, here, str(out), dtype], env=env,
+    subprocess.run([sys.executable, "-c", _CHUNKED_SCRIPT, here, str(out), dtype, str(hw[0]),
+                    str(hw[1])], env=env,
                    check=True, cwd=os.path.dirname(here), timeout=300)
     z = np.load(out)
     tdt = {"bf16": torch.bfloat16, "fp32": torch.float32}[dtype]
