@@ -314,9 +314,13 @@ def main():
     vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
     clocks = ClockSampler(vis.split(",")[local] if vis else local)
     clocks.start()
+    ms_step = timed(lambda: step(x, off, m, gy), args.steps)
+    # the same steps again with every kernel bracketed by CUDA events (the
+    # per-kernel breakdown and the roofline; the brackets themselves add about
+    # 2 us per launch, so the step time above is taken without them)
     _lib.trace_reset()
     _lib.trace_enable(True)
-    ms_step = timed(lambda: step(x, off, m, gy), args.steps)
+    ms_step_traced = timed(lambda: step(x, off, m, gy), args.steps)
     _lib.trace_enable(False)
     trace = _lib.trace_collect()
     # forward alone (reported beside the step)
@@ -374,7 +378,8 @@ def main():
         basis = f"algorithmic bytes {nbytes:.4g} per launch (gcol, x, offset/mask, fp32 grad_input acc, outputs, columns)"
         achieved = work / (per_launch_ms * 1e-3) / 1e9
     traffic = load_traffic(dom, args.workload, args.dtype)
-    # kernels of this library in the timed region (the accumulator memset is a runtime call)
+    # kernels of this library per timed step (counted in the traced pass, which runs
+    # the same steps; the accumulator memset is a runtime call)
     launches = sum(n for kk, (n, _) in kernels.items() if kk != "zero_accumulators")
 
     line = {
@@ -386,6 +391,7 @@ def main():
         "fwd_ms": ms_fwd, "fwd_readme_tflops": readme_flops(B, C, Ho, Wo, Co, k) / (ms_fwd * 1e-3) / 1e12,
         "fwd_bwd_gemm_tflops": 3 * gflop / (ms_step * 1e-3) / 1e12,
         "kernels_ms_per_step": {kk: v[1] / args.steps for kk, v in kernels.items()},
+        "ms_per_step_traced": ms_step_traced,
         "roofline": {"kernel": dom, "bound": bound, "achieved": achieved, "peak": peak,
                      "unit": unit, "frac": achieved / peak,
                      "peak_source": f"{peak_kind} ({'bf16 dense, burst' if bound == 'tensor' else 'HBM copy'})",

@@ -116,6 +116,14 @@ void plan_weight_grad(Plan* p, int num_sms) {
 
 }  // namespace
 
+bool pdl_enabled() {
+  static bool v = [] {
+    const char* e = getenv("DCN_NO_PDL");
+    return !(e != nullptr && atoi(e) != 0);
+  }();
+  return v;
+}
+
 bool make_gout_tmap(const Plan& P, const void* gout, TmaDesc* out) {
   static_assert(sizeof(CUtensorMap) == sizeof(TmaDesc), "tensor map size");
   EncodeTiledFn fn = encode_tiled();
@@ -280,13 +288,15 @@ int dcn_forward(const dcn_desc* d, const void* input, const void* weight, const 
     return DCN_E_WORKSPACE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  if (cudaMemsetAsync(ws + P.off_status, 0, sizeof(int), s) != cudaSuccess) return DCN_E_CUDA;
-  if (P.totalP == 0) return DCN_OK;
+  int* status = reinterpret_cast<int*>(ws + P.off_status);
+  if (P.totalP == 0)
+    return cudaMemsetAsync(status, 0, sizeof(int), s) == cudaSuccess ? DCN_OK : DCN_E_CUDA;
   if (!input || !weight || !mask || !offset || !output) return DCN_E_NULLPTR;
   if (d->has_bias && !bias) return DCN_E_NULLPTR;
   {
+    // the input pack also clears the status word
     TraceScope ts(TR_PACK_INPUT, s);
-    if ((rc = launch_pack_input(P, input, ws + P.off_x, s)) != DCN_OK) return rc;
+    if ((rc = launch_pack_input(P, input, ws + P.off_x, nullptr, status, s)) != DCN_OK) return rc;
   }
   {
     TraceScope ts(TR_PACK_WEIGHT_FWD, s);
@@ -344,14 +354,12 @@ int dcn_backward(const dcn_desc* d, const void* input, const void* weight, const
   float* gxn = reinterpret_cast<float*>(ws + P.off_gx);
   float* gw = reinterpret_cast<float*>(ws + P.off_gw);
   float* gb = reinterpret_cast<float*>(ws + P.off_gb);
-  if (cudaMemsetAsync(ws + P.off_status, 0, sizeof(int), s) != cudaSuccess) return DCN_E_CUDA;
-  // gx, gw and gb accumulators are contiguous: one memset
-  {
-    TraceScope ts(TR_ZERO_ACCUM, s);
-    if (cudaMemsetAsync(ws + P.off_gx, 0, P.bwd_bytes - P.off_gx, s) != cudaSuccess)
-      return DCN_E_CUDA;
-  }
+  int* status = reinterpret_cast<int*>(ws + P.off_status);
   if (P.totalP == 0) {
+    // gx, gw and gb accumulators are contiguous: one memset
+    if (cudaMemsetAsync(status, 0, sizeof(int), s) != cudaSuccess ||
+        cudaMemsetAsync(ws + P.off_gx, 0, P.bwd_bytes - P.off_gx, s) != cudaSuccess)
+      return DCN_E_CUDA;
     if ((rc = launch_finish_grad_weight(P, gw, gb, grad_weight, d->has_bias ? grad_bias : nullptr, s)) != DCN_OK)
       return rc;
     // empty output but non-empty input (cannot happen with Ho, Wo > 0): zero grad_input
@@ -360,12 +368,15 @@ int dcn_backward(const dcn_desc* d, const void* input, const void* weight, const
     return DCN_OK;
   }
   {
+    // the input pack also clears the status word and the grad_input accumulator
     TraceScope ts(TR_PACK_INPUT, s);
-    if ((rc = launch_pack_input(P, input, ws + P.off_x, s)) != DCN_OK) return rc;
+    if ((rc = launch_pack_input(P, input, ws + P.off_x, gxn, status, s)) != DCN_OK) return rc;
   }
   {
     TraceScope ts(TR_PACK_WEIGHT_BWD, s);
-    if ((rc = launch_pack_weight_bwd(P, weight, ws + P.off_wd, s)) != DCN_OK) return rc;
+    // ... and the weight pack the gw and gb accumulators (contiguous)
+    if ((rc = launch_pack_weight_bwd(P, weight, ws + P.off_wd, gw, P.bwd_bytes - P.off_gw, s)) != DCN_OK)
+      return rc;
   }
   // 16-bit grad_output whose 64-pixel blocks never straddle two images is read
   // by the GEMMs directly (TMA tiles of 64 pixels x 64 Co); otherwise it is

@@ -109,6 +109,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_slot;
+  pdl_wait();
   const int pend = a.pix0 + a.npix;
   if (warp == kMmaWarp) DCN_TS(1000);
 
@@ -357,22 +358,21 @@ int launch_backward_data(const BwdDataArgs& a, cudaStream_t stream) {
     case DCN_F32:
       e = cudaFuncSetAttribute(dcn_bwd_data_kernel<float>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e == cudaSuccess) dcn_bwd_data_kernel<float><<<(int)grid, kThreads, smem, stream>>>(args);
+      if (e == cudaSuccess) e = launch_k(dcn_bwd_data_kernel<float>, dim3((int)grid), dim3(kThreads), smem, stream, args);
       break;
     case DCN_F16:
       e = cudaFuncSetAttribute(dcn_bwd_data_kernel<__half>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e == cudaSuccess) dcn_bwd_data_kernel<__half><<<(int)grid, kThreads, smem, stream>>>(args);
+      if (e == cudaSuccess) e = launch_k(dcn_bwd_data_kernel<__half>, dim3((int)grid), dim3(kThreads), smem, stream, args);
       break;
     default:
       e = cudaFuncSetAttribute(dcn_bwd_data_kernel<__nv_bfloat16>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e == cudaSuccess)
-        dcn_bwd_data_kernel<__nv_bfloat16><<<(int)grid, kThreads, smem, stream>>>(args);
+        e = launch_k(dcn_bwd_data_kernel<__nv_bfloat16>, dim3((int)grid), dim3(kThreads), smem, stream, args);
       break;
   }
-  if (e != cudaSuccess) return DCN_E_CUDA;
-  return cudaGetLastError() == cudaSuccess ? DCN_OK : DCN_E_CUDA;
+  return e == cudaSuccess ? DCN_OK : DCN_E_CUDA;
 }
 
 }  // namespace dcn

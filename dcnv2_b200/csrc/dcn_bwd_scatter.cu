@@ -59,6 +59,7 @@ template <typename T>
 __global__ void __launch_bounds__(kThreads, 3) dcn_bwd_scatter_kernel(const __grid_constant__ BwdDataArgs a) {
   using G = typename std::conditional<std::is_same<T, float>::value, float, T>::type;
   constexpr int LD = GatherShape<T>::kLD;
+  pdl_wait();
   const Plan& P = a.plan;
   const int lane = threadIdx.x & 31;
   const int lp = lane >> 3, q = lane & 7;
@@ -248,18 +249,19 @@ int launch_backward_scatter(const BwdDataArgs& a, cudaStream_t stream) {
   const long long cap = (long long)a.num_sms * 16;
   if (blocks > cap) blocks = cap;
   if (blocks <= 0) return DCN_OK;
+  cudaError_t e;
   switch (P.dtype) {
     case DCN_F32:
-      dcn_bwd_scatter_kernel<float><<<(int)blocks, kThreads, 0, stream>>>(a);
+      e = launch_k(dcn_bwd_scatter_kernel<float>, dim3((int)blocks), dim3(kThreads), 0, stream, a);
       break;
     case DCN_F16:
-      dcn_bwd_scatter_kernel<__half><<<(int)blocks, kThreads, 0, stream>>>(a);
+      e = launch_k(dcn_bwd_scatter_kernel<__half>, dim3((int)blocks), dim3(kThreads), 0, stream, a);
       break;
     default:
-      dcn_bwd_scatter_kernel<__nv_bfloat16><<<(int)blocks, kThreads, 0, stream>>>(a);
+      e = launch_k(dcn_bwd_scatter_kernel<__nv_bfloat16>, dim3((int)blocks), dim3(kThreads), 0, stream, a);
       break;
   }
-  return cudaGetLastError() == cudaSuccess ? DCN_OK : DCN_E_CUDA;
+  return e == cudaSuccess ? DCN_OK : DCN_E_CUDA;
 }
 
 }  // namespace dcn

@@ -103,6 +103,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_slot;
+  pdl_wait();
   if (warp == 0) DCN_TS(1000);
 
   if (warp == kLoadWarp) {
@@ -295,22 +296,21 @@ int launch_backward_weight(const BwdWeightArgs& a, cudaStream_t stream) {
     case DCN_F32:
       e = cudaFuncSetAttribute(dcn_bwd_weight_kernel<float>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e == cudaSuccess) dcn_bwd_weight_kernel<float><<<grid, kThreads, smem, stream>>>(args);
+      if (e == cudaSuccess) e = launch_k(dcn_bwd_weight_kernel<float>, dim3(grid), dim3(kThreads), smem, stream, args);
       break;
     case DCN_F16:
       e = cudaFuncSetAttribute(dcn_bwd_weight_kernel<__half>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e == cudaSuccess) dcn_bwd_weight_kernel<__half><<<grid, kThreads, smem, stream>>>(args);
+      if (e == cudaSuccess) e = launch_k(dcn_bwd_weight_kernel<__half>, dim3(grid), dim3(kThreads), smem, stream, args);
       break;
     default:
       e = cudaFuncSetAttribute(dcn_bwd_weight_kernel<__nv_bfloat16>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e == cudaSuccess)
-        dcn_bwd_weight_kernel<__nv_bfloat16><<<grid, kThreads, smem, stream>>>(args);
+        e = launch_k(dcn_bwd_weight_kernel<__nv_bfloat16>, dim3(grid), dim3(kThreads), smem, stream, args);
       break;
   }
-  if (e != cudaSuccess) return DCN_E_CUDA;
-  return cudaGetLastError() == cudaSuccess ? DCN_OK : DCN_E_CUDA;
+  return e == cudaSuccess ? DCN_OK : DCN_E_CUDA;
 }
 
 }  // namespace dcn

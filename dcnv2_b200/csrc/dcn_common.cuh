@@ -134,6 +134,16 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int 
       : "memory");
 }
 
+// Programmatic dependent launch.  Every kernel of this library is launched with
+// the previous kernel of its stream allowed to be still running; it calls
+// pdl_wait() before its first global-memory access (the wait returns once the
+// previous grid has completed and its writes are visible), so only its launch
+// and set-up (barrier init, TMEM allocation) overlap the previous kernel's end.
+// No kernel triggers its dependents early (griddepcontrol.launch_dependents):
+// measured on the README layer, an early trigger made the step slower
+// (537 vs 504 us) because waiting CTAs of the next kernel took SM slots.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Warpgroup register re-allocation: every warp of a warpgroup executes the same
 // call; the block's register file (launch registers x threads) is redistributed.
 template <uint32_t N>

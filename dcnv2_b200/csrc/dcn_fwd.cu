@@ -92,6 +92,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  pdl_wait();
   // bias staged once per CTA (the epilogue reads it for every output element)
   for (int c = tid; c < P.nCoT * NT; c += kFwdThreads)
     sbias[c] = (a.bias != nullptr && c < P.Co) ? ldf(reinterpret_cast<const T*>(a.bias) + c) : 0.f;
@@ -448,22 +449,22 @@ int launch_forward(const FwdArgs& a, cudaStream_t stream) {
       e = cudaFuncSetAttribute(dcn_fwd_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)smem);
       if (e != cudaSuccess) return DCN_E_CUDA;
-      dcn_fwd_kernel<float><<<grid, kFwdThreads, smem, stream>>>(args);
+      e = launch_k(dcn_fwd_kernel<float>, dim3(grid), dim3(kFwdThreads), smem, stream, args);
       break;
     case DCN_F16:
       e = cudaFuncSetAttribute(dcn_fwd_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)smem);
       if (e != cudaSuccess) return DCN_E_CUDA;
-      dcn_fwd_kernel<__half><<<grid, kFwdThreads, smem, stream>>>(args);
+      e = launch_k(dcn_fwd_kernel<__half>, dim3(grid), dim3(kFwdThreads), smem, stream, args);
       break;
     default:
       e = cudaFuncSetAttribute(dcn_fwd_kernel<__nv_bfloat16>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return DCN_E_CUDA;
-      dcn_fwd_kernel<__nv_bfloat16><<<grid, kFwdThreads, smem, stream>>>(args);
+      e = launch_k(dcn_fwd_kernel<__nv_bfloat16>, dim3(grid), dim3(kFwdThreads), smem, stream, args);
       break;
   }
-  return cudaGetLastError() == cudaSuccess ? DCN_OK : DCN_E_CUDA;
+  return e == cudaSuccess ? DCN_OK : DCN_E_CUDA;
 }
 
 }  // namespace dcn

@@ -2,6 +2,8 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <utility>
+
 #include "dcn_plan.h"
 
 namespace dcn {
@@ -78,10 +80,36 @@ struct BwdWeightArgs {
   int dbg;              // experiment switches (DCN_DEBUG_SKIP); 0 in normal use
 };
 
+// Programmatic dependent launch of the library's kernels (each one waits with
+// griddepcontrol.wait before touching global memory); DCN_NO_PDL=1 turns it off.
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                     Args&&... args) {
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 // Packing / finishing kernels (dcn_pack.cu)
-int launch_pack_input(const Plan& p, const void* x, void* xt, cudaStream_t s);
+// x NCHW -> packed NHWC xt; optionally zeroes an fp32 accumulator of xt's
+// layout (`zero_acc`) and the status word (`status`) in the same pass.
+int launch_pack_input(const Plan& p, const void* x, void* xt, float* zero_acc, int* status,
+                      cudaStream_t s);
 int launch_pack_weight_fwd(const Plan& p, const void* w, uint8_t* wpk, cudaStream_t s);
-int launch_pack_weight_bwd(const Plan& p, const void* w, uint8_t* wpk, cudaStream_t s);
+// W -> backward-data B tiles; also zeroes `zero_bytes` (a multiple of 16) at
+// `zero_acc` when it is not null.
+int launch_pack_weight_bwd(const Plan& p, const void* w, uint8_t* wpk, float* zero_acc, size_t zero_bytes,
+                           cudaStream_t s);
 int launch_pack_gout(const Plan& p, const void* gout, uint8_t* gpk, float* gb, int vec,
                      cudaStream_t s);
 int launch_finish_grad_input(const Plan& p, const float* gx_nhwc, void* gx, cudaStream_t s);

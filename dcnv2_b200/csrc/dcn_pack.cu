@@ -22,6 +22,7 @@ __global__ void __launch_bounds__(256) pack_input_kernel(const T* __restrict__ x
                                                          T* __restrict__ xt, int C, int HW,
                                                          int Cg, int Cgp, int CS, int vec,
                                                          int npb, int ncb, int nblocks) {
+  pdl_wait();
   constexpr int EPV = 16 / (int)sizeof(T);           // elements per 16-byte vector
   constexpr int kItems = 64 * (64 / EPV) / 256;       // 16-byte loads per thread and block
   __shared__ __align__(16) T tile[64][64 + EPV];      // [channel][pixel]
@@ -110,6 +111,7 @@ __device__ __forceinline__ void write_chunk(uint8_t* tile, size_t lo_ofs, int ro
 template <typename T>
 __global__ void pack_weight_fwd_kernel(const T* __restrict__ w, uint8_t* __restrict__ wpk,
                                        const Plan P) {
+  pdl_wait();
   const long long nchunks = (long long)P.nCoT * P.nK * P.NT * 8;
   for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < nchunks;
        idx += (long long)gridDim.x * blockDim.x) {
@@ -140,9 +142,15 @@ __global__ void pack_weight_fwd_kernel(const T* __restrict__ w, uint8_t* __restr
 // holds rows n = j*NC + nn for the gT (tap, group)s tg = set*gT + j of the set,
 // channel cc = cch*NC + nn (packed order inside 64-channel blocks), and K
 // elements co = ko*64 + e; rows of (tap, group)s past the end are zero.
+// `zacc` (nz4 float4s, may be null) is zeroed on the side: the weight-gradient
+// accumulators.
 template <typename T>
 __global__ void pack_weight_bwd_kernel(const T* __restrict__ w, uint8_t* __restrict__ wpk,
-                                       const Plan P) {
+                                       const Plan P, float4* __restrict__ zacc, long long nz4) {
+  pdl_wait();
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < nz4;
+       i += (long long)gridDim.x * blockDim.x)
+    zacc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   const long long nchunks = (long long)P.gnU * P.nKo * P.gNC * 8;
   const int nTG = P.K2 * P.dg;
   for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < nchunks;
@@ -183,6 +191,7 @@ __global__ void __launch_bounds__(256) pack_gout_kernel(const T* __restrict__ go
                                                         uint8_t* __restrict__ gpk,
                                                         float* __restrict__ gb, const Plan P,
                                                         int vec) {
+  pdl_wait();
   __shared__ float tile[64][65];
   const int ko = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31;
@@ -266,6 +275,7 @@ template <typename T>
 __global__ void __launch_bounds__(256) finish_grad_input_kernel(const float* __restrict__ gxn,
                                                                 T* __restrict__ gx, int C, int HW,
                                                                 int Cg, int Cgp, int CS, int vec) {
+  pdl_wait();
   constexpr int EPV = 16 / (int)sizeof(T);
   __shared__ float tile[64][65];                      // [pixel][channel]
   const int b = blockIdx.z;
@@ -307,6 +317,7 @@ __global__ void __launch_bounds__(256) finish_grad_input_kernel(const float* __r
 template <typename T>
 __global__ void finish_grad_weight_kernel(const float* __restrict__ gw, const float* __restrict__ gb,
                                           T* __restrict__ gwo, T* __restrict__ gbo, const Plan P) {
+  pdl_wait();
   const long long n = (long long)P.Co * P.C * P.K2;
   for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < n;
        idx += (long long)gridDim.x * blockDim.x) {
@@ -342,11 +353,16 @@ __device__ __forceinline__ void transpose8x8_b16(const uint4 (&row)[8], uint4 (&
 // x [B][C][HW] -> xt [B][HW][dg][Cgp] (perm_logical order).  Thread: 16-byte
 // chunk q of a 64-channel block and 8 pixels; q varies fastest so that the
 // eight chunks of a pixel's 128-byte line are stored by one warp instruction.
+// When `acc` is not null the fp32 accumulator of the same layout (the backward's
+// grad_input sums) is zeroed alongside, and `status` (if not null) is cleared.
 template <typename T>
 __global__ void __launch_bounds__(256) pack_input_rt_kernel(const T* __restrict__ x, T* __restrict__ xt,
                                                             int C, int HW, int Cg, int Cgp, int CS,
-                                                            long long nthr) {
+                                                            long long nthr, float* __restrict__ acc,
+                                                            int* __restrict__ status) {
+  pdl_wait();
   const int np8 = HW >> 3, nblk = CS >> 6;
+  if (status != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *status = 0;
   for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < nthr;
        idx += (long long)gridDim.x * blockDim.x) {
     const int q = (int)(idx & 7);
@@ -362,20 +378,31 @@ __global__ void __launch_bounds__(256) pack_input_rt_kernel(const T* __restrict_
       row[r] = cc < Cg ? ldg_nc_v4(x + ((size_t)b * C + g * Cg + cc) * HW + p8 * 8) : make_uint4(0u, 0u, 0u, 0u);
     }
     transpose8x8_b16(row, col);
-    T* o = xt + ((size_t)b * HW + p8 * 8) * CS + d0 + q * 8;
+    const size_t eo = ((size_t)b * HW + p8 * 8) * CS + d0 + q * 8;
+    T* o = xt + eo;
 #pragma unroll
     for (int e = 0; e < 8; ++e) *reinterpret_cast<uint4*>(o + (size_t)e * CS) = col[e];
+    if (acc != nullptr) {
+      const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float4* a4 = reinterpret_cast<float4*>(acc + eo + (size_t)e * CS);
+        a4[0] = z;
+        a4[1] = z;
+      }
+    }
   }
 }
 
 template <typename F>
 int dispatch(int dtype, F&& f) {
+  cudaError_t e;
   switch (dtype) {
-    case DCN_F32: f(float{}); break;
-    case DCN_F16: f(__half{}); break;
-    default: f(__nv_bfloat16{}); break;
+    case DCN_F32: e = f(float{}); break;
+    case DCN_F16: e = f(__half{}); break;
+    default: e = f(__nv_bfloat16{}); break;
   }
-  return cudaGetLastError() == cudaSuccess ? DCN_OK : DCN_E_CUDA;
+  return e == cudaSuccess ? DCN_OK : DCN_E_CUDA;
 }
 
 int grid_for(long long n, int threads) {
@@ -386,7 +413,8 @@ int grid_for(long long n, int threads) {
 
 }  // namespace
 
-int launch_pack_input(const Plan& P, const void* x, void* xt, cudaStream_t s) {
+int launch_pack_input(const Plan& P, const void* x, void* xt, float* zero_acc, int* status,
+                      cudaStream_t s) {
   const int HW = P.H * P.W;
   const int vec = (HW % 8 == 0) && (((uintptr_t)x & 15u) == 0);
   const int npb = ceil_div(HW, 64), ncb = P.CS / 64;
@@ -397,14 +425,19 @@ int launch_pack_input(const Plan& P, const void* x, void* xt, cudaStream_t s) {
     const long long nthr = (long long)P.B * (HW / 8) * (P.CS / 64) * 8;
     return dispatch(P.dtype, [&](auto tag) {
       using T = decltype(tag);
-      if constexpr (sizeof(T) == 2)
-        pack_input_rt_kernel<T><<<grid_for(nthr, 256), 256, 0, s>>>(static_cast<const T*>(x), static_cast<T*>(xt),
-                                                                     P.C, HW, P.Cg, P.Cgp, P.CS, nthr);
+      if constexpr (sizeof(T) != 2) return cudaErrorInvalidValue;
+      else return launch_k(pack_input_rt_kernel<T>, dim3(grid_for(nthr, 256)), dim3(256), 0, s, static_cast<const T*>(x), static_cast<T*>(xt),
+                                                                     P.C, HW, P.Cg, P.Cgp, P.CS, nthr,
+                                                                     zero_acc, status);
     });
   }
+  if (status != nullptr && cudaMemsetAsync(status, 0, sizeof(int), s) != cudaSuccess) return DCN_E_CUDA;
+  if (zero_acc != nullptr &&
+      cudaMemsetAsync(zero_acc, 0, (size_t)P.B * HW * P.CS * sizeof(float), s) != cudaSuccess)
+    return DCN_E_CUDA;
   return dispatch(P.dtype, [&](auto tag) {
     using T = decltype(tag);
-    pack_input_kernel<T><<<grid, 256, 0, s>>>(static_cast<const T*>(x), static_cast<T*>(xt), P.C,
+    return launch_k(pack_input_kernel<T>, dim3(grid), dim3(256), 0, s, static_cast<const T*>(x), static_cast<T*>(xt), P.C,
                                               HW, P.Cg, P.Cgp, P.CS, vec, npb, ncb, (int)nblocks);
   });
 }
@@ -413,15 +446,18 @@ int launch_pack_weight_fwd(const Plan& P, const void* w, uint8_t* wpk, cudaStrea
   const long long n = (long long)P.nCoT * P.nK * P.NT * 8;
   return dispatch(P.dtype, [&](auto tag) {
     using T = decltype(tag);
-    pack_weight_fwd_kernel<T><<<grid_for(n, 256), 256, 0, s>>>(static_cast<const T*>(w), wpk, P);
+    return launch_k(pack_weight_fwd_kernel<T>, dim3(grid_for(n, 256)), dim3(256), 0, s, static_cast<const T*>(w), wpk, P);
   });
 }
 
-int launch_pack_weight_bwd(const Plan& P, const void* w, uint8_t* wpk, cudaStream_t s) {
+int launch_pack_weight_bwd(const Plan& P, const void* w, uint8_t* wpk, float* zero_acc, size_t zero_bytes,
+                           cudaStream_t s) {
   const long long n = (long long)P.gnU * P.nKo * P.gNC * 8;
+  if (zero_bytes % 16 != 0 || ((uintptr_t)zero_acc & 15u) != 0) return DCN_E_UNSUPPORTED;
+  const long long nz4 = zero_acc ? (long long)(zero_bytes / 16) : 0;
   return dispatch(P.dtype, [&](auto tag) {
     using T = decltype(tag);
-    pack_weight_bwd_kernel<T><<<grid_for(n, 256), 256, 0, s>>>(static_cast<const T*>(w), wpk, P);
+    return launch_k(pack_weight_bwd_kernel<T>, dim3(grid_for(n > nz4 ? n : nz4, 256)), dim3(256), 0, s, static_cast<const T*>(w), wpk, P, reinterpret_cast<float4*>(zero_acc), nz4);
   });
 }
 
@@ -434,7 +470,7 @@ int launch_pack_gout(const Plan& P, const void* gout, uint8_t* gpk, float* gb, i
   dim3 grid(gx, P.nKo);
   return dispatch(P.dtype, [&](auto tag) {
     using T = decltype(tag);
-    pack_gout_kernel<T><<<grid, 256, 0, s>>>(static_cast<const T*>(gout), gpk, gb, P, vec);
+    return launch_k(pack_gout_kernel<T>, dim3(grid), dim3(256), 0, s, static_cast<const T*>(gout), gpk, gb, P, vec);
   });
 }
 
@@ -444,7 +480,7 @@ int launch_finish_grad_input(const Plan& P, const float* gxn, void* gx, cudaStre
   dim3 grid(ceil_div(HW, 64), P.CS / 64, P.B);
   return dispatch(P.dtype, [&](auto tag) {
     using T = decltype(tag);
-    finish_grad_input_kernel<T><<<grid, 256, 0, s>>>(gxn, static_cast<T*>(gx), P.C, HW, P.Cg,
+    return launch_k(finish_grad_input_kernel<T>, dim3(grid), dim3(256), 0, s, gxn, static_cast<T*>(gx), P.C, HW, P.Cg,
                                                      P.Cgp, P.CS, vec);
   });
 }
@@ -454,8 +490,7 @@ int launch_finish_grad_weight(const Plan& P, const float* gw, const float* gb, v
   const long long n = (long long)P.Co * P.C * P.K2;
   return dispatch(P.dtype, [&](auto tag) {
     using T = decltype(tag);
-    finish_grad_weight_kernel<T><<<grid_for(n, 256), 256, 0, s>>>(
-        gw, gb, static_cast<T*>(gwo), static_cast<T*>(gbo), P);
+    return launch_k(finish_grad_weight_kernel<T>, dim3(grid_for(n, 256)), dim3(256), 0, s, gw, gb, static_cast<T*>(gwo), static_cast<T*>(gbo), P);
   });
 }
 
