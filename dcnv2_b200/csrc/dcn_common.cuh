@@ -141,7 +141,7 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int 
 // and set-up (barrier init, TMEM allocation) overlap the previous kernel's end.
 // No kernel triggers its dependents early (griddepcontrol.launch_dependents):
 // measured on the README layer, an early trigger made the step slower
-// (537 vs 504 us) because waiting CTAs of the next kernel took SM slots.
+// (537 vs 504 us).
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // Warpgroup register re-allocation: every warp of a warpgroup executes the same

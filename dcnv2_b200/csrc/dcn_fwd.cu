@@ -5,15 +5,16 @@
 //   D[pixel, co] = sum_{t, g, c} A[pixel, (t,g,c)] * Wt[co, (t,g,c)]
 //   A[pixel, (t,g,c)] = mask * bilinear(x_nhwc[b, :, :, g, c], pos(pixel, t) + offset)
 //
-// CTA roles (448 threads):
-//   warps 0-7  gather producers: 16 pixel rows per warp, 8 lanes per pixel so
-//              each warp-wide load reads whole corner lines; build the A tile
-//              (128 pixels x 64 channels, K-major, 128B swizzle) in smem
-//   warps 8-11 epilogue: TMEM -> registers, + bias, NCHW store
-//   warp 12    bulk-copy (TMA) producer of the pre-packed weight tile
-//   warp 13    TMEM owner and single-thread tcgen05.mma issuer (warps 14-15 idle)
-// Registers are moved to the gather warps with setmaxnreg (184 each; epilogue
-// 88, control warpgroup 56).
+// CTA roles (640 threads, one CTA per SM, persistent over (pixel, Co) tiles):
+//   warps 0-7   gather producers: 16 pixel rows per warp, 8 lanes per pixel so
+//               each warp-wide load reads whole corner lines; build the A tile
+//               (128 pixels x 64 channels, K-major, 128B swizzle) in smem
+//   warps 8-15  epilogue: TMEM -> registers, + bias, NCHW store; between tiles
+//               they also build the next tile's sampling geometry (corner index
+//               and the four weights x mask per row and tap) in shared memory
+//   warp 16     bulk-copy (TMA) producer of the pre-packed weight tile
+//   warp 17     TMEM owner and single-thread tcgen05.mma issuer (warps 18-19 idle)
+// Registers are moved with setmaxnreg (producers 160, epilogue 64, control 32).
 // A/B stages form an mbarrier ring; the accumulator is double-buffered in TMEM so
 // the epilogue of tile i overlaps the main loop of tile i+1.
 #include "dcn_common.cuh"
