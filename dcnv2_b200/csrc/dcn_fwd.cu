@@ -17,6 +17,8 @@
 // Registers are moved with setmaxnreg (producers 160, epilogue 64, control 32).
 // A/B stages form an mbarrier ring; the accumulator is double-buffered in TMEM so
 // the epilogue of tile i overlaps the main loop of tile i+1.
+#include <stdlib.h>
+
 #include "dcn_common.cuh"
 #include "dcn_gather.cuh"
 #include "dcn_kernels.h"
@@ -148,10 +150,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           const int i = fdiv(t, P.fd_kw), j = t - i * P.kw;
           const float hs = (float)(ho * P.sh - P.ph + i * P.dh) + raw_to_f<T>(rh[k]);
           const float ws = (float)(wo * P.sw - P.pw + j * P.dw) + raw_to_f<T>(rw[k]);
-          r = make_pixgeo(b * HW, hs, ws, raw_to_f<T>(rm[k]), P.H, P.W);
+          r = make_pixgeo_clamped(b * HW, hs, ws, raw_to_f<T>(rm[k]), P.H, P.W);
         }
         const int e = (buf * kGeoTaps + slot) * kTileM + row;
-        sgeo_idx[e] = r.gidx;
+        sgeo_idx[e] = (int)((unsigned)r.gidx * (unsigned)P.CS);   // element offset of the corner line
         sgeo_w[e] = make_float4(r.w[0], r.w[1], r.w[2], r.w[3]);
       }
     }
@@ -172,6 +174,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     constexpr int BATCH = sizeof(T) == 4 ? 2 : 4;
     const int lp = lane / LPP, q = lane % LPP;
     const T* __restrict__ xt = reinterpret_cast<const T*>(a.xt);
+    // element distance of the right and the lower corner line of a clamped block
+    const size_t dxe = P.W > 1 ? (size_t)P.CS : 0, dye = P.H > 1 ? (size_t)P.W * P.CS : 0;
     uint32_t kidx = 0, gcnt = 0, gbuf = 0;
     int rs = 0;                                   // ring stage of step kidx and its phase
     uint32_t rph = 0;
@@ -234,7 +238,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         for (int i0 = 0; i0 < ITER; i0 += BATCH) {
 #pragma unroll
           for (int it = 0; it < BATCH; ++it)
-            load_corners_px<T>(xt, geo[i0 + it], P.W, P.CS, cofs, v[it]);
+            load_block<T>(xt + ((size_t)(unsigned)geo[i0 + it].gidx + cofs), dxe, dye, v[it]);
           if (i0 == 0 && !mbar_wait(empty0 + 8 * s, ph ^ 1u, a.err, &abort_flag)) { ok = false; break; }
           if (warp == 0 && i0 == 0) DCN_TS(4 * kidx + 1);
 #pragma unroll
@@ -243,7 +247,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
         if (!ok) break;
         if (warp == 0) DCN_TS(4 * kidx + 2);
-        fence_proxy_async_smem();
+        if (!(a.dbg & 16)) fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(full0 + 8 * s);
         if (warp == 0) DCN_TS(4 * kidx + 3);
@@ -359,6 +363,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         for (int kc = 0; kc < P.nK; ++kc, (++s == S ? (s = 0, ph ^= 1u) : 0u)) {
           if (!mbar_wait(empty0 + 8 * s, ph ^ 1u, a.err, &abort_flag)) { ok = false; break; }
           const uint32_t btile = sbase + s * stageBytes + NS * kATile;
+          if (a.dbg & 8) {   // study switch: no weight copy (the MMA reads stale data)
+            mbar_arrive(full0 + 8 * s);
+            continue;
+          }
           mbar_arrive_expect_tx(full0 + 8 * s, NS * bTile);
           bulk_g2s(btile, wsrc + (size_t)kc * P.wf_tile_bytes, NS * bTile, full0 + 8 * s);
         }
@@ -436,11 +444,24 @@ int launch_forward(const FwdArgs& a, cudaStream_t stream) {
   const size_t geoBytes = NB * geoWin + biasBytes;
   int S = (int)((kFwdSmemBudget - 1024 - geoBytes) / stageBytes);
   if (S > kMaxStages) S = kMaxStages;
+  if (const char* e = getenv("DCN_FWD_STAGES")) {   // study switch: fewer stages, more L1
+    const int sm = atoi(e);
+    if (sm >= 2 && sm < S) S = sm;
+  }
   if (S < 2) return DCN_E_UNSUPPORTED;
   FwdArgs args = a;
   args.stages = S;
   args.geo_bufs = NB;
   const size_t smem = 1024 + (size_t)S * stageBytes + geoBytes;
+  static int carve_set = -1;
+  if (getenv("DCN_FWD_CARVE")) {   // study switch: shared-memory carveout in percent
+    const int pc = atoi(getenv("DCN_FWD_CARVE"));
+    if (pc != carve_set) {
+      cudaFuncSetAttribute(dcn_fwd_kernel<__nv_bfloat16>, cudaFuncAttributePreferredSharedMemoryCarveout, pc);
+      cudaFuncSetAttribute(dcn_fwd_kernel<__half>, cudaFuncAttributePreferredSharedMemoryCarveout, pc);
+      carve_set = pc;
+    }
+  }
   const int nTiles = P.nPT * P.nCoT;
   int grid = nTiles < a.num_sms ? nTiles : a.num_sms;
   if (grid <= 0) return DCN_OK;

@@ -142,6 +142,49 @@ __device__ __forceinline__ PixGeo make_pixgeo(int img_base, float h, float w, fl
   return r;
 }
 
+// As make_pixgeo, but with the 2 x 2 corner block moved inside the image: the
+// block's top-left corner is clamped to row 0 .. max(H-2, 0) and column
+// 0 .. max(W-2, 0) and the weights of the corners that lie inside the image are
+// carried over to their place in the moved block (a corner outside the image
+// has weight 0 already).  All four corner lines of the block are then inside the
+// image (rows r and r + (H > 1), columns c and c + (W > 1)), so they can be
+// loaded without a per-corner test; the blend is unchanged.
+__device__ __forceinline__ PixGeo make_pixgeo_clamped(int img_base, float h, float w, float m, int H, int W) {
+  const Geo g = make_geo(h, w, m, H, W);
+  const float hf = floorf(h), wf = floorf(w);
+  const int hl = (int)hf, wl = (int)wf;
+  const int r = min(max(hl, 0), max(H - 2, 0));
+  const int c = min(max(wl, 0), max(W - 2, 0));
+  const int sy = hl - r, sx = wl - c;   // -1, 0 or 1 whenever a weight is non-zero
+  // rows: (top, bottom) pairs of the original block -> moved block
+  float t0 = g.w[0], t1 = g.w[1], b0 = g.w[2], b1 = g.w[3];
+  if (sy < 0) { t0 = b0; t1 = b1; b0 = 0.f; b1 = 0.f; }
+  else if (sy > 0) { b0 = t0; b1 = t1; t0 = 0.f; t1 = 0.f; }
+  // columns: (left, right) of each row
+  if (sx < 0) { t0 = t1; b0 = b1; t1 = 0.f; b1 = 0.f; }
+  else if (sx > 0) { t1 = t0; b1 = b0; t0 = 0.f; b0 = 0.f; }
+  PixGeo out;
+  out.gidx = img_base + r * W + c;
+  out.w[0] = t0;
+  out.w[1] = t1;
+  out.w[2] = b0;
+  out.w[3] = b1;
+  return out;
+}
+
+// Loads one lane's 8-channel slices of a clamped 2 x 2 block (no tests):
+// corner i at p0 + {0, dx, dy, dy + dx} elements, p0 = the lane's top-left slice.
+template <typename T>
+__device__ __forceinline__ void load_block(const T* __restrict__ p0, size_t dx, size_t dy,
+                                           uint4 (&v)[4][GatherShape<T>::kLD]) {
+  constexpr int LD = GatherShape<T>::kLD;
+  const T* p[4] = {p0, p0 + dx, p0 + dy, p0 + dy + dx};
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int k = 0; k < LD; ++k) v[i][k] = ldg_nc_v4(p[i] + k * (8 / LD));
+}
+
 __device__ __forceinline__ PixGeo zero_pixgeo() {
   PixGeo r;
   r.gidx = 0;

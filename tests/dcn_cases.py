@@ -77,4 +77,7 @@ SMALL = [
     # GEMMs read grad_output directly and the weight-gradient kernel sums grad_bias
     Case("direct_co100", 3, 32, 8, 16, 100, 3, 3),
     Case("direct_co40", 2, 16, 8, 8, 40, 3, 3, off_std=2.0),
+    # one-pixel-high / -wide images: the clamped 2x2 corner block degenerates
+    Case("thin_h1", 2, 16, 1, 9, 24, 3, 3),
+    Case("thin_w1", 1, 16, 6, 1, 24, 3, 3, off_std=2.0),
 ]
