@@ -5,19 +5,21 @@
 //   D[pixel, co] = sum_{t, g, c} A[pixel, (t,g,c)] * Wt[co, (t,g,c)]
 //   A[pixel, (t,g,c)] = mask * bilinear(x_nhwc[b, :, :, g, c], pos(pixel, t) + offset)
 //
-// CTA roles (640 threads, one CTA per SM, persistent over (pixel, Co) tiles):
-//   warps 0-7   gather producers: 16 pixel rows per warp, 8 lanes per pixel so
+// CTA roles (896 threads, one CTA per SM, persistent over (pixel, Co) tiles):
+//   warps 0-15  gather producers: 8 pixel rows per warp, 8 lanes per pixel so
 //               each warp-wide load reads whole corner lines; build the A tile
 //               (128 pixels x 64 channels, K-major, 128B swizzle) in smem
-//   warps 8-15  epilogue: TMEM -> registers, + bias, NCHW store; between tiles
+//   warps 16-23 epilogue: TMEM -> registers, + bias, NCHW store; between tiles
 //               they also build the next tile's sampling geometry (corner index
 //               and the four weights x mask per row and tap) in shared memory
-//   warp 16     bulk-copy (TMA) producer of the pre-packed weight tile
-//   warp 17     TMEM owner and single-thread tcgen05.mma issuer (warps 18-19 idle)
-// Registers are moved with setmaxnreg (producers 160, epilogue 64, control 32).
+//   warp 24     bulk-copy (TMA) producer of the pre-packed weight tile
+//   warp 25     TMEM owner and single-thread tcgen05.mma issuer (warps 26-27 idle)
+// Registers are moved with setmaxnreg (producers 80, epilogue 64, control 32).
 // A/B stages form an mbarrier ring; the accumulator is double-buffered in TMEM so
 // the epilogue of tile i overlaps the main loop of tile i+1.
 #include <stdlib.h>
+
+#include <type_traits>
 
 #include "dcn_common.cuh"
 #include "dcn_gather.cuh"
@@ -30,14 +32,22 @@ namespace {
 #define DCN_TS(slot) \
   do { if (a.ts && blockIdx.x == 0 && lane == 0 && (slot) < 1024) a.ts[(slot)] = globaltimer(); } while (0)
 
-constexpr int kFwdThreads = 640;  // 5 warpgroups; warps 18-19 idle
 constexpr int kMaxCo = 2048;  // bias staged in smem: Co up to 2048
 constexpr int kGeoTaps = 9;   // (tap, group)s per geometry window
-constexpr int kProdThreads = 256;
-constexpr int kEpiWarp0 = 8;
-constexpr int kEpiWarps = 8;
-constexpr int kTmaWarp = 16;
-constexpr int kMmaWarp = 17;
+constexpr int kProdWarps = 16;                       // gather producers (4 warpgroups)
+constexpr int kProdThreads = kProdWarps * 32;
+constexpr int kRowsPerWarp = kTileM / kProdWarps;    // A-tile rows per producer warp
+constexpr int kEpiWarp0 = kProdWarps;
+constexpr int kEpiWarps = 8;                         // two per TMEM lane quarter
+constexpr int kTmaWarp = kEpiWarp0 + kEpiWarps;
+constexpr int kMmaWarp = kTmaWarp + 1;
+constexpr int kFwdThreads = (kTmaWarp + 4) * 32;     // 7 warpgroups (896); the last two warps idle
+constexpr int kLaunchRegs = 72;                      // 65536 / 896, rounded down to a multiple of 8
+// setmaxnreg split of the launch pool (896 x 72 = 64512):
+// producers 4 x 128 x 80 + epilogue 2 x 128 x 64 + control 128 x 32 = 61440
+constexpr int kProdRegs = 80, kEpiRegs = 64, kCtlRegs = 32;
+static_assert(kProdThreads * kProdRegs + kEpiWarps * 32 * kEpiRegs + 128 * kCtlRegs <= kFwdThreads * kLaunchRegs,
+              "register split exceeds the launch pool");
 
 template <typename T>
 __global__ void __launch_bounds__(kFwdThreads, 1)
@@ -112,16 +122,18 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   if (warp == 0) DCN_TS(1000);
 
   // Builds geometry window slot `buf` for pixel tile pt and (tap, group)s
-  // tg0 .. tg0 + wt - 1 with 256 threads (this one is thread gt).  Thread gt
-  // owns row gt % 128 and slots gt / 128 + 2k: the row's coordinates are
-  // computed once, and every offset / mask load of the window is issued before
-  // the first one is used, so their latencies overlap.
-  auto build_geometry = [&](int pt, int tg0, int wt, int buf, int gt) {
-    constexpr int KI = (kGeoTaps * kTileM + 255) / 256;
+  // tg0 .. tg0 + wt - 1 with NTHR threads (this one is thread gt).  Thread gt
+  // owns row gt % 128 and slots gt / 128 + (NTHR / 128) k: the row's
+  // coordinates are computed once, and every offset / mask load of the window
+  // is issued before the first one is used, so their latencies overlap.
+  auto build_geometry = [&](auto nthr_c, int pt, int tg0, int wt, int buf, int gt) {
+    constexpr int NTHR = decltype(nthr_c)::value;
+    constexpr int SSTEP = NTHR / kTileM;
+    constexpr int KI = (kGeoTaps * kTileM + NTHR - 1) / NTHR;
     const T* __restrict__ off = reinterpret_cast<const T*>(a.offset);
     const T* __restrict__ msk = reinterpret_cast<const T*>(a.mask);
     const int HW = P.H * P.W;
-    const int row = gt & (kTileM - 1), slot0 = gt >> 7;
+    const int row = gt & (kTileM - 1), slot0 = gt / kTileM;
     const int pix = pt * kTileM + row;
     const bool pv = pix < P.totalP && !(a.dbg & 1);
     const int b = pv ? fdiv(pix, P.fd_howo) : 0, p = pv ? pix - b * HoWo : 0;
@@ -129,7 +141,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     uint32_t rh[KI], rw[KI], rm[KI];
 #pragma unroll
     for (int k = 0; k < KI; ++k) {
-      const int slot = slot0 + 2 * k;
+      const int slot = slot0 + SSTEP * k;
       rh[k] = rw[k] = rm[k] = 0u;
       if (pv && slot < wt) {
         const int tgi = tg0 + slot;
@@ -142,7 +154,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
 #pragma unroll
     for (int k = 0; k < KI; ++k) {
-      const int slot = slot0 + 2 * k;
+      const int slot = slot0 + SSTEP * k;
       if (slot < wt) {
         PixGeo r = zero_pixgeo();
         if (pv) {
@@ -164,14 +176,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   // producers 2 x 4 warps x 160, epilogue 2 x 4 warps x 64, control 4 warps x 32
   // (= 61440, the launch pool).
   if (warp < kProdThreads / 32) {
-    regs_inc<160>();
+    regs_inc<kProdRegs>();
     // ------------------------------------------------ gather producers
-    // Warp w builds rows w*16 .. w*16+15 of every A tile, 4 rows at a time with
-    // 8 lanes per row.
+    // Warp w builds rows w*R .. w*R+R-1 (R = kRowsPerWarp) of every A tile, 4
+    // rows at a time with 8 lanes per row.
     using GS = GatherShape<T>;
     constexpr int LPP = GS::kLPP, CPL = GS::kCPL, PPI = GS::kPPI;
-    constexpr int ITER = 16 / PPI;
-    constexpr int BATCH = sizeof(T) == 4 ? 2 : 4;
+    constexpr int ITER = kRowsPerWarp / PPI;
+    constexpr int BATCH = sizeof(T) == 4 ? 1 : (ITER < 4 ? ITER : 4);
     const int lp = lane / LPP, q = lane % LPP;
     const T* __restrict__ xt = reinterpret_cast<const T*>(a.xt);
     // element distance of the right and the lower corner line of a clamped block
@@ -207,7 +219,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(geoe);
             if (!mbar_wait(geoe, gcnt & 1u, a.err, &abort_flag)) { ok = false; break; }
-            build_geometry(pt, tg, min(nwin_t, nTG - tg), 0, tid);
+            build_geometry(std::integral_constant<int, kProdThreads>{}, pt, tg, min(nwin_t, nTG - tg), 0, tid);
             __syncwarp();
             if (lane == 0) mbar_arrive(geof);
             if (!mbar_wait(geof, gcnt & 1u, a.err, &abort_flag)) { ok = false; break; }
@@ -218,7 +230,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         if (cb == 0) {
 #pragma unroll
           for (int it = 0; it < ITER; ++it) {
-            const int e = (gbuf * kGeoTaps + tl) * kTileM + warp * 16 + it * PPI + lp;
+            const int e = (gbuf * kGeoTaps + tl) * kTileM + warp * kRowsPerWarp + it * PPI + lp;
             const float4 w4 = sgeo_w[e];
             geo[it].gidx = sgeo_idx[e];
             geo[it].w[0] = w4.x;
@@ -243,7 +255,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           if (warp == 0 && i0 == 0) DCN_TS(4 * kidx + 1);
 #pragma unroll
           for (int it = 0; it < BATCH; ++it)
-            blend_store<T>(v[it], geo[i0 + it], atile, kATile, warp * 16 + (i0 + it) * PPI + lp, q);
+            blend_store<T>(v[it], geo[i0 + it], atile, kATile, warp * kRowsPerWarp + (i0 + it) * PPI + lp, q);
         }
         if (!ok) break;
         if (warp == 0) DCN_TS(4 * kidx + 2);
@@ -260,10 +272,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
     }
   } else if (warp < kTmaWarp) {
-    regs_dec<64>();
+    regs_dec<kEpiRegs>();
     // ------------------------------------------------ epilogue
     const int q = warp & 3;
-    const int chalf = (warp - kEpiWarp0) >> 2;   // the two warps of a lane quarter interleave 16-column blocks
+    constexpr int kEpiPerQuarter = kEpiWarps / 4;
+    const int chalf = (warp - kEpiWarp0) >> 2;   // warps of one lane quarter interleave 16-column blocks
     const int row = q * 32 + lane;
     T* __restrict__ y = reinterpret_cast<T*>(a.out);
     int it = 0;
@@ -279,7 +292,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           const int gb = gnext & 1;
           if (!mbar_wait(gfree0 + 8 * gb, ((gnext >> 1) & 1) ^ 1, a.err, &abort_flag)) { gok = false; break; }
           const int gpt = (blockIdx.x + gnext * (int)gridDim.x) / P.nCoT;
-          build_geometry(gpt, 0, P.K2 * P.dg, gb, tid - kEpiWarp0 * 32);
+          // study switch 32: windows after the first two are not rebuilt (they
+          // keep earlier tiles' geometry: valid indices, wrong results)
+          if (!((a.dbg & 32) && gnext >= 2))
+            build_geometry(std::integral_constant<int, kEpiWarps * 32>{}, gpt, 0, P.K2 * P.dg, gb,
+                           tid - kEpiWarp0 * 32);
           __syncwarp();
           if (lane == 0) mbar_arrive(gready0 + 8 * gb);
         }
@@ -307,7 +324,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const int rpl = wpix0 + cvl * EPV;
       const int rbl = vec ? rpl / HoWo : 0;
       T* yrun = y + (size_t)rbl * P.Co * HoWo + (rpl - rbl * HoWo);
-      for (int c0 = 16 * chalf; c0 < NT; c0 += 32) {
+      for (int c0 = 16 * chalf; c0 < NT && !(a.dbg & 64); c0 += 16 * kEpiPerQuarter) {   // 64: no epilogue (study)
         float v[16];
         tmem_ld16(tbase + c0, v);
         if (vec) {
@@ -350,7 +367,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       if (warp == kEpiWarp0) DCN_TS(801 + 2 * it);
     }
   } else {
-    regs_dec<32>();
+    regs_dec<kCtlRegs>();
     if (warp == kTmaWarp) {
     // ------------------------------------------------ weight tiles (bulk copy)
     if (lane == 0) {
