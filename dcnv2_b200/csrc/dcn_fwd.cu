@@ -334,8 +334,34 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             const float4 b4 = *reinterpret_cast<const float4*>(sbias + ct * NT + c0 + j);
             bz[j] = b4.x; bz[j + 1] = b4.y; bz[j + 2] = b4.z; bz[j + 3] = b4.w;
           }
-          // stage [JH co][32 px] (JH = 16 columns for 16-bit outputs, 8 per pass for
-          // f32 so the stage stays 1 KB a warp) then store 16-byte runs of pixels per co row
+          if constexpr (sizeof(T) == 2) {
+            // stage [8 co pairs][32 px] words (co 2p in the low half, 2p+1 in the
+            // high half: one packed conversion and one 32-bit store per pair), then
+            // lane (pair lane / 4, run lane % 4) reads its 8 pixels of the pair and
+            // splits them into the two co rows' 16-byte runs
+            constexpr int kBF = OpOf<T>::kBF16;
+            const uint32_t sw = smem_u32(stg);
+#pragma unroll
+            for (int p2 = 0; p2 < 8; ++p2)
+              sts_u32(sw + (p2 * 32 + lane) * 4u,
+                      pack2<kBF>(v[2 * p2] + bz[2 * p2], v[2 * p2 + 1] + bz[2 * p2 + 1]));
+            __syncwarp();
+            const int pp = lane >> 2;
+            const uint4 w0 = lds_v4(sw + (pp * 32 + cvl * 8) * 4u);
+            const uint4 w1 = lds_v4(sw + (pp * 32 + cvl * 8 + 4) * 4u);
+            const uint4 ev = make_uint4(__byte_perm(w0.x, w0.y, 0x5410), __byte_perm(w0.z, w0.w, 0x5410),
+                                        __byte_perm(w1.x, w1.y, 0x5410), __byte_perm(w1.z, w1.w, 0x5410));
+            const uint4 od = make_uint4(__byte_perm(w0.x, w0.y, 0x7632), __byte_perm(w0.z, w0.w, 0x7632),
+                                        __byte_perm(w1.x, w1.y, 0x7632), __byte_perm(w1.z, w1.w, 0x7632));
+            const int co = ct * NT + c0 + 2 * pp;
+            if (!(a.dbg & 2)) {
+              if (co < P.Co) *reinterpret_cast<uint4*>(yrun + (size_t)co * HoWo) = ev;
+              if (co + 1 < P.Co) *reinterpret_cast<uint4*>(yrun + (size_t)(co + 1) * HoWo) = od;
+            }
+            __syncwarp();
+          } else {
+          // stage [JH co][32 px] (8 columns per pass for f32 so the stage stays
+          // 1 KB a warp) then store 16-byte runs of pixels per co row
 #pragma unroll
           for (int h = 0; h < 16 / JH; ++h) {
 #pragma unroll
@@ -352,6 +378,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
               }
             }
             __syncwarp();
+          }
           }
         } else {
 #pragma unroll
