@@ -55,6 +55,7 @@ WORKLOADS = {
 }
 DTYPES = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+RED_PEAK_TBS = 5.9  # fp32 L2 reduction rate of the scatter's access pattern, measured on a B200
 
 
 def readme_flops(B, C, Ho, Wo, Co, k):
@@ -377,6 +378,14 @@ def main():
         work, bound, unit, peak = nbytes, "hbm", "GB/s", peaks["hbm_gbs"]
         basis = f"algorithmic bytes {nbytes:.4g} per launch (gcol, x, offset/mask, fp32 grad_input acc, outputs, columns)"
         achieved = work / (per_launch_ms * 1e-3) / 1e9
+        # the scatter's real limiter: fp32 reductions into L2 (4 corners x C x 4 B per
+        # pixel and tap) against the rate a microbenchmark of the same access pattern
+        # sustains on this B200 (red.global.add.v4.f32, random target pixels)
+        red_bytes = P * K2 * 4 * C * 4 / (n_dom / args.steps)
+        red_tbs = red_bytes / (per_launch_ms * 1e-3) / 1e12
+        reduction = {"achieved": red_tbs, "peak": RED_PEAK_TBS, "unit": "TB/s", "frac": red_tbs / RED_PEAK_TBS,
+                     "bytes_per_launch": red_bytes,
+                     "peak_source": "microbenchmark of red.global.add.v4.f32 with random targets on this B200"}
     traffic = load_traffic(dom, args.workload, args.dtype)
     # kernels of this library per timed step (counted in the traced pass, which runs
     # the same steps; the accumulator memset is a runtime call)
@@ -395,7 +404,8 @@ def main():
         "roofline": {"kernel": dom, "bound": bound, "achieved": achieved, "peak": peak,
                      "unit": unit, "frac": achieved / peak,
                      "peak_source": f"{peak_kind} ({'bf16 dense, burst' if bound == 'tensor' else 'HBM copy'})",
-                     "traffic": traffic, "algorithmic": basis},
+                     "traffic": traffic, "algorithmic": basis,
+                     **({"l2_reduction": reduction} if bound == "hbm" else {})},
         "clocks": clk,
         "e2e": {"value": e2e_value, "unit": "TFLOP/s (README formula, fwd+bwd)",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e},
