@@ -53,6 +53,11 @@ WORKLOADS = {
     "c512_dg4": (32, 512, 32, 32, 512, 3, 1, 1, 1, 4, 2.0),
     "edge_k5": (4, 96, 97, 131, 160, 5, 2, 4, 2, 2, 8.0),
 }
+# stacks of DCN modules (offset/mask predicted by a plain 3x3 conv, ReLU between),
+# the global batch split over the ranks: one data-parallel training step per step
+STACKS = {
+    "stack3": {"global_batch": 256, "C": 256, "H": 64, "W": 64, "layers": 3, "k": 3, "off_std": 1.5},
+}
 DTYPES = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 RED_PEAK_TBS = 5.9  # fp32 L2 reduction rate of the scatter's access pattern, measured on a B200
@@ -194,6 +199,36 @@ def cpu_baseline(wl, budget_s=20.0):
             "sample": f"batch {bs} of {B} (fwd+bwd, float32), best of 2, {t:.3f} s per sample"}
 
 
+def cpu_torchvision(wl, budget_s=20.0):
+    """torchvision.ops.deform_conv2d on the host cores (float32, forward + backward) on a
+    bounded sample of the workload: the CPU path the benchmark configuration names."""
+    try:
+        import torchvision
+        from torchvision.ops import deform_conv2d
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"torchvision not importable: {e}"}
+    torch.set_num_threads(host_threads())
+    B, C, H, W, Co, k, s, p, d, dg, _ = wl
+    x, w, b, off, m, gy = make_inputs(wl, None, None, 0)
+
+    def one(bs):
+        xs, offs, ms = [t[:bs].clone().requires_grad_(True) for t in (x, off, m)]
+        ws, bias = w.clone().requires_grad_(True), b.clone().requires_grad_(True)
+        t0 = time.perf_counter()
+        y = deform_conv2d(xs, offs, ws, bias, stride=(s, s), padding=(p, p), dilation=(d, d), mask=ms)
+        y.backward(gy[:bs])
+        return time.perf_counter() - t0
+
+    t1 = one(1)
+    bs = int(max(1, min(B, (budget_s / 3) // max(t1, 1e-3))))
+    t = min(one(bs) for _ in range(2))
+    Ho, Wo = out_hw(H, W, k, s, p, d)
+    return {"value": 3 * readme_flops(bs, C, Ho, Wo, Co, k) / t / 1e12,
+            "unit": "TFLOP/s (README formula, fwd+bwd)", "cores": torch.get_num_threads(),
+            "kind": f"torchvision {torchvision.__version__} deform_conv2d (CPU)",
+            "sample": f"batch {bs} of {B} (fwd+bwd, float32), best of 2, {t:.3f} s per sample"}
+
+
 def run_reference(args, wl, rank):
     """--impl reference: the CPU port of the reference path on the host cores."""
     if rank != 0:
@@ -227,6 +262,203 @@ def run_reference(args, wl, rank):
     print(json.dumps(line), file=_JSON_OUT, flush=True)
 
 
+def make_timer(world, dev, stream, flush):
+    """Per-step CUDA events on `stream`, L2 flushed before every step (outside the
+    events), barrier before and after, max over ranks; returns ms per step."""
+    import torch.distributed as dist
+
+    def timed(fn, n):
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(n)]
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        for i in range(n):
+            flush.zero_()
+            ev[i][0].record(stream)
+            fn()
+            ev[i][1].record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ms = sum(a.elapsed_time(b_) for a, b_ in ev)
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item()) / n
+    return timed
+
+
+def run_stack(args):
+    """Data-parallel training step of a stack of DCN modules (the reference's `DCN`
+    module API: offset/mask predictor conv, sigmoid mask, DCNv2 op), ReLU between
+    layers, the global batch split over the ranks (strong scaling), every layer's
+    weight and bias gradients (the predictor's included) summed over the ranks with
+    one bucketed NCCL all-reduce."""
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    from dcnv2_b200 import _lib
+    from dcnv2_b200.dp import GradBucket
+    from dcnv2_b200.modules import DCN
+
+    cfg = STACKS[args.workload]
+    dtype = DTYPES[args.dtype]
+    G, C, H, W, L, k = cfg["global_batch"], cfg["C"], cfg["H"], cfg["W"], cfg["layers"], cfg["k"]
+    if G % world != 0:
+        raise SystemExit(f"global batch {G} does not split over {world} ranks")
+    Bl = G // world
+    torch.manual_seed(1234)                       # the same parameters on every rank
+    layers = [DCN(C, C, k, stride=1, padding=k // 2).to(dev) for _ in range(L)]
+    gen = torch.Generator().manual_seed(100 + rank)
+    x = torch.randn(Bl, C, H, W, generator=gen).to(dev, dtype)
+    gy = torch.randn(Bl, C, H, W, generator=gen).to(dev, dtype)
+    with torch.no_grad():
+        # predictor: random init scaled so the offsets have the configured std
+        h = x.float()
+        for lay in layers:
+            lay.conv_offset_mask.weight.normal_()
+            lay.conv_offset_mask.bias.zero_()
+            o = lay.conv_offset_mask(h)[:, : 2 * k * k]
+            lay.conv_offset_mask.weight.mul_(cfg["off_std"] / float(o.std()))
+            h = torch.relu(torch.nn.functional.conv2d(h, lay.weight, lay.bias, padding=k // 2))
+        for lay in layers:
+            lay.to(dtype)
+    bucket = GradBucket(layers)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    timed = make_timer(world, dev, stream, flush)
+
+    def step(xin, gin):
+        for lay in layers:
+            for prm in lay.parameters():
+                prm.grad = None
+        hh = xin
+        for i, lay in enumerate(layers):
+            hh = lay(hh)
+            if i + 1 < L:
+                hh = torch.relu(hh)
+        hh.backward(gin)
+        if world > 1:
+            bucket.allreduce(average=True)
+
+    for _ in range(args.warmup):
+        step(x, gy)
+    torch.cuda.synchronize()
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    clocks = ClockSampler(vis.split(",")[local] if vis else local)
+    clocks.start()
+    ms_step = timed(lambda: step(x, gy), args.steps)
+    _lib.trace_reset()
+    _lib.trace_enable(True)
+    timed(lambda: step(x, gy), args.steps)
+    _lib.trace_enable(False)
+    trace = _lib.trace_collect()
+    # end to end: the rank's inputs from pinned host memory, the last layer's weight
+    # gradient back to the host, every step
+    hx, hgy = x.cpu().pin_memory(), gy.cpu().pin_memory()
+    dx, dgy = torch.empty_like(x), torch.empty_like(gy)
+    hgw = torch.empty(layers[-1].weight.shape, dtype=dtype).pin_memory()
+
+    def e2e_step():
+        dx.copy_(hx, non_blocking=True)
+        dgy.copy_(hgy, non_blocking=True)
+        step(dx, dgy)
+        hgw.copy_(layers[-1].weight.grad, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    ms_e2e = timed(e2e_step, args.steps)
+    clk = clocks.stop()
+
+    flops_rank = L * 3 * readme_flops(Bl, C, H, W, C, k)
+    value = world * flops_rank / (ms_step * 1e-3) / 1e12
+    gflop = L * gemm_flops(Bl, C, H, W, C, k)   # one GEMM pass of every layer
+    layer_wl = (Bl, C, H, W, C, k, 1, k // 2, 1, 1, cfg["off_std"])
+    roofline, launches = roofline_of(trace, args.steps, layer_wl, dtype, L, args.workload, args.dtype)
+    kernels = {kname: (n, tot) for kname, (n, tot) in trace.items()}
+    line = {
+        "metric": "dcnv2_fwd_bwd_readme_tflops", "value": value,
+        "unit": "TFLOP/s (README formula, fwd+bwd of every DCN layer)", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": args.dtype, "data": "synthetic (seeded)",
+        "config": {"workload": f"{args.workload}: {L} x DCN({C},{C},{k}x{k},pad {k // 2}) + ReLU, "
+                               f"{H}x{W}, global batch {G}, {Bl} per rank, fwd+bwd+all-reduce",
+                   "global_batch": G, "parallelism": f"dp{world}",
+                   "l2": "flushed before every step (256 MiB write)", "offset_std_px": cfg["off_std"]},
+        "fwd_bwd_gemm_tflops": world * 3 * gflop / (ms_step * 1e-3) / 1e12,
+        "kernels_ms_per_step": {kk: v[1] / args.steps for kk, v in kernels.items()},
+        "roofline": roofline,
+        "clocks": clk,
+        "e2e": {"value": world * flops_rank / (ms_e2e * 1e-3) / 1e12,
+                "unit": "TFLOP/s (README formula, fwd+bwd of every DCN layer)",
+                "h2d_bytes_per_step": 2 * x.numel() * x.element_size(),
+                "d2h_bytes_per_step": hgw.numel() * hgw.element_size(), "ms_per_step": ms_e2e},
+        "gpu_launches": int(launches),
+    }
+    if rank == 0:
+        print(json.dumps(line), file=_JSON_OUT, flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def roofline_of(trace, steps, wl, dtype, layers_per_step, workload, dtype_name):
+    """Roofline of the dominant kernel of a traced run: the tensor-core kernels against
+    the measured bf16 dense peak with the algorithmic FLOPs of one GEMM pass; the SIMT
+    scatter against the measured HBM copy bandwidth with its algorithmic bytes (and
+    against the measured L2 reduction rate).  `wl` is one layer's shape; a step runs
+    `layers_per_step` such layers.  Returns (roofline, library launches in the run)."""
+    B, C, H, W, Co, k, s, p, d, dg, _ = wl
+    Ho, Wo = out_hw(H, W, k, s, p, d)
+    peaks, peak_kind = load_peaks()
+    kernels = {kname: (n, tot) for kname, (n, tot) in trace.items()}
+    dom = max(kernels, key=lambda kk: kernels[kk][1])
+    n_dom, tot_dom = kernels[dom]
+    per_launch_ms = tot_dom / n_dom
+    launches_per_layer = n_dom / steps / layers_per_step   # > 1 when the backward runs in chunks
+    esz = torch.tensor([], dtype=dtype).element_size()
+    K2 = k * k
+    extra = {}
+    if dom in ("forward", "backward_data", "backward_weight"):
+        gflop = gemm_flops(B, C, Ho, Wo, Co, k) / launches_per_layer
+        work, bound, unit, peak = gflop, "tensor", "TFLOP/s", peaks["bf16_tflops"]
+        basis = f"2*Co*C*k*k*B*Ho*Wo = {gflop:.4g} FLOP per launch"
+        achieved = work / (per_launch_ms * 1e-3) / 1e12
+    else:
+        # scatter: read gcol (P*K2*C), x (B*C*H*W), offset+mask (3*K2*P); read+write the
+        # fp32 grad_input accumulator (2 * 4*B*C*H*W); write grad_offset+grad_mask (3*K2*P)
+        # and the sampled columns for the weight gradient (P*K2*C operands, hi+lo for f32)
+        P = B * Ho * Wo
+        nsplit = 2 if esz == 4 else 1
+        nbytes = (P * K2 * C * esz + B * C * H * W * esz + 6 * K2 * P * esz + 8 * B * C * H * W
+                  + P * K2 * C * 2 * nsplit) / launches_per_layer
+        work, bound, unit, peak = nbytes, "hbm", "GB/s", peaks["hbm_gbs"]
+        basis = (f"algorithmic bytes {nbytes:.4g} per launch (gcol, x, offset/mask, fp32 grad_input acc, "
+                 "outputs, columns)")
+        achieved = work / (per_launch_ms * 1e-3) / 1e9
+        # the scatter's real limiter: fp32 reductions into L2 (4 corners x C x 4 B per
+        # pixel and tap) against the rate a microbenchmark of the same access pattern
+        # sustains on this B200 (red.global.add.v4.f32, random target pixels)
+        red_bytes = P * K2 * 4 * C * 4 / launches_per_layer
+        red_tbs = red_bytes / (per_launch_ms * 1e-3) / 1e12
+        extra["l2_reduction"] = {
+            "achieved": red_tbs, "peak": RED_PEAK_TBS, "unit": "TB/s", "frac": red_tbs / RED_PEAK_TBS,
+            "bytes_per_launch": red_bytes,
+            "peak_source": "microbenchmark of red.global.add.v4.f32 with random targets on this B200"}
+    roofline = {"kernel": dom, "bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
+                "frac": achieved / peak,
+                "peak_source": f"{peak_kind} ({'bf16 dense, burst' if bound == 'tensor' else 'HBM copy'})",
+                "traffic": load_traffic(dom, workload, dtype_name), "algorithmic": basis, **extra}
+    # library kernels in the traced run (the accumulator memset is a runtime call)
+    launches = sum(n for kk, (n, _) in kernels.items() if kk != "zero_accumulators")
+    return roofline, launches
+
+
 def config_of(args, wl):
     B, C, H, W, Co, k, s, p, d, dg, off_std = wl
     return {"workload": f"{args.workload}: B={B}/gpu C={C} {H}x{W} Co={Co} {k}x{k} s{s} p{p} "
@@ -242,12 +474,20 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--dtype", default="bf16", choices=list(DTYPES))
-    ap.add_argument("--workload", default="readme", choices=list(WORKLOADS))
+    ap.add_argument("--workload", default="readme", choices=list(WORKLOADS) + list(STACKS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--launch-only", type=int, default=0, metavar="N",
                     help="run N forward+backward calls without timing and exit (for ncu)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    if args.workload in STACKS:
+        if args.impl == "reference":
+            if int(os.environ.get("RANK", "0")) == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "the stack workloads have no CPU "
+                                  "reference arm; use the single-layer workloads"}), file=_JSON_OUT, flush=True)
+            return
+        run_stack(args)
+        return
     wl = WORKLOADS[args.workload]
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -351,45 +591,9 @@ def main():
     value = world * step_flops / (ms_step * 1e-3) / 1e12
     e2e_value = world * step_flops / (ms_e2e * 1e-3) / 1e12
 
-    # roofline of the dominant kernel: tensor kernels against the measured bf16
-    # dense peak with the algorithmic FLOPs of one GEMM pass; the SIMT scatter
-    # against the measured HBM copy bandwidth with its algorithmic bytes
-    peaks, peak_kind = load_peaks()
+    roofline, launches = roofline_of(trace, args.steps, wl, dtype, 1, args.workload, args.dtype)
     kernels = {kname: (n, tot) for kname, (n, tot) in trace.items()}
-    dom = max(kernels, key=lambda kk: kernels[kk][1])
-    n_dom, tot_dom = kernels[dom]
-    per_launch_ms = tot_dom / n_dom
     gflop = gemm_flops(B, C, Ho, Wo, Co, k)
-    esz = torch.tensor([], dtype=dtype).element_size()
-    K2 = k * k
-    if dom in ("forward", "backward_data", "backward_weight"):
-        work, bound, unit, peak = gflop, "tensor", "TFLOP/s", peaks["bf16_tflops"]
-        basis = f"2*Co*C*k*k*B*Ho*Wo = {gflop:.4g} FLOP per launch"
-        achieved = work / (per_launch_ms * 1e-3) / 1e12
-    else:
-        # scatter: read gcol (P*K2*C), x (B*C*H*W), offset+mask (3*K2*P); read+write the
-        # fp32 grad_input accumulator (2 * 4*B*C*H*W); write grad_offset+grad_mask (3*K2*P)
-        # and the sampled columns for the weight gradient (P*K2*C operands, hi+lo for f32)
-        P = B * Ho * Wo
-        nsplit = 2 if esz == 4 else 1
-        nbytes = (P * K2 * C * esz + B * C * H * W * esz + 6 * K2 * P * esz + 8 * B * C * H * W
-                  + P * K2 * C * 2 * nsplit)
-        nbytes /= n_dom / args.steps  # per launch (the scatter may run in chunks)
-        work, bound, unit, peak = nbytes, "hbm", "GB/s", peaks["hbm_gbs"]
-        basis = f"algorithmic bytes {nbytes:.4g} per launch (gcol, x, offset/mask, fp32 grad_input acc, outputs, columns)"
-        achieved = work / (per_launch_ms * 1e-3) / 1e9
-        # the scatter's real limiter: fp32 reductions into L2 (4 corners x C x 4 B per
-        # pixel and tap) against the rate a microbenchmark of the same access pattern
-        # sustains on this B200 (red.global.add.v4.f32, random target pixels)
-        red_bytes = P * K2 * 4 * C * 4 / (n_dom / args.steps)
-        red_tbs = red_bytes / (per_launch_ms * 1e-3) / 1e12
-        reduction = {"achieved": red_tbs, "peak": RED_PEAK_TBS, "unit": "TB/s", "frac": red_tbs / RED_PEAK_TBS,
-                     "bytes_per_launch": red_bytes,
-                     "peak_source": "microbenchmark of red.global.add.v4.f32 with random targets on this B200"}
-    traffic = load_traffic(dom, args.workload, args.dtype)
-    # kernels of this library per timed step (counted in the traced pass, which runs
-    # the same steps; the accumulator memset is a runtime call)
-    launches = sum(n for kk, (n, _) in kernels.items() if kk != "zero_accumulators")
 
     line = {
         "metric": "dcnv2_fwd_bwd_readme_tflops", "value": value,
@@ -398,14 +602,10 @@ def main():
         "scaling": "weak", "vs_baseline": None, "dtype": args.dtype, "data": "synthetic (seeded)",
         "config": config_of(args, wl),
         "fwd_ms": ms_fwd, "fwd_readme_tflops": readme_flops(B, C, Ho, Wo, Co, k) / (ms_fwd * 1e-3) / 1e12,
-        "fwd_bwd_gemm_tflops": 3 * gflop / (ms_step * 1e-3) / 1e12,
+        "fwd_bwd_gemm_tflops": world * 3 * gflop / (ms_step * 1e-3) / 1e12,
         "kernels_ms_per_step": {kk: v[1] / args.steps for kk, v in kernels.items()},
         "ms_per_step_traced": ms_step_traced,
-        "roofline": {"kernel": dom, "bound": bound, "achieved": achieved, "peak": peak,
-                     "unit": unit, "frac": achieved / peak,
-                     "peak_source": f"{peak_kind} ({'bf16 dense, burst' if bound == 'tensor' else 'HBM copy'})",
-                     "traffic": traffic, "algorithmic": basis,
-                     **({"l2_reduction": reduction} if bound == "hbm" else {})},
+        "roofline": roofline,
         "clocks": clk,
         "e2e": {"value": e2e_value, "unit": "TFLOP/s (README formula, fwd+bwd)",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e},
@@ -413,6 +613,7 @@ def main():
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(wl)
+        line["cpu_torchvision"] = cpu_torchvision(wl)
     if rank == 0:
         print(json.dumps(line), file=_JSON_OUT, flush=True)
     if world > 1:
