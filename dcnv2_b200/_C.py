@@ -140,6 +140,68 @@ def dcn_v2_backward(input: torch.Tensor, weight: torch.Tensor, mask: torch.Tenso
     return [gi, goff, gm, gw, gb if has_bias else None]
 
 
+def dcn_v2_forward_om(input: torch.Tensor, weight: torch.Tensor, offset_mask: torch.Tensor,
+                      bias: Optional[torch.Tensor], stride_h: int, stride_w: int, pad_h: int, pad_w: int,
+                      dilation_h: int = 1, dilation_w: int = 1, deformable_groups: int = 1) -> torch.Tensor:
+    """Forward fed by the raw predictor output [B, 3*dg*K2, Ho, Wo]: offsets in the
+    first 2*dg*K2 channels, mask logits (sigmoid applied in the kernel) in the rest;
+    the same result as ``dcn_v2_forward`` with the reference module's chunk / cat /
+    sigmoid (dcn_v2_mm.py:133-137) done in the operator."""
+    _check_cuda(input=input, weight=weight, bias=bias, offset_mask=offset_mask)
+    d, Ho, Wo = _desc(input, weight, stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w,
+                      deformable_groups, bias is not None)
+    B, dg, K2 = input.shape[0], deformable_groups, weight.shape[2] * weight.shape[3]
+    dt = input.dtype
+    input = input.contiguous()
+    weight = _prep(weight, dt, "weight")
+    offset_mask = _prep(offset_mask, dt, "offset_mask", (B, 3 * dg * K2, Ho, Wo))
+    if bias is not None:
+        bias = _prep(bias, dt, "bias", (weight.shape[0],))
+    with torch.cuda.device(input.device):
+        out = torch.empty((B, weight.shape[0], Ho, Wo), dtype=dt, device=input.device)
+        nbytes = _lib.lib.dcn_forward_workspace_size(ctypes.byref(d))
+        ws = torch.empty((max(nbytes, 256),), dtype=torch.uint8, device=input.device)
+        stream = torch.cuda.current_stream(input.device).cuda_stream
+        _check(_lib.lib.dcn_forward_om(ctypes.byref(d), _ptr(input), _ptr(weight), _ptr(offset_mask),
+                                       _ptr(bias), _ptr(out), _ptr(ws), ws.numel(), ctypes.c_void_p(stream)))
+        if _CHECK:
+            _check_device(ws)
+    return out
+
+
+def dcn_v2_backward_om(input: torch.Tensor, weight: torch.Tensor, offset_mask: torch.Tensor,
+                       bias: Optional[torch.Tensor], grad_output: torch.Tensor, stride_h: int,
+                       stride_w: int, pad_h: int, pad_w: int, dilation_h: int = 1, dilation_w: int = 1,
+                       deformable_groups: int = 1) -> List[torch.Tensor]:
+    """[grad_input, grad_offset_mask, grad_weight, grad_bias] of ``dcn_v2_forward_om``;
+    grad_offset_mask holds the offset gradients and the mask-logit gradients."""
+    _check_cuda(input=input, weight=weight, bias=bias, offset_mask=offset_mask, grad_output=grad_output)
+    has_bias = bias is not None
+    d, Ho, Wo = _desc(input, weight, stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w,
+                      deformable_groups, True)
+    B, dg, K2 = input.shape[0], deformable_groups, weight.shape[2] * weight.shape[3]
+    Co = weight.shape[0]
+    dt = input.dtype
+    input = input.contiguous()
+    weight = _prep(weight, dt, "weight")
+    offset_mask = _prep(offset_mask, dt, "offset_mask", (B, 3 * dg * K2, Ho, Wo))
+    grad_output = _prep(grad_output, dt, "grad_output", (B, Co, Ho, Wo))
+    with torch.cuda.device(input.device):
+        gi = torch.empty_like(input)
+        gom = torch.empty_like(offset_mask)
+        gw = torch.empty_like(weight)
+        gb = torch.empty((Co,), dtype=dt, device=input.device)
+        nbytes = _lib.lib.dcn_backward_workspace_size(ctypes.byref(d))
+        ws = torch.empty((max(nbytes, 256),), dtype=torch.uint8, device=input.device)
+        stream = torch.cuda.current_stream(input.device).cuda_stream
+        _check(_lib.lib.dcn_backward_om(ctypes.byref(d), _ptr(input), _ptr(weight), _ptr(offset_mask),
+                                        _ptr(bias), _ptr(grad_output), _ptr(gi), _ptr(gom), _ptr(gw),
+                                        _ptr(gb), _ptr(ws), ws.numel(), ctypes.c_void_p(stream)))
+        if _CHECK:
+            _check_device(ws)
+    return [gi, gom, gw, gb if has_bias else None]
+
+
 def read_device_status(workspace: torch.Tensor) -> int:
     """Synchronises the current stream and returns (and clears) the device error bits."""
     stream = torch.cuda.current_stream(workspace.device).cuda_stream

@@ -7,6 +7,6 @@ Drop-in for the reference's ``Conv2d._C`` ops and ``dcn_v2_mm`` modules:
 """
 from . import _C  # noqa: F401  (loads libdcn_b200.so; raises ImportError if it is not built)
 from ._lib import version  # noqa: F401
-from .modules import DCN, DCNv2, _DCNv2, dcn_v2_conv  # noqa: F401
+from .modules import DCN, DCNv2, _DCNv2, dcn_v2_conv, dcn_v2_conv_om  # noqa: F401
 
-__all__ = ["_C", "DCN", "DCNv2", "dcn_v2_conv", "version"]
+__all__ = ["_C", "DCN", "DCNv2", "dcn_v2_conv", "dcn_v2_conv_om", "version"]

@@ -24,6 +24,8 @@ EXPORTS = (
     "dcn_backward_workspace_size",
     "dcn_forward",
     "dcn_backward",
+    "dcn_forward_om",
+    "dcn_backward_om",
     "dcn_read_device_status",
     "dcn_strerror",
     "dcn_version",
@@ -66,6 +68,10 @@ def _load() -> ctypes.CDLL:
     lib.dcn_forward.restype = ctypes.c_int
     lib.dcn_backward.argtypes = [dp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, sz, vp]
     lib.dcn_backward.restype = ctypes.c_int
+    lib.dcn_forward_om.argtypes = [dp, vp, vp, vp, vp, vp, vp, sz, vp]
+    lib.dcn_forward_om.restype = ctypes.c_int
+    lib.dcn_backward_om.argtypes = [dp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, sz, vp]
+    lib.dcn_backward_om.restype = ctypes.c_int
     lib.dcn_read_device_status.argtypes = [vp, vp]
     lib.dcn_read_device_status.restype = ctypes.c_int
     lib.dcn_strerror.argtypes = [ctypes.c_int]

@@ -243,6 +243,9 @@ int make_plan(const dcn_desc* d, Plan* p, int num_sms) {
   p->fd_kw = make_fastdiv((uint32_t)p->kw);
   p->fd_dg = make_fastdiv((uint32_t)p->dg);
   p->fd_ntg = make_fastdiv((uint32_t)(p->K2 * p->dg));
+  p->off_bs = 2 * p->dg * p->K2 * p->HoWo;
+  p->msk_bs = p->dg * p->K2 * p->HoWo;
+  p->mask_logit = 0;
   return DCN_OK;
 }
 
@@ -277,12 +280,19 @@ size_t dcn_backward_workspace_size(const dcn_desc* d) {
   return make_plan(d, &p, device_sms()) == DCN_OK ? p.bwd_bytes : 0;
 }
 
-int dcn_forward(const dcn_desc* d, const void* input, const void* weight, const void* mask,
-                const void* offset, const void* bias, void* output, void* workspace,
-                size_t workspace_bytes, void* stream) {
+// om != 0: `offset` is the predictor output [B][3*dg*K2][Ho][Wo] (offsets in
+// channels 0 .. 2*dg*K2-1, mask logits after them) and `mask` is ignored.
+static int forward_impl(const dcn_desc* d, const void* input, const void* weight, const void* mask,
+                        const void* offset, const void* bias, void* output, void* workspace,
+                        size_t workspace_bytes, void* stream, int om) {
   Plan P;
   int rc = make_plan(d, &P, device_sms());
   if (rc != DCN_OK) return rc;
+  if (om) {
+    P.off_bs = P.msk_bs = 3 * P.dg * P.K2 * P.HoWo;
+    P.mask_logit = 1;
+    mask = offset ? static_cast<const uint8_t*>(offset) + (size_t)2 * P.dg * P.K2 * P.HoWo * P.esz : nullptr;
+  }
   if (!workspace) return DCN_E_NULLPTR;
   if (workspace_bytes < P.fwd_bytes || ((uintptr_t)workspace & (kWsAlign - 1)) != 0)
     return DCN_E_WORKSPACE;
@@ -334,14 +344,24 @@ int dcn_forward(const dcn_desc* d, const void* input, const void* weight, const 
   return rc;
 }
 
-int dcn_backward(const dcn_desc* d, const void* input, const void* weight, const void* mask,
-                 const void* offset, const void* bias, const void* grad_output, void* grad_input,
-                 void* grad_offset, void* grad_mask, void* grad_weight, void* grad_bias,
-                 void* workspace, size_t workspace_bytes, void* stream) {
+// om != 0: `offset` / `grad_offset` are the predictor output and its gradient
+// (grad_offset then receives the gradient of the mask logits in its last dg*K2
+// channels); `mask` / `grad_mask` are ignored.
+static int backward_impl(const dcn_desc* d, const void* input, const void* weight, const void* mask,
+                         const void* offset, const void* bias, const void* grad_output, void* grad_input,
+                         void* grad_offset, void* grad_mask, void* grad_weight, void* grad_bias,
+                         void* workspace, size_t workspace_bytes, void* stream, int om) {
   (void)bias;
   Plan P;
   int rc = make_plan(d, &P, device_sms());
   if (rc != DCN_OK) return rc;
+  if (om) {
+    const size_t mofs = (size_t)2 * P.dg * P.K2 * P.HoWo * P.esz;
+    P.off_bs = P.msk_bs = 3 * P.dg * P.K2 * P.HoWo;
+    P.mask_logit = 1;
+    mask = offset ? static_cast<const uint8_t*>(offset) + mofs : nullptr;
+    grad_mask = grad_offset ? static_cast<uint8_t*>(grad_offset) + mofs : nullptr;
+  }
   if (!weight || !grad_weight || !workspace) return DCN_E_NULLPTR;
   if (P.totalP > 0 && (!input || !mask || !offset || !grad_output || !grad_input ||
                        !grad_offset || !grad_mask))
@@ -476,6 +496,35 @@ int dcn_backward(const dcn_desc* d, const void* input, const void* weight, const
   }
   TraceScope ts(TR_FINISH_GRAD_WEIGHT, s);
   return launch_finish_grad_weight(P, gw, gb, grad_weight, d->has_bias ? grad_bias : nullptr, s);
+}
+
+int dcn_forward(const dcn_desc* d, const void* input, const void* weight, const void* mask,
+                const void* offset, const void* bias, void* output, void* workspace,
+                size_t workspace_bytes, void* stream) {
+  return forward_impl(d, input, weight, mask, offset, bias, output, workspace, workspace_bytes, stream, 0);
+}
+
+int dcn_backward(const dcn_desc* d, const void* input, const void* weight, const void* mask,
+                 const void* offset, const void* bias, const void* grad_output, void* grad_input,
+                 void* grad_offset, void* grad_mask, void* grad_weight, void* grad_bias,
+                 void* workspace, size_t workspace_bytes, void* stream) {
+  return backward_impl(d, input, weight, mask, offset, bias, grad_output, grad_input, grad_offset,
+                       grad_mask, grad_weight, grad_bias, workspace, workspace_bytes, stream, 0);
+}
+
+int dcn_forward_om(const dcn_desc* d, const void* input, const void* weight, const void* offset_mask,
+                   const void* bias, void* output, void* workspace, size_t workspace_bytes, void* stream) {
+  return forward_impl(d, input, weight, nullptr, offset_mask, bias, output, workspace, workspace_bytes,
+                      stream, 1);
+}
+
+int dcn_backward_om(const dcn_desc* d, const void* input, const void* weight, const void* offset_mask,
+                    const void* bias, const void* grad_output, void* grad_input, void* grad_offset_mask,
+                    void* grad_weight, void* grad_bias, void* workspace, size_t workspace_bytes,
+                    void* stream) {
+  return backward_impl(d, input, weight, nullptr, offset_mask, bias, grad_output, grad_input,
+                       grad_offset_mask, nullptr, grad_weight, grad_bias, workspace, workspace_bytes,
+                       stream, 1);
 }
 
 int dcn_read_device_status(void* workspace, void* stream) {

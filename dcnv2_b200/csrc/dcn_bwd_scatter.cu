@@ -89,8 +89,8 @@ __global__ void __launch_bounds__(kThreads, 3) dcn_bwd_scatter_kernel(const __gr
     const bool mpv = mpix < pend;
     const int mb = mpv ? fdiv(mpix, P.fd_howo) : 0;
     const int mp = mpv ? mpix - mb * HoWo : 0;
-    const int obase = ((mb * P.dg + g) * 2 * P.K2 + 2 * t) * HoWo + mp;
-    const int mbase = ((mb * P.dg + g) * P.K2 + t) * HoWo + mp;
+    const int obase = mb * P.off_bs + (g * 2 * P.K2 + 2 * t) * HoWo + mp;
+    const int mbase = mb * P.msk_bs + (g * P.K2 + t) * HoWo + mp;
     float mlh = 0.f, mlw = 0.f, mm = 0.f;
     int mgidx = 0;
     uint32_t mval = 0u;
@@ -100,6 +100,7 @@ __global__ void __launch_bounds__(kThreads, 3) dcn_bwd_scatter_kernel(const __gr
       const float h = (float)(ho * P.sh - P.ph + i * P.dh) + ldf(off + obase);
       const float w = (float)(wo * P.sw - P.pw + j * P.dw) + ldf(off + obase + HoWo);
       mm = ldf(msk + mbase);
+      if (P.mask_logit) mm = 1.f / (1.f + __expf(-mm));   // sigmoid of a predictor logit
       const float hf = floorf(h), wf = floorf(w);
       const int hl = (int)hf, wl = (int)wf;
       mlh = h - hf;
@@ -235,7 +236,8 @@ __global__ void __launch_bounds__(kThreads, 3) dcn_bwd_scatter_kernel(const __gr
     if (mpv) {
       goff[obase] = Elem<T>::from_f(oh * mm);
       goff[obase + HoWo] = Elem<T>::from_f(ow * mm);
-      gmsk[mbase] = Elem<T>::from_f(om);
+      // with logits: d/dx sigmoid(x) = s (1 - s)
+      gmsk[mbase] = Elem<T>::from_f(P.mask_logit ? om * mm * (1.f - mm) : om);
     }
   }
 }

@@ -146,10 +146,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       if (pv && slot < wt) {
         const int tgi = tg0 + slot;
         const int t = fdiv(tgi, P.fd_dg), gi = tgi - t * P.dg;
-        const int ob = ((b * P.dg + gi) * 2 * P.K2 + 2 * t) * HoWo + p;
+        const int ob = b * P.off_bs + (gi * 2 * P.K2 + 2 * t) * HoWo + p;
         rh[k] = ldg_raw<T>(off + ob);
         rw[k] = ldg_raw<T>(off + ob + HoWo);
-        rm[k] = ldg_raw<T>(msk + ((b * P.dg + gi) * P.K2 + t) * HoWo + p);
+        rm[k] = ldg_raw<T>(msk + b * P.msk_bs + (gi * P.K2 + t) * HoWo + p);
       }
     }
 #pragma unroll
@@ -162,7 +162,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           const int i = fdiv(t, P.fd_kw), j = t - i * P.kw;
           const float hs = (float)(ho * P.sh - P.ph + i * P.dh) + raw_to_f<T>(rh[k]);
           const float ws = (float)(wo * P.sw - P.pw + j * P.dw) + raw_to_f<T>(rw[k]);
-          r = make_pixgeo_clamped(b * HW, hs, ws, raw_to_f<T>(rm[k]), P.H, P.W);
+          float mv = raw_to_f<T>(rm[k]);
+          if (P.mask_logit) mv = 1.f / (1.f + __expf(-mv));   // sigmoid of a predictor logit
+          r = make_pixgeo_clamped(b * HW, hs, ws, mv, P.H, P.W);
         }
         const int e = (buf * kGeoTaps + slot) * kTileM + row;
         sgeo_idx[e] = (int)((unsigned)r.gidx * (unsigned)P.CS);   // element offset of the corner line

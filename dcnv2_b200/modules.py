@@ -49,6 +49,37 @@ class _DCNv2(Function):
 dcn_v2_conv = _DCNv2.apply
 
 
+class _DCNv2OM(Function):
+    """Autograd glue of the fused predictor path: input, weight, the predictor's raw
+    output (offsets, then mask logits) and bias; the gradient of the raw output goes
+    straight back into the predictor conv."""
+
+    @staticmethod
+    def forward(ctx, input, weight, offset_mask, bias, stride, padding, dilation=1,
+                deformable_groups=1):
+        ctx.stride = _pair(stride)
+        ctx.padding = _pair(padding)
+        ctx.dilation = _pair(dilation)
+        ctx.deformable_groups = int(deformable_groups)
+        output = _C.dcn_v2_forward_om(input, weight, offset_mask, bias, ctx.stride[0], ctx.stride[1],
+                                      ctx.padding[0], ctx.padding[1], ctx.dilation[0], ctx.dilation[1],
+                                      ctx.deformable_groups)
+        ctx.save_for_backward(input, weight, offset_mask, bias)
+        return output
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, grad_output):
+        input, weight, offset_mask, bias = ctx.saved_tensors
+        grad_input, grad_om, grad_weight, grad_bias = _C.dcn_v2_backward_om(
+            input, weight, offset_mask, bias, grad_output, ctx.stride[0], ctx.stride[1],
+            ctx.padding[0], ctx.padding[1], ctx.dilation[0], ctx.dilation[1], ctx.deformable_groups)
+        return (grad_input, grad_weight, grad_om, grad_bias, None, None, None, None)
+
+
+dcn_v2_conv_om = _DCNv2OM.apply
+
+
 class DCNv2(nn.Module):
     """Modulated deformable conv taking external offset and mask (dcn_v2_mm.py:59-102)."""
 
@@ -100,9 +131,8 @@ class DCN(DCNv2):
         self.conv_offset_mask.bias.data.zero_()
 
     def forward(self, input):
+        # the predictor's output goes to the operator as it is: the reference's
+        # chunk / cat / sigmoid (dcn_v2_mm.py:133-137) happen inside the kernels
         out = self.conv_offset_mask(input)
-        o1, o2, mask = torch.chunk(out, 3, dim=1)
-        offset = torch.cat((o1, o2), dim=1)
-        mask = torch.sigmoid(mask)
-        return dcn_v2_conv(input, self.weight, mask, offset, self.bias, self.stride, self.padding,
-                           self.dilation, self.deformable_groups)
+        return dcn_v2_conv_om(input, self.weight, out, self.bias, self.stride, self.padding,
+                              self.dilation, self.deformable_groups)

@@ -98,6 +98,24 @@ DCN_API int dcn_backward(const dcn_desc* d, const void* input, const void* weigh
                  void* grad_offset, void* grad_mask, void* grad_weight, void* grad_bias,
                  void* workspace, size_t workspace_bytes, void* stream);
 
+/* DCNv2 fed by the raw output of the offset/mask predictor conv.  Replaces the
+ * reference module's chunk / cat / sigmoid between its predictor and the op
+ * (dcn_v2_mm.py:133-137, DCN.forward): offset_mask is [B][3*dg*K2][Ho][Wo],
+ * channels 0 .. 2*dg*K2-1 are the offsets in the op's order (the reference's
+ * cat(o1, o2)) and channels 2*dg*K2 .. 3*dg*K2-1 the mask logits, which the
+ * kernels pass through a sigmoid.  Same workspace and result as dcn_forward. */
+DCN_API int dcn_forward_om(const dcn_desc* d, const void* input, const void* weight,
+                           const void* offset_mask, const void* bias, void* output, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
+/* Gradients of dcn_forward_om: grad_offset_mask has the layout of offset_mask
+ * (offset gradients, then the gradients of the mask logits, i.e. grad_mask *
+ * s * (1 - s) with s the sigmoid); the other outputs as dcn_backward. */
+DCN_API int dcn_backward_om(const dcn_desc* d, const void* input, const void* weight,
+                            const void* offset_mask, const void* bias, const void* grad_output,
+                            void* grad_input, void* grad_offset_mask, void* grad_weight, void* grad_bias,
+                            void* workspace, size_t workspace_bytes, void* stream);
+
 /* Forward pass that allocates nothing and takes no workspace.  No counterpart
  * in the reference.  For callers that may not allocate GPU memory at all (code
  * running while a framework records a stream into a graph and forbids
