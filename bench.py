@@ -350,13 +350,31 @@ def run_stack(args):
     for _ in range(args.warmup):
         step(x, gy)
     torch.cuda.synchronize()
+    run_step = lambda: step(x, gy)  # noqa: E731
+    if args.graph:
+        # the whole step (predictor convs, DCN kernels, autograd, all-reduce) as one
+        # CUDA graph replayed on the launching stream; x and gy are its static inputs
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                step(x, gy)
+        stream.wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step(x, gy)
+        torch.cuda.synchronize()
+        run_step = graph.replay
+        for _ in range(args.warmup):
+            run_step()
+        torch.cuda.synchronize()
     vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
     clocks = ClockSampler(vis.split(",")[local] if vis else local)
     clocks.start()
-    ms_step = timed(lambda: step(x, gy), args.steps)
+    ms_step = timed(run_step, args.steps)
     _lib.trace_reset()
     _lib.trace_enable(True)
-    timed(lambda: step(x, gy), args.steps)
+    timed(lambda: step(x, gy), args.steps)   # eager (the trace records library launches)
     _lib.trace_enable(False)
     trace = _lib.trace_collect()
     # end to end: the rank's inputs from pinned host memory, the last layer's weight
@@ -366,9 +384,14 @@ def run_stack(args):
     hgw = torch.empty(layers[-1].weight.shape, dtype=dtype).pin_memory()
 
     def e2e_step():
-        dx.copy_(hx, non_blocking=True)
-        dgy.copy_(hgy, non_blocking=True)
-        step(dx, dgy)
+        if args.graph:   # the graph's static inputs receive the copies
+            x.copy_(hx, non_blocking=True)
+            gy.copy_(hgy, non_blocking=True)
+            run_step()
+        else:
+            dx.copy_(hx, non_blocking=True)
+            dgy.copy_(hgy, non_blocking=True)
+            step(dx, dgy)
         hgw.copy_(layers[-1].weight.grad, non_blocking=True)
 
     for _ in range(2):
@@ -390,7 +413,8 @@ def run_stack(args):
         "config": {"workload": f"{args.workload}: {L} x DCN({C},{C},{k}x{k},pad {k // 2}) + ReLU, "
                                f"{H}x{W}, global batch {G}, {Bl} per rank, fwd+bwd+all-reduce",
                    "global_batch": G, "parallelism": f"dp{world}",
-                   "l2": "flushed before every step (256 MiB write)", "offset_std_px": cfg["off_std"]},
+                   "l2": "flushed before every step (256 MiB write)", "offset_std_px": cfg["off_std"],
+                   "cuda_graph": bool(args.graph)},
         "fwd_bwd_gemm_tflops": world * 3 * gflop / (ms_step * 1e-3) / 1e12,
         "kernels_ms_per_step": {kk: v[1] / args.steps for kk, v in kernels.items()},
         "roofline": roofline,
@@ -476,6 +500,8 @@ def main():
     ap.add_argument("--dtype", default="bf16", choices=list(DTYPES))
     ap.add_argument("--workload", default="readme", choices=list(WORKLOADS) + list(STACKS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--graph", action="store_true",
+                    help="stack workloads: capture the training step in a CUDA graph and replay it")
     ap.add_argument("--launch-only", type=int, default=0, metavar="N",
                     help="run N forward+backward calls without timing and exit (for ncu)")
     args = ap.parse_args()
