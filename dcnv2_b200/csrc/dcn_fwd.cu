@@ -5,7 +5,8 @@
 //   D[pixel, co] = sum_{t, g, c} A[pixel, (t,g,c)] * Wt[co, (t,g,c)]
 //   A[pixel, (t,g,c)] = mask * bilinear(x_nhwc[b, :, :, g, c], pos(pixel, t) + offset)
 //
-// CTA roles (896 threads, one CTA per SM, persistent over (pixel, Co) tiles):
+// CTA roles (896 threads for 16-bit types, one CTA per SM, persistent over
+// (pixel, Co) tiles; f32 uses 8 producer warps of 16 rows, 640 threads):
 //   warps 0-15  gather producers: 8 pixel rows per warp, 8 lanes per pixel so
 //               each warp-wide load reads whole corner lines; build the A tile
 //               (128 pixels x 64 channels, K-major, 128B swizzle) in smem
@@ -14,7 +15,8 @@
 //               and the four weights x mask per row and tap) in shared memory
 //   warp 24     bulk-copy (TMA) producer of the pre-packed weight tile
 //   warp 25     TMEM owner and single-thread tcgen05.mma issuer (warps 26-27 idle)
-// Registers are moved with setmaxnreg (producers 80, epilogue 64, control 32).
+// Registers are moved with setmaxnreg (producers 80 (f32: 160), epilogue 64,
+// control 32).
 // A/B stages form an mbarrier ring; the accumulator is double-buffered in TMEM so
 // the epilogue of tile i overlaps the main loop of tile i+1.
 #include <stdlib.h>
@@ -34,24 +36,36 @@ namespace {
 
 constexpr int kMaxCo = 2048;  // bias staged in smem: Co up to 2048
 constexpr int kGeoTaps = 9;   // (tap, group)s per geometry window
-constexpr int kProdWarps = 16;                       // gather producers (4 warpgroups)
-constexpr int kProdThreads = kProdWarps * 32;
-constexpr int kRowsPerWarp = kTileM / kProdWarps;    // A-tile rows per producer warp
-constexpr int kEpiWarp0 = kProdWarps;
-constexpr int kEpiWarps = 8;                         // two per TMEM lane quarter
-constexpr int kTmaWarp = kEpiWarp0 + kEpiWarps;
-constexpr int kMmaWarp = kTmaWarp + 1;
-constexpr int kFwdThreads = (kTmaWarp + 4) * 32;     // 7 warpgroups (896); the last two warps idle
-constexpr int kLaunchRegs = 72;                      // 65536 / 896, rounded down to a multiple of 8
-// setmaxnreg split of the launch pool (896 x 72 = 64512):
-// producers 4 x 128 x 80 + epilogue 2 x 128 x 64 + control 128 x 32 = 61440
-constexpr int kProdRegs = 80, kEpiRegs = 64, kCtlRegs = 32;
-static_assert(kProdThreads * kProdRegs + kEpiWarps * 32 * kEpiRegs + 128 * kCtlRegs <= kFwdThreads * kLaunchRegs,
-              "register split exceeds the launch pool");
+// Warp layout of the CTA for PW gather-producer warps: PW/4 producer warpgroups,
+// two epilogue warpgroups, one control warpgroup (weight copies, MMA, two idle
+// warps).  16-bit types use 16 producer warps of 8 rows at 80 registers, f32 (two
+// 16-byte loads per corner slice) 8 warps of 16 rows at 160 registers.
+template <int PW>
+struct FwdLayout {
+  static constexpr int kProdWarps = PW;
+  static constexpr int kProdThreads = PW * 32;
+  static constexpr int kRowsPerWarp = kTileM / PW;       // A-tile rows per producer warp
+  static constexpr int kEpiWarp0 = PW;
+  static constexpr int kEpiWarps = 8;                    // two per TMEM lane quarter
+  static constexpr int kTmaWarp = kEpiWarp0 + kEpiWarps;
+  static constexpr int kMmaWarp = kTmaWarp + 1;
+  static constexpr int kThreads = (kTmaWarp + 4) * 32;   // 896 (PW 16) or 640 (PW 8)
+  static constexpr int kLaunchRegs = (65536 / kThreads) & ~7;   // 72 or 96
+  // setmaxnreg split of the launch pool: PW 16: 4 x 128 x 80 + 2 x 128 x 64 +
+  // 128 x 32 = 61440 <= 64512; PW 8: 2 x 128 x 160 + 2 x 128 x 64 + 128 x 32 = 61440
+  static constexpr int kProdRegs = PW == 16 ? 80 : 160, kEpiRegs = 64, kCtlRegs = 32;
+  static_assert(kProdThreads * kProdRegs + kEpiWarps * 32 * kEpiRegs + 128 * kCtlRegs <= kThreads * kLaunchRegs,
+                "register split exceeds the launch pool");
+};
 
-template <typename T>
-__global__ void __launch_bounds__(kFwdThreads, 1)
+template <typename T, int PW>
+__global__ void __launch_bounds__(FwdLayout<PW>::kThreads, 1)
     dcn_fwd_kernel(const __grid_constant__ FwdArgs a) {
+  using L = FwdLayout<PW>;
+  constexpr int kProdThreads = L::kProdThreads, kRowsPerWarp = L::kRowsPerWarp;
+  constexpr int kEpiWarp0 = L::kEpiWarp0, kEpiWarps = L::kEpiWarps;
+  constexpr int kTmaWarp = L::kTmaWarp, kMmaWarp = L::kMmaWarp, kFwdThreads = L::kThreads;
+  constexpr int kProdRegs = L::kProdRegs, kEpiRegs = L::kEpiRegs, kCtlRegs = L::kCtlRegs;
   constexpr int NS = OpOf<T>::kSplit ? 2 : 1;
   constexpr uint32_t kATile = 128 * 128;  // 128 rows x 128 B
   const Plan& P = a.plan;
@@ -185,7 +199,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     using GS = GatherShape<T>;
     constexpr int LPP = GS::kLPP, CPL = GS::kCPL, PPI = GS::kPPI;
     constexpr int ITER = kRowsPerWarp / PPI;
-    constexpr int BATCH = sizeof(T) == 4 ? 1 : (ITER < 4 ? ITER : 4);
+    constexpr int BATCH = sizeof(T) == 4 ? (ITER >= 2 ? 2 : 1) : (ITER < 4 ? ITER : 4);
     const int lp = lane / LPP, q = lane % LPP;
     const T* __restrict__ xt = reinterpret_cast<const T*>(a.xt);
     // element distance of the right and the lower corner line of a clamped block
@@ -261,7 +275,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
         if (!ok) break;
         if (warp == 0) DCN_TS(4 * kidx + 2);
-        if (!(a.dbg & 16)) fence_proxy_async_smem();
+        fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(full0 + 8 * s);
         if (warp == 0) DCN_TS(4 * kidx + 3);
@@ -294,11 +308,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           const int gb = gnext & 1;
           if (!mbar_wait(gfree0 + 8 * gb, ((gnext >> 1) & 1) ^ 1, a.err, &abort_flag)) { gok = false; break; }
           const int gpt = (blockIdx.x + gnext * (int)gridDim.x) / P.nCoT;
-          // study switch 32: windows after the first two are not rebuilt (they
-          // keep earlier tiles' geometry: valid indices, wrong results)
-          if (!((a.dbg & 32) && gnext >= 2))
-            build_geometry(std::integral_constant<int, kEpiWarps * 32>{}, gpt, 0, P.K2 * P.dg, gb,
-                           tid - kEpiWarp0 * 32);
+          build_geometry(std::integral_constant<int, kEpiWarps * 32>{}, gpt, 0, P.K2 * P.dg, gb,
+                         tid - kEpiWarp0 * 32);
           __syncwarp();
           if (lane == 0) mbar_arrive(gready0 + 8 * gb);
         }
@@ -326,7 +337,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const int rpl = wpix0 + cvl * EPV;
       const int rbl = vec ? rpl / HoWo : 0;
       T* yrun = y + (size_t)rbl * P.Co * HoWo + (rpl - rbl * HoWo);
-      for (int c0 = 16 * chalf; c0 < NT && !(a.dbg & 64); c0 += 16 * kEpiPerQuarter) {   // 64: no epilogue (study)
+      for (int c0 = 16 * chalf; c0 < NT; c0 += 16 * kEpiPerQuarter) {
         float v[16];
         tmem_ld16(tbase + c0, v);
         if (vec) {
@@ -409,10 +420,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         for (int kc = 0; kc < P.nK; ++kc, (++s == S ? (s = 0, ph ^= 1u) : 0u)) {
           if (!mbar_wait(empty0 + 8 * s, ph ^ 1u, a.err, &abort_flag)) { ok = false; break; }
           const uint32_t btile = sbase + s * stageBytes + NS * kATile;
-          if (a.dbg & 8) {   // study switch: no weight copy (the MMA reads stale data)
-            mbar_arrive(full0 + 8 * s);
-            continue;
-          }
           mbar_arrive_expect_tx(full0 + 8 * s, NS * bTile);
           bulk_g2s(btile, wsrc + (size_t)kc * P.wf_tile_bytes, NS * bTile, full0 + 8 * s);
         }
@@ -503,8 +510,8 @@ int launch_forward(const FwdArgs& a, cudaStream_t stream) {
   if (getenv("DCN_FWD_CARVE")) {   // study switch: shared-memory carveout in percent
     const int pc = atoi(getenv("DCN_FWD_CARVE"));
     if (pc != carve_set) {
-      cudaFuncSetAttribute(dcn_fwd_kernel<__nv_bfloat16>, cudaFuncAttributePreferredSharedMemoryCarveout, pc);
-      cudaFuncSetAttribute(dcn_fwd_kernel<__half>, cudaFuncAttributePreferredSharedMemoryCarveout, pc);
+      cudaFuncSetAttribute(dcn_fwd_kernel<__nv_bfloat16, 16>, cudaFuncAttributePreferredSharedMemoryCarveout, pc);
+      cudaFuncSetAttribute(dcn_fwd_kernel<__half, 16>, cudaFuncAttributePreferredSharedMemoryCarveout, pc);
       carve_set = pc;
     }
   }
@@ -514,22 +521,22 @@ int launch_forward(const FwdArgs& a, cudaStream_t stream) {
   cudaError_t e;
   switch (P.dtype) {
     case DCN_F32:
-      e = cudaFuncSetAttribute(dcn_fwd_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      e = cudaFuncSetAttribute(dcn_fwd_kernel<float, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)smem);
       if (e != cudaSuccess) return DCN_E_CUDA;
-      e = launch_k(dcn_fwd_kernel<float>, dim3(grid), dim3(kFwdThreads), smem, stream, args);
+      e = launch_k(dcn_fwd_kernel<float, 8>, dim3(grid), dim3(FwdLayout<8>::kThreads), smem, stream, args);
       break;
     case DCN_F16:
-      e = cudaFuncSetAttribute(dcn_fwd_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      e = cudaFuncSetAttribute(dcn_fwd_kernel<__half, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)smem);
       if (e != cudaSuccess) return DCN_E_CUDA;
-      e = launch_k(dcn_fwd_kernel<__half>, dim3(grid), dim3(kFwdThreads), smem, stream, args);
+      e = launch_k(dcn_fwd_kernel<__half, 16>, dim3(grid), dim3(FwdLayout<16>::kThreads), smem, stream, args);
       break;
     default:
-      e = cudaFuncSetAttribute(dcn_fwd_kernel<__nv_bfloat16>,
+      e = cudaFuncSetAttribute(dcn_fwd_kernel<__nv_bfloat16, 16>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return DCN_E_CUDA;
-      e = launch_k(dcn_fwd_kernel<__nv_bfloat16>, dim3(grid), dim3(kFwdThreads), smem, stream, args);
+      e = launch_k(dcn_fwd_kernel<__nv_bfloat16, 16>, dim3(grid), dim3(FwdLayout<16>::kThreads), smem, stream, args);
       break;
   }
   return e == cudaSuccess ? DCN_OK : DCN_E_CUDA;
