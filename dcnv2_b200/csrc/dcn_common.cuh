@@ -262,6 +262,18 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo_byte
   return d;
 }
 
+// Shared-memory matrix descriptor, no swizzle (K-major: 8-row x 16-byte core
+// matrices; lbo = byte distance of the core matrices adjacent in K, sbo = of the
+// 8-row groups).
+__device__ __forceinline__ uint64_t nosw_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;
+  return d;
+}
+
 // Instruction descriptor for kind::f16: f32 accumulator, A/B format (0 f16, 1 bf16),
 // major-ness of A and B (0 K-major, 1 MN-major), M and N.
 __host__ __device__ constexpr uint32_t make_idesc(int bf16, int a_mn, int b_mn, int M, int N) {

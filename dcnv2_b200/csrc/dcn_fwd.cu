@@ -98,6 +98,13 @@ __global__ void __launch_bounds__(FwdLayout<PW>::kThreads, 1)
   float4* sgeo_w = reinterpret_cast<float4*>(smem_raw + ((sbase - smem_u32(smem_raw)) + S * stageBytes));
   int* sgeo_idx = reinterpret_cast<int*>(sgeo_w + NB * kGeoTaps * kTileM);
   float* sbias = reinterpret_cast<float*>(sgeo_idx + NB * kGeoTaps * kTileM);  // [Co]
+  // bias as an MMA operand (16-bit, one Co tile): a K = 16 slice whose only
+  // non-zero column is A = 1 (128 rows) and B = bias (NT rows), in the
+  // no-swizzle K-major layout (8-row x 16-byte core matrices, the two K halves
+  // 128 B apart, 8-row groups 256 B apart); the first MMA of every tile then
+  // starts the accumulator at the bias and the epilogue adds nothing
+  const uint32_t sbias_a = (smem_u32(sbias + P.nCoT * NT) + 127u) & ~127u;
+  const uint32_t sbias_b = sbias_a + kTileM * 32u;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
@@ -123,6 +130,23 @@ __global__ void __launch_bounds__(FwdLayout<PW>::kThreads, 1)
   // bias staged once per CTA (the epilogue reads it for every output element)
   for (int c = tid; c < P.nCoT * NT; c += kFwdThreads)
     sbias[c] = (a.bias != nullptr && c < P.Co) ? ldf(reinterpret_cast<const T*>(a.bias) + c) : 0.f;
+  if constexpr (NS == 1) {
+    if (a.mma_bias) {
+      // word w of row r (elements 2w, 2w+1) at (r/8)*256 + (w/4)*128 + (r%8)*16 + (w%4)*4
+      for (int e = tid; e < (kTileM + NT) * 8; e += kFwdThreads) {
+        const int r = e >> 3, w = e & 7;
+        uint32_t val = 0u;
+        if (w == 0) {
+          const float f = r < kTileM ? 1.f : (r - kTileM < P.Co ? ldf(reinterpret_cast<const T*>(a.bias) + (r - kTileM)) : 0.f);
+          val = pack2<OpOf<T>::kBF16>(f, 0.f);
+        }
+        const int rr = r < kTileM ? r : r - kTileM;
+        const uint32_t base = r < kTileM ? sbias_a : sbias_b;
+        sts_u32(base + (uint32_t)((rr >> 3) * 256 + (w >> 2) * 128 + (rr & 7) * 16 + (w & 3) * 4), val);
+      }
+      fence_proxy_async_smem();
+    }
+  }
   uint32_t tmem_cols = 32;
   while (tmem_cols < (uint32_t)(2 * NT)) tmem_cols <<= 1;
   if (warp == kMmaWarp) tmem_alloc(smem_u32(&tmem_slot), tmem_cols);
@@ -341,12 +365,6 @@ __global__ void __launch_bounds__(FwdLayout<PW>::kThreads, 1)
         float v[16];
         tmem_ld16(tbase + c0, v);
         if (vec) {
-          float bz[16];
-#pragma unroll
-          for (int j = 0; j < 16; j += 4) {
-            const float4 b4 = *reinterpret_cast<const float4*>(sbias + ct * NT + c0 + j);
-            bz[j] = b4.x; bz[j + 1] = b4.y; bz[j + 2] = b4.z; bz[j + 3] = b4.w;
-          }
           if constexpr (sizeof(T) == 2) {
             // stage [8 co pairs][32 px] words (co 2p in the low half, 2p+1 in the
             // high half: one packed conversion and one 32-bit store per pair), then
@@ -354,10 +372,18 @@ __global__ void __launch_bounds__(FwdLayout<PW>::kThreads, 1)
             // splits them into the two co rows' 16-byte runs
             constexpr int kBF = OpOf<T>::kBF16;
             const uint32_t sw = smem_u32(stg);
+            if (a.mma_bias) {   // the bias is already in the accumulator
 #pragma unroll
-            for (int p2 = 0; p2 < 8; ++p2)
-              sts_u32(sw + (p2 * 32 + lane) * 4u,
-                      pack2<kBF>(v[2 * p2] + bz[2 * p2], v[2 * p2 + 1] + bz[2 * p2 + 1]));
+              for (int p2 = 0; p2 < 8; ++p2)
+                sts_u32(sw + (p2 * 32 + lane) * 4u, pack2<kBF>(v[2 * p2], v[2 * p2 + 1]));
+            } else {
+#pragma unroll
+              for (int p2 = 0; p2 < 8; p2 += 2) {
+                const float4 b4 = *reinterpret_cast<const float4*>(sbias + ct * NT + c0 + 2 * p2);
+                sts_u32(sw + (p2 * 32 + lane) * 4u, pack2<kBF>(v[2 * p2] + b4.x, v[2 * p2 + 1] + b4.y));
+                sts_u32(sw + ((p2 + 1) * 32 + lane) * 4u, pack2<kBF>(v[2 * p2 + 2] + b4.z, v[2 * p2 + 3] + b4.w));
+              }
+            }
             __syncwarp();
             const int pp = lane >> 2;
             const uint4 w0 = lds_v4(sw + (pp * 32 + cvl * 8) * 4u);
@@ -373,6 +399,12 @@ __global__ void __launch_bounds__(FwdLayout<PW>::kThreads, 1)
             }
             __syncwarp();
           } else {
+          float bz[16];
+#pragma unroll
+          for (int j = 0; j < 16; j += 4) {
+            const float4 b4 = *reinterpret_cast<const float4*>(sbias + ct * NT + c0 + j);
+            bz[j] = b4.x; bz[j + 1] = b4.y; bz[j + 2] = b4.z; bz[j + 3] = b4.w;
+          }
           // stage [JH co][32 px] (8 columns per pass for f32 so the stage stays
           // 1 KB a warp) then store 16-byte runs of pixels per co row
 #pragma unroll
@@ -397,7 +429,8 @@ __global__ void __launch_bounds__(FwdLayout<PW>::kThreads, 1)
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int co = ct * NT + c0 + j;
-            if (pv && co < P.Co && !(a.dbg & 2)) yb[(size_t)co * HoWo] = Elem<T>::from_f(v[j] + sbias[co]);
+            if (pv && co < P.Co && !(a.dbg & 2))
+              yb[(size_t)co * HoWo] = Elem<T>::from_f(a.mma_bias ? v[j] : v[j] + sbias[co]);
           }
         }
       }
@@ -439,6 +472,9 @@ __global__ void __launch_bounds__(FwdLayout<PW>::kThreads, 1)
         if (!mbar_wait(acce0 + 8 * ab, ((it >> 1) & 1) ^ 1, a.err, &abort_flag)) break;
         tc_fence_after();
         const uint32_t dt = tmem_base + (uint32_t)(ab * NT);
+        const bool mbias = NS == 1 && a.mma_bias;
+        if (mbias)   // D = 1 x bias^T over a K = 16 slice: the accumulator starts at the bias
+          umma_f16(dt, nosw_desc(sbias_a, 128, 256), nosw_desc(sbias_b, 128, 256), idesc, 0u);
         for (int kc = 0; kc < P.nK; ++kc, ++kidx) {
           const int s = ms;
           const uint32_t ph = mph;
@@ -452,7 +488,7 @@ __global__ void __launch_bounds__(FwdLayout<PW>::kThreads, 1)
           for (int kk = 0; kk < 4; ++kk) {
             const uint64_t ad = sw128_desc(at + kk * 32, 16, 1024);
             const uint64_t bd = sw128_desc(bt + kk * 32, 16, 1024);
-            if (!(a.dbg & 4)) umma_f16(dt, ad, bd, idesc, (kc | kk) != 0);
+            if (!(a.dbg & 4)) umma_f16(dt, ad, bd, idesc, (mbias || (kc | kk) != 0) ? 1u : 0u);
             if constexpr (NS == 2) {
               const uint64_t adl = sw128_desc(at + kATile + kk * 32, 16, 1024);
               const uint64_t bdl = sw128_desc(bt + bTile + kk * 32, 16, 1024);
@@ -491,7 +527,10 @@ int launch_forward(const FwdArgs& a, cudaStream_t stream) {
   // two geometry windows built by the epilogue warps when every (tap, group) of
   // a tile fits one window and two stages still fit, else one built by the producers
   const size_t geoWin = (size_t)kGeoTaps * kTileM * (sizeof(float4) + sizeof(int));
-  const size_t biasBytes = (size_t)P.nCoT * P.NT * sizeof(float);
+  // the bias goes into the MMA for 16-bit types with one Co tile: its A and B
+  // slices (128 x 16 and NT x 16 elements) after the fp32 bias copy
+  const int mma_bias = NS == 1 && P.nCoT == 1 && a.bias != nullptr;
+  const size_t biasBytes = (size_t)P.nCoT * P.NT * sizeof(float) + (mma_bias ? 128 + (128 + (size_t)P.NT) * 32 : 0);
   int NB = P.K2 * P.dg <= kGeoTaps ? 2 : 1;
   if (NB == 2 && (kFwdSmemBudget - 1024 - 2 * geoWin - biasBytes) / stageBytes < 2) NB = 1;
   const size_t geoBytes = NB * geoWin + biasBytes;
@@ -505,6 +544,7 @@ int launch_forward(const FwdArgs& a, cudaStream_t stream) {
   FwdArgs args = a;
   args.stages = S;
   args.geo_bufs = NB;
+  args.mma_bias = mma_bias;
   const size_t smem = 1024 + (size_t)S * stageBytes + geoBytes;
   static int carve_set = -1;
   if (getenv("DCN_FWD_CARVE")) {   // study switch: shared-memory carveout in percent

@@ -32,6 +32,7 @@ struct FwdArgs {
   int* err;             // device error word
   int stages;
   int geo_bufs;         // geometry windows: 2 built by the epilogue warps, 1 by the producers
+  int mma_bias;         // bias added by an extra K = 16 MMA slice (set by the launcher)
   int num_sms;
   int dbg;              // experiment switches (DCN_DEBUG_SKIP); 0 in normal use
 };
