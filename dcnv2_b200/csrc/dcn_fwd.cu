@@ -98,8 +98,8 @@ __global__ void __launch_bounds__(FwdLayout<PW>::kThreads, 1)
   float4* sgeo_w = reinterpret_cast<float4*>(smem_raw + ((sbase - smem_u32(smem_raw)) + S * stageBytes));
   int* sgeo_idx = reinterpret_cast<int*>(sgeo_w + NB * kGeoTaps * kTileM);
   float* sbias = reinterpret_cast<float*>(sgeo_idx + NB * kGeoTaps * kTileM);  // [Co]
-  // bias as an MMA operand (16-bit, one Co tile): a K = 16 slice whose only
-  // non-zero column is A = 1 (128 rows) and B = bias (NT rows), in the
+  // bias as an MMA operand (16-bit, up to two Co tiles): a K = 16 slice whose
+  // only non-zero column is A = 1 (128 rows) and B = bias (NT rows per Co tile), in the
   // no-swizzle K-major layout (8-row x 16-byte core matrices, the two K halves
   // 128 B apart, 8-row groups 256 B apart); the first MMA of every tile then
   // starts the accumulator at the bias and the epilogue adds nothing
@@ -133,7 +133,7 @@ __global__ void __launch_bounds__(FwdLayout<PW>::kThreads, 1)
   if constexpr (NS == 1) {
     if (a.mma_bias) {
       // word w of row r (elements 2w, 2w+1) at (r/8)*256 + (w/4)*128 + (r%8)*16 + (w%4)*4
-      for (int e = tid; e < (kTileM + NT) * 8; e += kFwdThreads) {
+      for (int e = tid; e < (kTileM + P.nCoT * NT) * 8; e += kFwdThreads) {
         const int r = e >> 3, w = e & 7;
         uint32_t val = 0u;
         if (w == 0) {
@@ -474,7 +474,8 @@ __global__ void __launch_bounds__(FwdLayout<PW>::kThreads, 1)
         const uint32_t dt = tmem_base + (uint32_t)(ab * NT);
         const bool mbias = NS == 1 && a.mma_bias;
         if (mbias)   // D = 1 x bias^T over a K = 16 slice: the accumulator starts at the bias
-          umma_f16(dt, nosw_desc(sbias_a, 128, 256), nosw_desc(sbias_b, 128, 256), idesc, 0u);
+          umma_f16(dt, nosw_desc(sbias_a, 128, 256),
+                   nosw_desc(sbias_b + (uint32_t)(tile % P.nCoT) * (uint32_t)NT * 32u, 128, 256), idesc, 0u);
         for (int kc = 0; kc < P.nK; ++kc, ++kidx) {
           const int s = ms;
           const uint32_t ph = mph;
@@ -527,10 +528,11 @@ int launch_forward(const FwdArgs& a, cudaStream_t stream) {
   // two geometry windows built by the epilogue warps when every (tap, group) of
   // a tile fits one window and two stages still fit, else one built by the producers
   const size_t geoWin = (size_t)kGeoTaps * kTileM * (sizeof(float4) + sizeof(int));
-  // the bias goes into the MMA for 16-bit types with one Co tile: its A and B
-  // slices (128 x 16 and NT x 16 elements) after the fp32 bias copy
-  const int mma_bias = NS == 1 && P.nCoT == 1 && a.bias != nullptr;
-  const size_t biasBytes = (size_t)P.nCoT * P.NT * sizeof(float) + (mma_bias ? 128 + (128 + (size_t)P.NT) * 32 : 0);
+  // the bias goes into the MMA for 16-bit types with up to two Co tiles: its A
+  // and B slices (128 x 16 and nCoT x NT x 16 elements) after the fp32 bias copy
+  const int mma_bias = NS == 1 && P.nCoT <= 2 && a.bias != nullptr;
+  const size_t biasBytes =
+      (size_t)P.nCoT * P.NT * sizeof(float) + (mma_bias ? 128 + (128 + (size_t)P.nCoT * P.NT) * 32 : 0);
   int NB = P.K2 * P.dg <= kGeoTaps ? 2 : 1;
   if (NB == 2 && (kFwdSmemBudget - 1024 - 2 * geoWin - biasBytes) / stageBytes < 2) NB = 1;
   const size_t geoBytes = NB * geoWin + biasBytes;
