@@ -52,6 +52,9 @@ WORKLOADS = {
     "resnet_s3": (16, 512, 16, 16, 512, 3, 1, 1, 1, 1, 1.5),
     "c512_dg4": (32, 512, 32, 32, 512, 3, 1, 1, 1, 4, 2.0),
     "edge_k5": (4, 96, 97, 131, 160, 5, 2, 4, 2, 2, 8.0),
+    # the 1x1 deformable conv of the reference's CIFAR training demo (bottleneck
+    # 256 -> 64 channels at 32x32, batch 128; train.py:56-73)
+    "k1_cifar": (128, 256, 32, 32, 64, 1, 1, 0, 1, 1, 1.5),
 }
 # stacks of DCN modules (offset/mask predicted by a plain 3x3 conv, ReLU between),
 # the global batch split over the ranks: one data-parallel training step per step
