@@ -613,7 +613,52 @@ def main():
 
     for _ in range(2):
         e2e_step()
-    ms_e2e = timed(e2e_step, args.steps)
+    ms_e2e_serial = timed(e2e_step, args.steps)
+
+    # the same end-to-end steps as a training loop runs them: the host->device
+    # copies of step i+1 go on a copy stream while step i computes (inputs double
+    # buffered; every step still copies its own inputs in and its result out)
+    copy_stream = torch.cuda.Stream(dev)
+    hosts = (hx, hoff, hm, hgy)
+    bufs = [[torch.empty_like(t) for t in (x, off, m, gy)] for _ in range(2)]
+    copied = [torch.cuda.Event() for _ in range(2)]
+    used = [torch.cuda.Event() for _ in range(2)]
+
+    def e2e_pipelined(n):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        copy_stream.wait_stream(stream)
+
+        def load(i):
+            with torch.cuda.stream(copy_stream):
+                if i >= 2:
+                    copy_stream.wait_event(used[i % 2])
+                for dst, src in zip(bufs[i % 2], hosts):
+                    dst.copy_(src, non_blocking=True)
+                copied[i % 2].record(copy_stream)
+
+        load(0)
+        for i in range(n):
+            if i + 1 < n:
+                load(i + 1)
+            flush.zero_()
+            stream.wait_event(copied[i % 2])
+            _, gw_, gb_ = step(*bufs[i % 2])
+            used[i % 2].record(stream)
+            hgw.copy_(gw_, non_blocking=True)
+            hgb.copy_(gb_, non_blocking=True)
+        t1.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([t0.elapsed_time(t1)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item()) / n
+
+    e2e_pipelined(3)
+    ms_e2e = e2e_pipelined(args.steps)
     clk = clocks.stop()
 
     step_flops = 3 * readme_flops(B, C, Ho, Wo, Co, k)
@@ -637,7 +682,9 @@ def main():
         "roofline": roofline,
         "clocks": clk,
         "e2e": {"value": e2e_value, "unit": "TFLOP/s (README formula, fwd+bwd)",
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e},
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e,
+                "pipelined": "copies of step i+1 overlap step i on a second stream",
+                "serial_ms_per_step": ms_e2e_serial},
         "gpu_launches": int(launches),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
