@@ -538,25 +538,28 @@ int launch_forward(const FwdArgs& a, cudaStream_t stream) {
   const size_t geoBytes = NB * geoWin + biasBytes;
   int S = (int)((kFwdSmemBudget - 1024 - geoBytes) / stageBytes);
   if (S > kMaxStages) S = kMaxStages;
-  if (const char* e = getenv("DCN_FWD_STAGES")) {   // study switch: fewer stages, more L1
-    const int sm = atoi(e);
-    if (sm >= 2 && sm < S) S = sm;
-  }
+  static const int study_stages = [] {   // study switch DCN_FWD_STAGES: fewer stages, more L1
+    const char* e = getenv("DCN_FWD_STAGES");
+    return e ? atoi(e) : 0;
+  }();
+  if (study_stages >= 2 && study_stages < S) S = study_stages;
   if (S < 2) return DCN_E_UNSUPPORTED;
   FwdArgs args = a;
   args.stages = S;
   args.geo_bufs = NB;
   args.mma_bias = mma_bias;
   const size_t smem = 1024 + (size_t)S * stageBytes + geoBytes;
-  static int carve_set = -1;
-  if (getenv("DCN_FWD_CARVE")) {   // study switch: shared-memory carveout in percent
-    const int pc = atoi(getenv("DCN_FWD_CARVE"));
-    if (pc != carve_set) {
+  static const int study_carve = [] {   // study switch DCN_FWD_CARVE: shared-memory carveout (%)
+    const char* e = getenv("DCN_FWD_CARVE");
+    if (e != nullptr) {
+      const int pc = atoi(e);
       cudaFuncSetAttribute(dcn_fwd_kernel<__nv_bfloat16, 16>, cudaFuncAttributePreferredSharedMemoryCarveout, pc);
       cudaFuncSetAttribute(dcn_fwd_kernel<__half, 16>, cudaFuncAttributePreferredSharedMemoryCarveout, pc);
-      carve_set = pc;
+      return pc;
     }
-  }
+    return -1;
+  }();
+  (void)study_carve;
   const int nTiles = P.nPT * P.nCoT;
   int grid = nTiles < a.num_sms ? nTiles : a.num_sms;
   if (grid <= 0) return DCN_OK;
