@@ -63,7 +63,6 @@ STACKS = {
 }
 DTYPES = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
-RED_PEAK_TBS = 5.9  # fp32 L2 reduction rate of the scatter's access pattern, measured on a B200
 
 
 def readme_flops(B, C, Ho, Wo, Co, k):
@@ -261,8 +260,64 @@ def run_reference(args, wl, rank):
                                    "reference arithmetic; the reference has no CPU kernel)"},
         "e2e": {"value": val, "unit": "TFLOP/s (README formula, fwd+bwd)",
                 "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "reference_gpu": reference_gpu(wl, args),
     }
     print(json.dumps(line), file=_JSON_OUT, flush=True)
+
+
+def reference_gpu(wl, args):
+    """Context for the reference arm: the reference's own CUDA operator (com.cu +
+    ext.cpp compiled for sm_100a by oracle/build_ref.py into oracle/_ref) timed on
+    this GPU, float32 (its only dtype), forward + backward of the same layer, CUDA
+    events, L2 flushed before every step.  The reference handles neither dilation
+    nor deformable groups, so other workloads report it as unavailable."""
+    import glob
+    import importlib.machinery
+    import importlib.util
+    B, C, H, W, Co, k, s, p, d, dg, _ = wl
+    if d != 1 or dg != 1:
+        return {"unavailable": "the reference operator implements neither dilation nor deformable groups"}
+    if not torch.cuda.is_available():
+        return {"unavailable": "no CUDA device"}
+    so = glob.glob(os.path.join(ROOT, "oracle", "_ref", "Conv2d_ref*.so"))
+    if not so:
+        return {"unavailable": "oracle/_ref not built (python oracle/build_ref.py <reference checkout>)"}
+    try:
+        loader = importlib.machinery.ExtensionFileLoader("Conv2d_ref", so[0])
+        spec = importlib.util.spec_from_loader("Conv2d_ref", loader)
+        ref = importlib.util.module_from_spec(spec)
+        loader.exec_module(ref)
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"oracle/_ref does not load: {e}"[:200]}
+    dev = torch.device("cuda", 0)
+    x, w, b, off, m, gy = make_inputs(wl, torch.float32, dev, seed=0)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def step():
+        ref.dcn_v2_forward(x, w, m, off, b, s, s, p, p)
+        ref.dcn_v2_backward(x, w, m, off, b, gy, s, s, p, p)
+
+    def timed(fn, n):
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+        torch.cuda.synchronize()
+        for i in range(n):
+            flush.zero_()
+            ev[i][0].record()
+            fn()
+            ev[i][1].record()
+        torch.cuda.synchronize()
+        return sum(a.elapsed_time(b_) for a, b_ in ev) / n
+
+    n = max(3, min(args.steps, 20))
+    for _ in range(3):
+        step()
+    ms = timed(step, n)
+    ms_fwd = timed(lambda: ref.dcn_v2_forward(x, w, m, off, b, s, s, p, p), n)
+    Ho, Wo = out_hw(H, W, k, s, p, d)
+    return {"ms_per_step": ms, "fwd_ms": ms_fwd,
+            "value": 3 * readme_flops(B, C, Ho, Wo, Co, k) / (ms * 1e-3) / 1e12,
+            "unit": "TFLOP/s (README formula, fwd+bwd)", "dtype": "f32", "steps": n,
+            "kind": "reference com.cu/ext.cpp built for sm_100a (oracle/_ref), on this GPU"}
 
 
 def make_timer(world, dev, stream, flush):
@@ -437,8 +492,8 @@ def run_stack(args):
 def roofline_of(trace, steps, wl, dtype, layers_per_step, workload, dtype_name):
     """Roofline of the dominant kernel of a traced run: the tensor-core kernels against
     the measured bf16 dense peak with the algorithmic FLOPs of one GEMM pass; the SIMT
-    scatter against the measured HBM copy bandwidth with its algorithmic bytes (and
-    against the measured L2 reduction rate).  `wl` is one layer's shape; a step runs
+    scatter against the measured HBM copy bandwidth with its algorithmic bytes.
+    `wl` is one layer's shape; a step runs
     `layers_per_step` such layers.  Returns (roofline, library launches in the run)."""
     B, C, H, W, Co, k, s, p, d, dg, _ = wl
     Ho, Wo = out_hw(H, W, k, s, p, d)
@@ -450,7 +505,6 @@ def roofline_of(trace, steps, wl, dtype, layers_per_step, workload, dtype_name):
     launches_per_layer = n_dom / steps / layers_per_step   # > 1 when the backward runs in chunks
     esz = torch.tensor([], dtype=dtype).element_size()
     K2 = k * k
-    extra = {}
     if dom in ("forward", "backward_data", "backward_weight"):
         gflop = gemm_flops(B, C, Ho, Wo, Co, k) / launches_per_layer
         work, bound, unit, peak = gflop, "tensor", "TFLOP/s", peaks["bf16_tflops"]
@@ -468,19 +522,10 @@ def roofline_of(trace, steps, wl, dtype, layers_per_step, workload, dtype_name):
         basis = (f"algorithmic bytes {nbytes:.4g} per launch (gcol, x, offset/mask, fp32 grad_input acc, "
                  "outputs, columns)")
         achieved = work / (per_launch_ms * 1e-3) / 1e9
-        # the scatter's real limiter: fp32 reductions into L2 (4 corners x C x 4 B per
-        # pixel and tap) against the rate a microbenchmark of the same access pattern
-        # sustains on this B200 (red.global.add.v4.f32, random target pixels)
-        red_bytes = P * K2 * 4 * C * 4 / launches_per_layer
-        red_tbs = red_bytes / (per_launch_ms * 1e-3) / 1e12
-        extra["l2_reduction"] = {
-            "achieved": red_tbs, "peak": RED_PEAK_TBS, "unit": "TB/s", "frac": red_tbs / RED_PEAK_TBS,
-            "bytes_per_launch": red_bytes,
-            "peak_source": "microbenchmark of red.global.add.v4.f32 with random targets on this B200"}
     roofline = {"kernel": dom, "bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
                 "frac": achieved / peak,
                 "peak_source": f"{peak_kind} ({'bf16 dense, burst' if bound == 'tensor' else 'HBM copy'})",
-                "traffic": load_traffic(dom, workload, dtype_name), "algorithmic": basis, **extra}
+                "traffic": load_traffic(dom, workload, dtype_name), "algorithmic": basis}
     # library kernels in the traced run (the accumulator memset is a runtime call)
     launches = sum(n for kk, (n, _) in kernels.items() if kk != "zero_accumulators")
     return roofline, launches
@@ -503,6 +548,8 @@ def main():
     ap.add_argument("--dtype", default="bf16", choices=list(DTYPES))
     ap.add_argument("--workload", default="readme", choices=list(WORKLOADS) + list(STACKS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-fp32", action="store_true",
+                    help="skip the float32 step reported beside a 16-bit run")
     ap.add_argument("--graph", action="store_true",
                     help="stack workloads: capture the training step in a CUDA graph and replay it")
     ap.add_argument("--launch-only", type=int, default=0, metavar="N",
@@ -659,15 +706,37 @@ def main():
 
     e2e_pipelined(3)
     ms_e2e = e2e_pipelined(args.steps)
-    clk = clocks.stop()
-
     step_flops = 3 * readme_flops(B, C, Ho, Wo, Co, k)
     value = world * step_flops / (ms_step * 1e-3) / 1e12
+    gflop = gemm_flops(B, C, Ho, Wo, Co, k)
+
+    # the same step in float32, the precision of the benchmark configuration
+    # (configs[0]) and of the reference operator, timed the same way
+    fp32_leg = None
+    if args.dtype != "fp32" and not args.no_fp32:
+        x32, w32, b32, off32, m32, gy32 = make_inputs(wl, torch.float32, dev, seed=rank)
+
+        def step32():
+            _C.dcn_v2_forward(x32, w32, m32, off32, b32, s, s, p, p, d, d, dg)
+            gi_, go_, gm_, gw_, gb_ = _C.dcn_v2_backward(x32, w32, m32, off32, b32, gy32, s, s, p, p, d, d, dg)
+            if world > 1:
+                allreduce_tensors([gw_, gb_])
+
+        for _ in range(args.warmup):
+            step32()
+        ms32 = timed(step32, args.steps)
+        ms32_fwd = timed(lambda: _C.dcn_v2_forward(x32, w32, m32, off32, b32, s, s, p, p, d, d, dg), args.steps)
+        fp32_leg = {"ms_per_step": ms32, "value": world * step_flops / (ms32 * 1e-3) / 1e12,
+                    "unit": "TFLOP/s (README formula, fwd+bwd)",
+                    "fwd_bwd_gemm_tflops": world * 3 * gflop / (ms32 * 1e-3) / 1e12,
+                    "fwd_ms": ms32_fwd,
+                    "note": "float32 tensors; every GEMM operand split into bf16 hi + lo, three MMAs"}
+        del x32, w32, b32, off32, m32, gy32
+    clk = clocks.stop()
     e2e_value = world * step_flops / (ms_e2e * 1e-3) / 1e12
 
     roofline, launches = roofline_of(trace, args.steps, wl, dtype, 1, args.workload, args.dtype)
     kernels = {kname: (n, tot) for kname, (n, tot) in trace.items()}
-    gflop = gemm_flops(B, C, Ho, Wo, Co, k)
 
     line = {
         "metric": "dcnv2_fwd_bwd_readme_tflops", "value": value,
@@ -683,10 +752,13 @@ def main():
         "clocks": clk,
         "e2e": {"value": e2e_value, "unit": "TFLOP/s (README formula, fwd+bwd)",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e,
-                "pipelined": "copies of step i+1 overlap step i on a second stream",
+                "pipelined": "copies of step i+1 overlap step i on a second stream; the 256 MiB L2 "
+                             "flush is also written before every step",
                 "serial_ms_per_step": ms_e2e_serial},
         "gpu_launches": int(launches),
     }
+    if fp32_leg is not None:
+        line["fp32"] = fp32_leg
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(wl)
         line["cpu_torchvision"] = cpu_torchvision(wl)

@@ -29,9 +29,19 @@ _DTYPES = {torch.float32: _lib.DCN_F32, torch.float16: _lib.DCN_F16, torch.bfloa
 
 
 def _check_cuda(**tensors):
+    """Every tensor must be a CUDA tensor (com.cu:209-213), and all on one device:
+    the kernels run on the first tensor's GPU and would otherwise dereference
+    another GPU's memory."""
+    dev = None
     for name, t in tensors.items():
-        if t is not None and not t.is_cuda:
+        if t is None:
+            continue
+        if not t.is_cuda:
             raise RuntimeError(f"{name} must be a CUDA tensor")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"{name} is on {t.device}, expected {dev} (all tensors on one device)")
 
 
 def _desc(input, weight, stride_h, stride_w, pad_h, pad_w, dil_h, dil_w, dg, has_bias):

@@ -17,17 +17,22 @@ namespace dcn {
 
 namespace {
 
-// Experiment switches for kernel studies (bit 0: skip the bilinear gathers,
-// bit 1: skip output stores / scatters, bit 2: skip the MMAs).  Results are
-// wrong when set; never set in normal use.
+// Study switch (DCN_STUDY builds only): bit 0 skips the bilinear gathers, bit 1
+// output stores / scatters, bit 2 the MMAs; results are wrong when set.
 int debug_skip() {
+#ifdef DCN_STUDY
   static int v = [] {
     const char* e = getenv("DCN_DEBUG_SKIP");
     return e ? atoi(e) : 0;
   }();
   return v;
+#else
+  return 0;
+#endif
 }
 
+// Pixel budget of one backward chunk in MB of gcol + sampled columns (results
+// do not depend on it; a test sets DCN_GCOL_MB=1 to exercise ragged chunks).
 long long gcol_budget_mb() {
   static long long v = [] {
     const char* e = getenv("DCN_GCOL_MB");
@@ -36,15 +41,45 @@ long long gcol_budget_mb() {
   return v;
 }
 
-// Study switch: DCN_GOUT_PACKED=1 keeps the packed grad_output copy even where
-// the GEMMs could read grad_output directly.
+// Study switch (DCN_STUDY builds only): DCN_GOUT_PACKED=1 keeps the packed
+// grad_output copy even where the GEMMs could read grad_output directly.
 bool gout_packed_forced() {
+#ifdef DCN_STUDY
   static bool v = [] {
     const char* e = getenv("DCN_GOUT_PACKED");
     return e != nullptr && atoi(e) != 0;
   }();
   return v;
+#else
+  return false;
+#endif
 }
+
+#ifdef DCN_STUDY
+// Study switch: DCN_DEBUG_TS prints per-stage global-timer stamps of CTA 0 of
+// a kernel to stderr.  One buffer per device (tag 0..2: forward, backward
+// data, backward weight); allocates and synchronises, so never in a normal build.
+unsigned long long* study_ts_buffer(int tag, cudaStream_t s) {
+  if (!getenv("DCN_DEBUG_TS")) return nullptr;
+  static unsigned long long* bufs[64][3];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!bufs[dev][tag] && cudaMalloc(&bufs[dev][tag], 1024 * sizeof(unsigned long long)) != cudaSuccess)
+    bufs[dev][tag] = nullptr;
+  if (bufs[dev][tag]) cudaMemsetAsync(bufs[dev][tag], 0, 1024 * sizeof(unsigned long long), s);
+  return bufs[dev][tag];
+}
+
+void study_ts_print(const char* label, unsigned long long* d, cudaStream_t s) {
+  if (!d) return;
+  unsigned long long h[1024];
+  cudaMemcpyAsync(h, d, sizeof(h), cudaMemcpyDeviceToHost, s);
+  cudaStreamSynchronize(s);
+  fprintf(stderr, "%s", label);
+  for (int i = 0; i < 1024; ++i) fprintf(stderr, " %llu", h[i]);
+  fprintf(stderr, "\n");
+}
+#endif
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -325,22 +360,16 @@ static int forward_impl(const dcn_desc* d, const void* input, const void* weight
   a.err = reinterpret_cast<int*>(ws + P.off_status);
   a.num_sms = device_sms();
   a.dbg = debug_skip();
-  static unsigned long long* dts = nullptr;
-  if (getenv("DCN_DEBUG_TS")) {  // pipeline timestamps of CTA 0, printed to stderr (studies only)
-    if (!dts && cudaMalloc(&dts, 1024 * sizeof(unsigned long long)) != cudaSuccess) dts = nullptr;
-    if (dts) cudaMemsetAsync(dts, 0, 1024 * sizeof(unsigned long long), s);
-    a.ts = dts;
+#ifdef DCN_STUDY
+  a.ts = study_ts_buffer(0, s);
+#endif
+  {
+    TraceScope ts(TR_FORWARD, s);
+    rc = launch_forward(a, s);
   }
-  TraceScope ts(TR_FORWARD, s);
-  rc = launch_forward(a, s);
-  if (a.ts) {
-    unsigned long long h[1024];
-    cudaMemcpyAsync(h, a.ts, sizeof(h), cudaMemcpyDeviceToHost, s);
-    cudaStreamSynchronize(s);
-    fprintf(stderr, "DCN_TS");
-    for (int i = 0; i < 1024; ++i) fprintf(stderr, " %llu", h[i]);
-    fprintf(stderr, "\n");
-  }
+#ifdef DCN_STUDY
+  study_ts_print("DCN_TS", a.ts, s);
+#endif
   return rc;
 }
 
@@ -428,12 +457,10 @@ static int backward_impl(const dcn_desc* d, const void* input, const void* weigh
   a.dbg = debug_skip();
   a.vec_gout = aligned16(grad_output);
   a.cols = ws + P.off_cols;
-  static unsigned long long* dts_d = nullptr;
-  if (getenv("DCN_DEBUG_TS")) {  // pipeline timestamps of CTA 0, printed to stderr (studies only)
-    if (!dts_d && cudaMalloc(&dts_d, 1024 * sizeof(unsigned long long)) != cudaSuccess) dts_d = nullptr;
-    if (dts_d) cudaMemsetAsync(dts_d, 0, 1024 * sizeof(unsigned long long), s);
-    a.ts = dts_d;
-  }
+#ifdef DCN_STUDY
+  unsigned long long* const dts_d = study_ts_buffer(1, s);
+  a.ts = dts_d;
+#endif
   BwdWeightArgs w;
   memset(&w, 0, sizeof(w));
   w.plan = P;
@@ -446,12 +473,10 @@ static int backward_impl(const dcn_desc* d, const void* input, const void* weigh
   w.err = a.err;
   w.num_sms = a.num_sms;
   w.dbg = a.dbg;
-  static unsigned long long* dts = nullptr;
-  if (getenv("DCN_DEBUG_TS")) {  // pipeline timestamps of CTA 0, printed to stderr (studies only)
-    if (!dts && cudaMalloc(&dts, 1024 * sizeof(unsigned long long)) != cudaSuccess) dts = nullptr;
-    if (dts) cudaMemsetAsync(dts, 0, 1024 * sizeof(unsigned long long), s);
-    w.ts = dts;
-  }
+#ifdef DCN_STUDY
+  unsigned long long* const dts = study_ts_buffer(2, s);
+  w.ts = dts;
+#endif
   // per pixel chunk: column gradients (tcgen05), then the scatter (grad_input,
   // grad_offset, grad_mask and the sampled columns), then the weight gradient
   for (long long p0 = 0; p0 < P.totalP; p0 += P.gcol_chunk) {
@@ -474,22 +499,10 @@ static int backward_impl(const dcn_desc* d, const void* input, const void* weigh
     if (w.ts) w.ts = nullptr;   // timestamps of the first chunk only
     if (a.ts) a.ts = nullptr;
   }
-  if (dts_d && getenv("DCN_DEBUG_TS")) {
-    unsigned long long h[1024];
-    cudaMemcpyAsync(h, dts_d, sizeof(h), cudaMemcpyDeviceToHost, s);
-    cudaStreamSynchronize(s);
-    fprintf(stderr, "DCN_TSD");
-    for (int i = 0; i < 1024; ++i) fprintf(stderr, " %llu", h[i]);
-    fprintf(stderr, "\n");
-  }
-  if (dts && getenv("DCN_DEBUG_TS")) {
-    unsigned long long h[1024];
-    cudaMemcpyAsync(h, dts, sizeof(h), cudaMemcpyDeviceToHost, s);
-    cudaStreamSynchronize(s);
-    fprintf(stderr, "DCN_TSW");
-    for (int i = 0; i < 1024; ++i) fprintf(stderr, " %llu", h[i]);
-    fprintf(stderr, "\n");
-  }
+#ifdef DCN_STUDY
+  study_ts_print("DCN_TSD", dts_d, s);
+  study_ts_print("DCN_TSW", dts, s);
+#endif
   {
     TraceScope ts(TR_FINISH_GRAD_INPUT, s);
     if ((rc = launch_finish_grad_input(P, gxn, grad_input, s)) != DCN_OK) return rc;

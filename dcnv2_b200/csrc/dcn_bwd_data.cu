@@ -33,7 +33,7 @@ namespace dcn {
 namespace {
 
 #define DCN_TS(slot) \
-  do { if (a.ts && blockIdx.x == 0 && lane == 0 && (slot) < 1024) a.ts[(slot)] = globaltimer(); } while (0)
+  do { if (DCN_STUDY_ON && a.ts && blockIdx.x == 0 && lane == 0 && (slot) < 1024) a.ts[(slot)] = globaltimer(); } while (0)
 
 constexpr int kThreads = 512;  // 4 warpgroups
 constexpr int kAWarps = 4;
@@ -144,7 +144,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int tile = r0; tile < nTiles && ok; tile += cpu, ++it) {
       const int ab = it & 1;
       if (ew == 0) DCN_TS(4 * it);
-      if (!mbar_wait(accf0 + 8 * ab, (it >> 1) & 1, a.err, &abort_flag)) { ok = false; break; }
+      if (!mbar_wait_warp(accf0 + 8 * ab, (it >> 1) & 1, a.err, &abort_flag)) { ok = false; break; }
       if (ew == 0) DCN_TS(4 * it + 1);
       tc_fence_after();
       const uint32_t tb = tmem_base + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(ab * NC);
@@ -178,7 +178,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // transpose buffer -> global, RPI rows per instruction
         const int j = c0 / P.NC, within = c0 - j * P.NC;
         const int tg = set * P.gT + j;
-        if (tg < P.K2 * P.dg && within < cend && !(a.dbg & 2)) {
+        if (tg < P.K2 * P.dg && within < cend && !DCN_SKIP(2)) {
 #pragma unroll
           for (int i = 0; i < 32 / RPI; ++i) {
             const int row = i * RPI + lane / NCH, c = lane % NCH;
@@ -291,7 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const uint64_t ad = gdirect ? sw128_desc(at + kk * 2048, 8192, 1024)
                                           : sw128_desc(at + kk * 32, 16, 1024);
               const uint64_t bd = sw128_desc(bt + kk * 32, 16, 1024);
-              if (!(a.dbg & 4)) umma_f16(dt, ad, bd, idesc, (ko | kk) != 0);
+              if (!DCN_SKIP(4)) umma_f16(dt, ad, bd, idesc, (ko | kk) != 0);
               if constexpr (NS == 2) {
                 const uint64_t adl = sw128_desc(at + kATile + kk * 32, 16, 1024);
                 const uint64_t bdl = sw128_desc(bt + bTile + kk * 32, 16, 1024);

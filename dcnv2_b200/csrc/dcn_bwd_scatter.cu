@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(kThreads, 3) dcn_bwd_scatter_kernel(const __gr
       const int hl = (int)hf, wl = (int)wf;
       mlh = h - hf;
       mlw = w - wf;
-      if ((h > -1.f) && (w > -1.f) && (h < (float)P.H) && (w < (float)P.W) && !(a.dbg & 1)) {
+      if ((h > -1.f) && (w > -1.f) && (h < (float)P.H) && (w < (float)P.W) && !DCN_SKIP(1)) {
         const bool r0 = hl >= 0, r1 = hl + 1 <= P.H - 1, c0 = wl >= 0, c1 = wl + 1 <= P.W - 1;
         mval = (r0 && c0 ? 1u : 0u) | (r0 && c1 ? 2u : 0u) | (r1 && c0 ? 4u : 0u) |
                (r1 && c1 ? 8u : 0u);
@@ -174,7 +174,7 @@ __global__ void __launch_bounds__(kThreads, 3) dcn_bwd_scatter_kernel(const __gr
             }
             S[c] += sp.x + sp.y;
           }
-          if (!(a.dbg & 2)) {
+          if (!DCN_SKIP(2)) {
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
               if (cval & (1u << c)) {

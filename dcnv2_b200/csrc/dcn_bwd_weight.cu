@@ -33,7 +33,7 @@ namespace dcn {
 namespace {
 
 #define DCN_TS(slot) \
-  do { if (a.ts && blockIdx.x == 0 && lane == 0 && (slot) < 1024) a.ts[(slot)] = globaltimer(); } while (0)
+  do { if (DCN_STUDY_ON && a.ts && blockIdx.x == 0 && lane == 0 && (slot) < 1024) a.ts[(slot)] = globaltimer(); } while (0)
 
 constexpr int kThreads = 192;
 constexpr int kLoadWarp = 4;
@@ -180,7 +180,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const uint64_t ad = gdirect ? sw128_desc(at + m * kATile + kk * 32, 16, 1024)
                                           : sw128_desc(at + m * kATile + kk * 2048, 8192, 1024);
               const uint64_t bd = sw128_desc(bt + (uint32_t)(n0 >> 6) * 8192u + kk * 2048, 8192, 1024);
-              if (!(a.dbg & 4)) umma_f16(dt, ad, bd, idesc, (kl > kl0 || kk > 0) ? 1u : 0u);
+              if (!DCN_SKIP(4)) umma_f16(dt, ad, bd, idesc, (kl > kl0 || kk > 0) ? 1u : 0u);
               if constexpr (NS == 2) {
                 const uint64_t adl = sw128_desc(at + aBytes + m * kATile + kk * 2048, 8192, 1024);
                 const uint64_t bdl =
@@ -214,7 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s = bs;
         const uint32_t ph = bph;
         if (++bs == S) { bs = 0; bph ^= 1u; }
-        if (!mbar_wait(full0 + 8 * s, ph, a.err, &abort_flag)) { ok = false; break; }
+        if (!mbar_wait_warp(full0 + 8 * s, ph, a.err, &abort_flag)) { ok = false; break; }
         const uint32_t at = sbase + s * stageBytes;
 #pragma unroll
         for (int m = 0; m < kMaxMT; ++m) {
@@ -239,7 +239,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     // ------------------------------------------------ epilogue: TMEM -> fp32 red.add
-    if (mbar_wait(accf, 0, a.err, &abort_flag)) {
+    if (mbar_wait_warp(accf, 0, a.err, &abort_flag)) {
       if (warp == 0) DCN_TS(1001);
       tc_fence_after();
       const int q = warp & 3;

@@ -67,7 +67,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 
 // Waits for the phase of parity `parity` to complete.  Returns false (and
 // records a timeout) when the wait exceeds DCN_WAIT_TIMEOUT_NS or when another
-// warp of the CTA has already aborted.
+// warp of the CTA has already aborted.  Single-thread form: for code run by one
+// elected lane (bulk-copy and MMA issuers); whole warps use mbar_wait_warp.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err,
                                           volatile int* abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
@@ -86,6 +87,40 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
         *abort_flag = 1;
         return false;
       }
+    }
+  }
+}
+
+// Warp-collective form of mbar_wait: all 32 lanes of the warp call it and all
+// get the same answer.  Every lane polls the barrier, the loop ends only when
+// every lane has seen the phase complete (__all_sync), and the decision to give
+// up (abort flag or timeout) is taken by lane 0 and broadcast, so no lane leaves
+// early and the warp reaches the next __syncwarp or .sync.aligned instruction
+// converged, whether the wait succeeded or not.
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, int* err,
+                                               volatile int* abort_flag) {
+  if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+  const int lane = threadIdx.x & 31;
+  uint64_t t0 = 0;
+  for (uint32_t i = 1;; ++i) {
+    if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+    if ((i & 255u) == 0u) {
+      int give_up = 0;
+      if (lane == 0) {
+        if (*abort_flag) {
+          give_up = 1;
+        } else {
+          const uint64_t now = globaltimer();
+          if (t0 == 0) {
+            t0 = now;
+          } else if (now - t0 > DCN_WAIT_TIMEOUT_NS) {
+            raise_error(err, DCN_DEVERR_TIMEOUT);
+            *abort_flag = 1;
+            give_up = 1;
+          }
+        }
+      }
+      if (__shfl_sync(0xffffffffu, give_up, 0)) return false;
     }
   }
 }

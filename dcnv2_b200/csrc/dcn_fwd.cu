@@ -32,7 +32,7 @@ namespace dcn {
 namespace {
 
 #define DCN_TS(slot) \
-  do { if (a.ts && blockIdx.x == 0 && lane == 0 && (slot) < 1024) a.ts[(slot)] = globaltimer(); } while (0)
+  do { if (DCN_STUDY_ON && a.ts && blockIdx.x == 0 && lane == 0 && (slot) < 1024) a.ts[(slot)] = globaltimer(); } while (0)
 
 constexpr int kMaxCo = 2048;  // bias staged in smem: Co up to 2048
 constexpr int kGeoTaps = 9;   // (tap, group)s per geometry window
@@ -173,7 +173,7 @@ __global__ void __launch_bounds__(FwdLayout<PW>::kThreads, 1)
     const int HW = P.H * P.W;
     const int row = gt & (kTileM - 1), slot0 = gt / kTileM;
     const int pix = pt * kTileM + row;
-    const bool pv = pix < P.totalP && !(a.dbg & 1);
+    const bool pv = pix < P.totalP && !DCN_SKIP(1);
     const int b = pv ? fdiv(pix, P.fd_howo) : 0, p = pv ? pix - b * HoWo : 0;
     const int ho = fdiv(p, P.fd_wo), wo = p - ho * P.Wo;
     uint32_t rh[KI], rw[KI], rm[KI];
@@ -212,9 +212,11 @@ __global__ void __launch_bounds__(FwdLayout<PW>::kThreads, 1)
   };
 
   // Roles by warpgroup; setmaxnreg at the top of each branch (one instruction
-  // per warpgroup).  Launch: 640 threads x 96 registers; after the split
-  // producers 2 x 4 warps x 160, epilogue 2 x 4 warps x 64, control 4 warps x 32
-  // (= 61440, the launch pool).
+  // per warpgroup).  16-bit types: launch 896 threads x 72 registers; after the
+  // split producers 4 x 4 warps x 80, epilogue 2 x 4 warps x 64, control 4 warps
+  // x 32.  f32: launch 640 threads x 96 registers; producers 2 x 4 warps x 160,
+  // epilogue and control as above.  Both sums are 61440 registers, within the
+  // launch pool (checked by FwdLayout's static_assert).
   if (warp < kProdThreads / 32) {
     regs_inc<kProdRegs>();
     // ------------------------------------------------ gather producers
@@ -252,17 +254,17 @@ __global__ void __launch_bounds__(FwdLayout<PW>::kThreads, 1)
             // window built by the epilogue warps: release the previous one, wait for this one
             __syncwarp();
             if (gcnt > 0 && lane == 0) mbar_arrive(gfree0 + 8 * ((gcnt - 1) & 1u));
-            if (!mbar_wait(gready0 + 8 * (gcnt & 1u), (gcnt >> 1) & 1u, a.err, &abort_flag)) { ok = false; break; }
+            if (!mbar_wait_warp(gready0 + 8 * (gcnt & 1u), (gcnt >> 1) & 1u, a.err, &abort_flag)) { ok = false; break; }
             gbuf = gcnt & 1u;
           } else {
             // built here by all producer threads; two bounded handoffs per window
             __syncwarp();
             if (lane == 0) mbar_arrive(geoe);
-            if (!mbar_wait(geoe, gcnt & 1u, a.err, &abort_flag)) { ok = false; break; }
+            if (!mbar_wait_warp(geoe, gcnt & 1u, a.err, &abort_flag)) { ok = false; break; }
             build_geometry(std::integral_constant<int, kProdThreads>{}, pt, tg, min(nwin_t, nTG - tg), 0, tid);
             __syncwarp();
             if (lane == 0) mbar_arrive(geof);
-            if (!mbar_wait(geof, gcnt & 1u, a.err, &abort_flag)) { ok = false; break; }
+            if (!mbar_wait_warp(geof, gcnt & 1u, a.err, &abort_flag)) { ok = false; break; }
             gbuf = 0;
           }
           ++gcnt;
@@ -291,7 +293,7 @@ __global__ void __launch_bounds__(FwdLayout<PW>::kThreads, 1)
 #pragma unroll
           for (int it = 0; it < BATCH; ++it)
             load_block<T>(xt + ((size_t)(unsigned)geo[i0 + it].gidx + cofs), dxe, dye, v[it]);
-          if (i0 == 0 && !mbar_wait(empty0 + 8 * s, ph ^ 1u, a.err, &abort_flag)) { ok = false; break; }
+          if (i0 == 0 && !mbar_wait_warp(empty0 + 8 * s, ph ^ 1u, a.err, &abort_flag)) { ok = false; break; }
           if (warp == 0 && i0 == 0) DCN_TS(4 * kidx + 1);
 #pragma unroll
           for (int it = 0; it < BATCH; ++it)
@@ -330,7 +332,7 @@ __global__ void __launch_bounds__(FwdLayout<PW>::kThreads, 1)
         bool gok = true;
         for (; gnext <= it + 1 && blockIdx.x + gnext * (int)gridDim.x < nTiles; ++gnext) {
           const int gb = gnext & 1;
-          if (!mbar_wait(gfree0 + 8 * gb, ((gnext >> 1) & 1) ^ 1, a.err, &abort_flag)) { gok = false; break; }
+          if (!mbar_wait_warp(gfree0 + 8 * gb, ((gnext >> 1) & 1) ^ 1, a.err, &abort_flag)) { gok = false; break; }
           const int gpt = (blockIdx.x + gnext * (int)gridDim.x) / P.nCoT;
           build_geometry(std::integral_constant<int, kEpiWarps * 32>{}, gpt, 0, P.K2 * P.dg, gb,
                          tid - kEpiWarp0 * 32);
@@ -339,7 +341,7 @@ __global__ void __launch_bounds__(FwdLayout<PW>::kThreads, 1)
         }
         if (!gok) break;
       }
-      if (!mbar_wait(accf0 + 8 * ab, (it >> 1) & 1, a.err, &abort_flag)) break;
+      if (!mbar_wait_warp(accf0 + 8 * ab, (it >> 1) & 1, a.err, &abort_flag)) break;
       if (warp == kEpiWarp0) DCN_TS(800 + 2 * it);
       tc_fence_after();
       const int pix = pt * kTileM + row;
@@ -393,7 +395,7 @@ __global__ void __launch_bounds__(FwdLayout<PW>::kThreads, 1)
             const uint4 od = make_uint4(__byte_perm(w0.x, w0.y, 0x7632), __byte_perm(w0.z, w0.w, 0x7632),
                                         __byte_perm(w1.x, w1.y, 0x7632), __byte_perm(w1.z, w1.w, 0x7632));
             const int co = ct * NT + c0 + 2 * pp;
-            if (!(a.dbg & 2)) {
+            if (!DCN_SKIP(2)) {
               if (co < P.Co) *reinterpret_cast<uint4*>(yrun + (size_t)co * HoWo) = ev;
               if (co + 1 < P.Co) *reinterpret_cast<uint4*>(yrun + (size_t)(co + 1) * HoWo) = od;
             }
@@ -417,7 +419,7 @@ __global__ void __launch_bounds__(FwdLayout<PW>::kThreads, 1)
             for (int k = 0; k < JH * VPR / 32; ++k) {
               const int j = lane / VPR + k * (32 / VPR);
               const int co = ct * NT + c0 + h * JH + j;
-              if (co < P.Co && !(a.dbg & 2)) {
+              if (co < P.Co && !DCN_SKIP(2)) {
                 const uint4 val = *reinterpret_cast<const uint4*>(stg + j * 32 + cvl * EPV);
                 *reinterpret_cast<uint4*>(yrun + (size_t)co * HoWo) = val;
               }
@@ -429,7 +431,7 @@ __global__ void __launch_bounds__(FwdLayout<PW>::kThreads, 1)
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int co = ct * NT + c0 + j;
-            if (pv && co < P.Co && !(a.dbg & 2))
+            if (pv && co < P.Co && !DCN_SKIP(2))
               yb[(size_t)co * HoWo] = Elem<T>::from_f(a.mma_bias ? v[j] : v[j] + sbias[co]);
           }
         }
@@ -459,7 +461,7 @@ __global__ void __launch_bounds__(FwdLayout<PW>::kThreads, 1)
       }
     }
     } else {
-    // ------------------------------------------------ MMA issuer (warp 13; warps 14-15 idle)
+    // ------------------------------------------------ MMA issuer (warp kMmaWarp: 25 for 16-bit types, 17 for f32; the next two warps idle)
     if (warp == kMmaWarp && lane == 0) {
       const uint32_t idesc = make_idesc(OpOf<T>::kBF16, 0, 0, kTileM, NT);
       uint32_t kidx = 0;
@@ -489,7 +491,7 @@ __global__ void __launch_bounds__(FwdLayout<PW>::kThreads, 1)
           for (int kk = 0; kk < 4; ++kk) {
             const uint64_t ad = sw128_desc(at + kk * 32, 16, 1024);
             const uint64_t bd = sw128_desc(bt + kk * 32, 16, 1024);
-            if (!(a.dbg & 4)) umma_f16(dt, ad, bd, idesc, (mbias || (kc | kk) != 0) ? 1u : 0u);
+            if (!DCN_SKIP(4)) umma_f16(dt, ad, bd, idesc, (mbias || (kc | kk) != 0) ? 1u : 0u);
             if constexpr (NS == 2) {
               const uint64_t adl = sw128_desc(at + kATile + kk * 32, 16, 1024);
               const uint64_t bdl = sw128_desc(bt + bTile + kk * 32, 16, 1024);
@@ -538,17 +540,20 @@ int launch_forward(const FwdArgs& a, cudaStream_t stream) {
   const size_t geoBytes = NB * geoWin + biasBytes;
   int S = (int)((kFwdSmemBudget - 1024 - geoBytes) / stageBytes);
   if (S > kMaxStages) S = kMaxStages;
+#ifdef DCN_STUDY
   static const int study_stages = [] {   // study switch DCN_FWD_STAGES: fewer stages, more L1
     const char* e = getenv("DCN_FWD_STAGES");
     return e ? atoi(e) : 0;
   }();
   if (study_stages >= 2 && study_stages < S) S = study_stages;
+#endif
   if (S < 2) return DCN_E_UNSUPPORTED;
   FwdArgs args = a;
   args.stages = S;
   args.geo_bufs = NB;
   args.mma_bias = mma_bias;
   const size_t smem = 1024 + (size_t)S * stageBytes + geoBytes;
+#ifdef DCN_STUDY
   static const int study_carve = [] {   // study switch DCN_FWD_CARVE: shared-memory carveout (%)
     const char* e = getenv("DCN_FWD_CARVE");
     if (e != nullptr) {
@@ -560,6 +565,7 @@ int launch_forward(const FwdArgs& a, cudaStream_t stream) {
     return -1;
   }();
   (void)study_carve;
+#endif
   const int nTiles = P.nPT * P.nCoT;
   int grid = nTiles < a.num_sms ? nTiles : a.num_sms;
   if (grid <= 0) return DCN_OK;

@@ -8,6 +8,19 @@
 
 namespace dcn {
 
+// Study builds (-DDCN_STUDY, never the shipped library) honour measurement
+// switches: DCN_DEBUG_SKIP drops parts of the kernels' work (results are then
+// wrong), DCN_DEBUG_TS records per-stage timestamps of CTA 0, DCN_FWD_STAGES /
+// DCN_FWD_CARVE / DCN_GOUT_PACKED change launch choices.  A normal build compiles
+// all of that out: the kernels cannot skip work whatever the environment holds.
+#ifdef DCN_STUDY
+#define DCN_STUDY_ON 1
+#else
+#define DCN_STUDY_ON 0
+#endif
+// true when study bit `bit` of the launch's skip mask is set (always false in a normal build)
+#define DCN_SKIP(bit) (DCN_STUDY_ON && (a.dbg & (bit)))
+
 constexpr int kMaxStages = 12;
 constexpr int kMaxASlots = 16;
 constexpr size_t kFwdSmemBudget = 218 * 1024;  // dynamic smem of the forward kernel

@@ -11,7 +11,8 @@ The module is used only as a checker: by ``tests/golden/make_ref_golden.py`` to 
 the C oracle against the reference's real kernels on a B200, and by GPU parity
 tests when the ``.so`` is present.  It is never on the product path.
 
-Usage: ``python oracle/build_ref.py [REFERENCE_DIR]``.
+Usage: ``python oracle/build_ref.py REFERENCE_DIR`` (or with ``DCN_REFERENCE_DIR``
+set in the environment).
 """
 import os
 import sys
@@ -42,4 +43,7 @@ def build(ref_dir: str) -> None:
 
 
 if __name__ == "__main__":
-    build(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("DCN_REFERENCE_DIR", "/root/reference"))
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("DCN_REFERENCE_DIR")
+    if not ref:
+        raise SystemExit("usage: build_ref.py REFERENCE_DIR (or set DCN_REFERENCE_DIR)")
+    build(ref)

@@ -81,3 +81,16 @@ SMALL = [
     Case("thin_h1", 2, 16, 1, 9, 24, 3, 3),
     Case("thin_w1", 1, 16, 6, 1, 24, 3, 3, off_std=2.0),
 ]
+
+
+def record(test: str, errs: dict, tol: float) -> None:
+    """Appends the achieved errors of a parity test as one JSON line to the file
+    named by DCN_PARITY_LOG (when set), so the margins of a GPU run can be read
+    back and tabulated."""
+    import json
+    import os
+    path = os.environ.get("DCN_PARITY_LOG")
+    if not path:
+        return
+    with open(path, "a") as f:
+        f.write(json.dumps({"test": test, "tol": tol, "errors": errs}) + "\n")

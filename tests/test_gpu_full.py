@@ -1,0 +1,135 @@
+"""Parity at the benchmark configurations' real sizes ([1],
+[2] and [4]), where the kernels take paths the small cases never reach:
+several persistent tiles per CTA, many pixel chunks of the weight-gradient
+split, full 32-bit index ranges.
+
+* configs[0] (fp32, B=8, C=64, 128x128, Co=256) and the three fp16 ResNet-50
+  layers of configs[1]: every output and gradient against the float64 C oracle
+  on the whole batch.
+* configs[4] (B=4, C=96, 97x131, Co=160, 5x5, s2 p4 d2 dg2, offsets N(0,8),
+  masks sigmoid(N(0,3))), fp32 and bf16: against the float64 oracle, whole batch.
+* configs[2] (bf16, B=32, C=512, 32x32, Co=512, dg=4): the per-sample tensors
+  (output, grad_input, grad_offset, grad_mask) of samples 0 and 31 against the
+  oracle run on those two samples; grad_weight and grad_bias (sums over the
+  whole batch) against torchvision's deform_conv2d run on the GPU in float64
+  (the same arithmetic; torchvision differs from the reference only in
+  grad_offset at integer sample coordinates, which is not compared with it).
+* The bf16 README layer against the float64 oracle on the UNROUNDED float32
+  inputs: the north star's "bf16 within 1e-2 of the fp32 result".
+
+Tolerances (max|a-b| / max|b| per tensor, as in the other parity tests): 1e-4
+for float32, 1e-2 for float16 / bfloat16.  Every achieved error is printed in
+the assertion message and, with DCN_PARITY_LOG set, appended to that file.
+"""
+import functools
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from dcn_cases import Case, make_inputs, record, rel_err
+
+NAMES = ["output", "grad_input", "grad_offset", "grad_mask", "grad_weight", "grad_bias"]
+TOL = {torch.float32: 1e-4, torch.float16: 1e-2, torch.bfloat16: 1e-2}
+
+README = Case("c0_readme", 8, 64, 128, 128, 256, 3, 3, off_std=1.5)
+RESNET = [Case("c1_s1", 16, 128, 64, 64, 128, 3, 3), Case("c1_s2", 16, 256, 32, 32, 256, 3, 3),
+          Case("c1_s3", 16, 512, 16, 16, 512, 3, 3)]
+EDGE = Case("c4_edge", 4, 96, 97, 131, 160, 5, 5, stride=2, pad=4, dil=2, dg=2, off_std=8.0, mask_std=3.0)
+C512 = Case("c2_c512_dg4", 32, 512, 32, 32, 512, 3, 3, dg=4, off_std=2.0)
+
+
+def _cuda_run(case, tensors):
+    from dcnv2_b200 import _C
+    x, w, b, off, m, gy = [None if t is None else t.cuda() for t in tensors]
+    s, p, d, dg = case.stride, case.pad, case.dil, case.dg
+    y = _C.dcn_v2_forward(x, w, m, off, b, s, s, p, p, d, d, dg)
+    grads = _C.dcn_v2_backward(x, w, m, off, b, gy, s, s, p, p, d, d, dg)
+    torch.cuda.synchronize()
+    return [t.double().cpu().numpy() for t in (y, *grads)]
+
+
+def _oracle_run(case, tensors):
+    x, w, b, off, m, gy = [None if t is None else t.double().numpy() for t in tensors]
+    s, p, d, dg = case.stride, case.pad, case.dil, case.dg
+    y = oracle.forward(x, w, b, off, m, s, p, d, dg)
+    return [y, *oracle.backward(x, w, off, m, gy, s, p, d, dg)]
+
+
+@functools.lru_cache(maxsize=2)
+def _oracle_fp32_inputs(case):
+    """The float64 oracle on the float32 inputs (shared by the fp32 and the
+    bf16-against-fp32 tests of the same case)."""
+    return _oracle_run(case, make_inputs(case))
+
+
+def _compare(label, got, ref, tol, names=NAMES):
+    errs = {n: rel_err(a, r) for n, a, r in zip(names, got, ref)}
+    record(label, errs, tol)
+    bad = {k: v for k, v in errs.items() if not v <= tol}
+    assert not bad, f"{label}: errors {errs} (tol {tol})"
+
+
+@pytest.mark.gpu
+def test_c0_readme_fp32_full():
+    case = README
+    _compare("c0_readme_fp32", _cuda_run(case, make_inputs(case)), _oracle_fp32_inputs(case), 1e-4)
+
+
+@pytest.mark.gpu
+def test_c0_readme_bf16_against_fp32_result():
+    """bf16 operator on bf16-rounded inputs against the float64 result of the
+    unrounded float32 inputs (the whole rounding of the inputs counts)."""
+    case = README
+    t32 = make_inputs(case)
+    got = _cuda_run(case, [t.to(torch.bfloat16) for t in t32])
+    _compare("c0_readme_bf16_vs_fp32", got, _oracle_fp32_inputs(case), 1e-2)
+
+
+@pytest.mark.gpu
+def test_c0_readme_bf16_against_rounded_inputs():
+    case = README
+    t = [v.to(torch.bfloat16) for v in make_inputs(case)]
+    _compare("c0_readme_bf16", _cuda_run(case, t), _oracle_run(case, t), 1e-2)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", RESNET, ids=lambda c: c.name)
+def test_c1_resnet_fp16_full(case):
+    t = [v.to(torch.float16) for v in make_inputs(case)]
+    _compare(f"{case.name}_fp16", _cuda_run(case, t), _oracle_run(case, t), 1e-2)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16], ids=["fp32", "bf16"])
+def test_c4_edge_full(dtype):
+    case = EDGE
+    t = [v.to(dtype) for v in make_inputs(case)]
+    _compare(f"c4_edge_{str(dtype).split('.')[-1]}", _cuda_run(case, t), _oracle_run(case, t), TOL[dtype])
+
+
+@pytest.mark.gpu
+def test_c2_c512_dg4_bf16_full():
+    from torchvision.ops import deform_conv2d
+    case = C512
+    t = [v.to(torch.bfloat16) for v in make_inputs(case)]
+    got = _cuda_run(case, t)
+    # per-sample tensors of the first and the last sample against the oracle
+    idx = [0, case.B - 1]
+    sub = [t[0][idx], t[1], t[2], t[3][idx], t[4][idx], t[5][idx]]
+    ref = _oracle_run(case, sub)
+    _compare("c2_c512_dg4_bf16_samples", [g[idx] for g in got[:4]], ref[:4], 1e-2, NAMES[:4])
+    # batch sums against torchvision on the GPU in float64
+    x, w, b, off, m, gy = [v.double().cuda() for v in t]
+    x.requires_grad_(True)
+    w.requires_grad_(True)
+    b.requires_grad_(True)
+    s, p, d = case.stride, case.pad, case.dil
+    y = deform_conv2d(x, off, w, b, stride=(s, s), padding=(p, p), dilation=(d, d), mask=m)
+    y.backward(gy)
+    torch.cuda.synchronize()
+    tv = [y.detach(), x.grad, w.grad, b.grad]
+    f = lambda v: v.double().cpu().numpy()  # noqa: E731
+    _compare("c2_c512_dg4_bf16_tv", [got[0], got[1], got[4], got[5]], [f(v) for v in tv], 1e-2,
+             ["output", "grad_input", "grad_weight", "grad_bias"])

@@ -9,7 +9,7 @@ import pytest
 import torch
 
 import oracle
-from dcn_cases import SMALL, make_inputs, rel_err
+from dcn_cases import SMALL, make_inputs, record, rel_err
 
 TOL = {torch.float32: 1e-4, torch.float16: 1e-2, torch.bfloat16: 1e-2}
 DTYPES = [torch.float32, torch.bfloat16, torch.float16]
@@ -46,6 +46,7 @@ def test_forward_backward_vs_oracle(case, dtype):
             assert g is None
             continue
         errs[name] = rel_err(g.float().cpu().numpy(), r)
+    record(f"{case.name}_{str(dtype).split('.')[-1]}", errs, tol)
     bad = {k: v for k, v in errs.items() if not v <= tol}
     assert not bad, f"{case.name} {dtype}: errors {errs} (tol {tol})"
 
