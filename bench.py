@@ -351,8 +351,8 @@ def run_stack(args):
     """Data-parallel training step of a stack of DCN modules (the reference's `DCN`
     module API: offset/mask predictor conv, sigmoid mask, DCNv2 op), ReLU between
     layers, the global batch split over the ranks (strong scaling), every layer's
-    weight and bias gradients (the predictor's included) summed over the ranks with
-    one bucketed NCCL all-reduce."""
+    weight and bias gradients (the predictor's included) averaged over the ranks by
+    NCCL, one bucket per layer started as soon as that layer's backward is done."""
     import torch.distributed as dist
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -387,7 +387,9 @@ def run_stack(args):
             h = torch.relu(torch.nn.functional.conv2d(h, lay.weight, lay.bias, padding=k // 2))
         for lay in layers:
             lay.to(dtype)
-    bucket = GradBucket(layers)
+    # each layer's gradients are all-reduced as soon as its backward has produced
+    # them, overlapping the backward of the layers below (not under graph capture)
+    bucket = GradBucket(layers, overlap=world > 1 and not args.graph, average=True)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
     timed = make_timer(world, dev, stream, flush)
@@ -403,7 +405,7 @@ def run_stack(args):
                 hh = torch.relu(hh)
         hh.backward(gin)
         if world > 1:
-            bucket.allreduce(average=True)
+            bucket.allreduce()
 
     for _ in range(args.warmup):
         step(x, gy)

@@ -178,6 +178,18 @@ bool make_gout_tmap(const Plan& P, const void* gout, TmaDesc* out) {
   return true;
 }
 
+// Strides of the offset and mask tensors (see Plan::off_bs); `om`: both are the
+// channels of one predictor output [B][3*dg*K2][Ho][Wo], offsets first.
+void set_offset_mask_strides(Plan* p, int om) {
+  const int noff = 2 * p->dg * p->K2, nmsk = p->dg * p->K2;
+  const int ctot_off = om ? 3 * nmsk : noff, ctot_msk = om ? 3 * nmsk : nmsk;
+  p->off_bs = ctot_off * p->HoWo;
+  p->msk_bs = ctot_msk * p->HoWo;
+  p->off_cs = p->msk_cs = p->HoWo;
+  p->off_ps = p->msk_ps = 1;
+  p->mask_logit = om;
+}
+
 int make_plan(const dcn_desc* d, Plan* p, int num_sms) {
   if (d == nullptr || p == nullptr) return DCN_E_NULLPTR;
   memset(p, 0, sizeof(*p));
@@ -278,9 +290,7 @@ int make_plan(const dcn_desc* d, Plan* p, int num_sms) {
   p->fd_kw = make_fastdiv((uint32_t)p->kw);
   p->fd_dg = make_fastdiv((uint32_t)p->dg);
   p->fd_ntg = make_fastdiv((uint32_t)(p->K2 * p->dg));
-  p->off_bs = 2 * p->dg * p->K2 * p->HoWo;
-  p->msk_bs = p->dg * p->K2 * p->HoWo;
-  p->mask_logit = 0;
+  set_offset_mask_strides(p, 0);
   return DCN_OK;
 }
 
@@ -324,8 +334,7 @@ static int forward_impl(const dcn_desc* d, const void* input, const void* weight
   int rc = make_plan(d, &P, device_sms());
   if (rc != DCN_OK) return rc;
   if (om) {
-    P.off_bs = P.msk_bs = 3 * P.dg * P.K2 * P.HoWo;
-    P.mask_logit = 1;
+    set_offset_mask_strides(&P, 1);
     mask = offset ? static_cast<const uint8_t*>(offset) + (size_t)2 * P.dg * P.K2 * P.HoWo * P.esz : nullptr;
   }
   if (!workspace) return DCN_E_NULLPTR;
@@ -386,8 +395,7 @@ static int backward_impl(const dcn_desc* d, const void* input, const void* weigh
   if (rc != DCN_OK) return rc;
   if (om) {
     const size_t mofs = (size_t)2 * P.dg * P.K2 * P.HoWo * P.esz;
-    P.off_bs = P.msk_bs = 3 * P.dg * P.K2 * P.HoWo;
-    P.mask_logit = 1;
+    set_offset_mask_strides(&P, 1);
     mask = offset ? static_cast<const uint8_t*>(offset) + mofs : nullptr;
     grad_mask = grad_offset ? static_cast<uint8_t*>(grad_offset) + mofs : nullptr;
   }

@@ -89,8 +89,8 @@ __global__ void __launch_bounds__(kThreads, 3) dcn_bwd_scatter_kernel(const __gr
     const bool mpv = mpix < pend;
     const int mb = mpv ? fdiv(mpix, P.fd_howo) : 0;
     const int mp = mpv ? mpix - mb * HoWo : 0;
-    const int obase = mb * P.off_bs + (g * 2 * P.K2 + 2 * t) * HoWo + mp;
-    const int mbase = mb * P.msk_bs + (g * P.K2 + t) * HoWo + mp;
+    const int obase = mb * P.off_bs + (g * 2 * P.K2 + 2 * t) * P.off_cs + mp * P.off_ps;
+    const int mbase = mb * P.msk_bs + (g * P.K2 + t) * P.msk_cs + mp * P.msk_ps;
     float mlh = 0.f, mlw = 0.f, mm = 0.f;
     int mgidx = 0;
     uint32_t mval = 0u;
@@ -98,7 +98,7 @@ __global__ void __launch_bounds__(kThreads, 3) dcn_bwd_scatter_kernel(const __gr
       const int i = fdiv(t, P.fd_kw), j = t - i * P.kw;
       const int ho = fdiv(mp, P.fd_wo), wo = mp - ho * P.Wo;
       const float h = (float)(ho * P.sh - P.ph + i * P.dh) + ldf(off + obase);
-      const float w = (float)(wo * P.sw - P.pw + j * P.dw) + ldf(off + obase + HoWo);
+      const float w = (float)(wo * P.sw - P.pw + j * P.dw) + ldf(off + obase + P.off_cs);
       mm = ldf(msk + mbase);
       if (P.mask_logit) mm = 1.f / (1.f + __expf(-mm));   // sigmoid of a predictor logit
       const float hf = floorf(h), wf = floorf(w);
@@ -179,13 +179,13 @@ __global__ void __launch_bounds__(kThreads, 3) dcn_bwd_scatter_kernel(const __gr
             for (int c = 0; c < 4; ++c) {
               if (cval & (1u << c)) {
                 const float sk = wc[c];
-                float* dst = a.gx_nhwc + (size_t)(unsigned)((gidx + d[c]) * P.CS + cofs + 4 * q);
+                float* dst = a.gx_nhwc + (size_t)(unsigned)((gidx + d[c]) * P.CS + cofs);
                 const float2 s0 = mul2(make_float2(gc[0], gc[1]), sk);
                 const float2 s1 = mul2(make_float2(gc[2], gc[3]), sk);
                 const float2 s2 = mul2(make_float2(gc[4], gc[5]), sk);
                 const float2 s3 = mul2(make_float2(gc[6], gc[7]), sk);
-                red_add_v4(dst, s0.x, s0.y, s1.x, s1.y);
-                red_add_v4(dst + 32, s2.x, s2.y, s3.x, s3.y);
+                red_add_v4(dst + slice_lo(q), s0.x, s0.y, s1.x, s1.y);
+                red_add_v4(dst + slice_hi(q), s2.x, s2.y, s3.x, s3.y);
               }
             }
           }
@@ -235,7 +235,7 @@ __global__ void __launch_bounds__(kThreads, 3) dcn_bwd_scatter_kernel(const __gr
     }
     if (mpv) {
       goff[obase] = Elem<T>::from_f(oh * mm);
-      goff[obase + HoWo] = Elem<T>::from_f(ow * mm);
+      goff[obase + P.off_cs] = Elem<T>::from_f(ow * mm);
       // with logits: d/dx sigmoid(x) = s (1 - s)
       gmsk[mbase] = Elem<T>::from_f(P.mask_logit ? om * mm * (1.f - mm) : om);
     }

@@ -257,9 +257,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_ld8(tb + c0, v);
             if (co < P.Co) {
               // packed columns c0..c0+7 are logical channels blk+4q' .. and blk+32+4q' ..
-              const int lc = (c0 & ~63) + 4 * ((c0 & 63) >> 3);
-              red_add_v4(dst + lc, v[0], v[1], v[2], v[3]);
-              red_add_v4(dst + lc + 32, v[4], v[5], v[6], v[7]);
+              const int blk = c0 & ~63, qs = (c0 & 63) >> 3;
+              red_add_v4(dst + blk + slice_lo(qs), v[0], v[1], v[2], v[3]);
+              red_add_v4(dst + blk + slice_hi(qs), v[4], v[5], v[6], v[7]);
             }
           }
         }

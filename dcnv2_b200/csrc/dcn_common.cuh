@@ -495,10 +495,23 @@ __device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, 
 // 32 + 4q + (r - 4) (r >= 4).  A lane's 16-byte slice q is then logical channels
 // [4q, 4q+4) and [32+4q, 32+4q+4), so the grad_input scatter (in logical order)
 // fills whole 32-byte sectors with two lanes per red.add instruction.
+// DCN_PERM=0 (study builds) keeps the logical order instead: lane q then owns
+// logical channels [8q, 8q+8), one 32-byte sector of fp32 per lane.
+#ifndef DCN_PERM
+#define DCN_PERM 1
+#endif
 __host__ __device__ __forceinline__ int perm_logical(int pp) {
+#if DCN_PERM
   const int q = pp >> 3, r = pp & 7;
   return r < 4 ? 4 * q + r : 32 + 4 * q + (r - 4);
+#else
+  return pp;
+#endif
 }
+// Logical channel (inside the 64-channel block) of the first and of the fifth
+// element of physical 16-byte slice q: where a lane's two fp32 quadruples go.
+__host__ __device__ __forceinline__ int slice_lo(int q) { return DCN_PERM ? 4 * q : 8 * q; }
+__host__ __device__ __forceinline__ int slice_hi(int q) { return DCN_PERM ? 32 + 4 * q : 8 * q + 4; }
 
 // ---------------------------------------------------------------- sampling geometry
 // Bilinear sampling geometry of one (pixel, tap, group): the four corner

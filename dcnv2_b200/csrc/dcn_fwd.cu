@@ -184,10 +184,10 @@ __global__ void __launch_bounds__(FwdLayout<PW>::kThreads, 1)
       if (pv && slot < wt) {
         const int tgi = tg0 + slot;
         const int t = fdiv(tgi, P.fd_dg), gi = tgi - t * P.dg;
-        const int ob = b * P.off_bs + (gi * 2 * P.K2 + 2 * t) * HoWo + p;
+        const int ob = b * P.off_bs + (gi * 2 * P.K2 + 2 * t) * P.off_cs + p * P.off_ps;
         rh[k] = ldg_raw<T>(off + ob);
-        rw[k] = ldg_raw<T>(off + ob + HoWo);
-        rm[k] = ldg_raw<T>(msk + b * P.msk_bs + (gi * P.K2 + t) * HoWo + p);
+        rw[k] = ldg_raw<T>(off + ob + P.off_cs);
+        rm[k] = ldg_raw<T>(msk + b * P.msk_bs + (gi * P.K2 + t) * P.msk_cs + p * P.msk_ps);
       }
     }
 #pragma unroll

@@ -374,7 +374,7 @@ __global__ void __launch_bounds__(256) pack_input_rt_kernel(const T* __restrict_
     uint4 row[8], col[8];
 #pragma unroll
     for (int r = 0; r < 8; ++r) {
-      const int cc = cb + (r < 4 ? 4 * q + r : 32 + 4 * q + r - 4);   // logical channel of position 8q + r
+      const int cc = cb + perm_logical(8 * q + r);   // logical channel of position 8q + r
       row[r] = cc < Cg ? ldg_nc_v4(x + ((size_t)b * C + g * Cg + cc) * HW + p8 * 8) : make_uint4(0u, 0u, 0u, 0u);
     }
     transpose8x8_b16(row, col);

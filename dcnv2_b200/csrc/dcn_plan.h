@@ -68,11 +68,13 @@ struct Plan {
   size_t wd_tile_bytes;   // one backward-data weight tile (gNC rows x 128 B x nsplit)
   // divisors of the index arithmetic in the kernels
   FastDiv fd_howo, fd_wo, fd_kw, fd_dg, fd_ntg;
-  // offset / mask addressing: elements per batch of the offset and mask tensors
-  // (2*dg*K2*HoWo and dg*K2*HoWo for separate tensors; 3*dg*K2*HoWo for both when
-  // they are the channels of one predictor output), and whether the mask values
-  // are logits that the kernels pass through a sigmoid
-  int off_bs, msk_bs, mask_logit;
+  // offset / mask addressing: element (b, channel, pixel) of the offset tensor is
+  // at b*off_bs + channel*off_cs + pixel*off_ps, likewise the mask (NCHW: channel
+  // stride HoWo, pixel stride 1; channels-last: channel stride 1, pixel stride =
+  // the channel count; the predictor output of the fused path holds both, with
+  // 3*dg*K2 channels), and whether the mask values are logits that the kernels
+  // pass through a sigmoid
+  int off_bs, off_cs, off_ps, msk_bs, msk_cs, msk_ps, mask_logit;
 };
 
 // Fills `p` from `d`; returns DCN_OK or DCN_E_INVALID / DCN_E_UNSUPPORTED.

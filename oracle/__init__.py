@@ -49,6 +49,8 @@ def _load():
         g.argtypes = [p, p, p, p, p, p, p, p, p, p, ip]
         g.restype = None
     lib.dcn_oracle_num_threads.restype = ctypes.c_int
+    lib.dcn_oracle_set_coord_f32.argtypes = [ctypes.c_int]
+    lib.dcn_oracle_set_coord_f32.restype = None
     lib.dcn_oracle_set_threads.argtypes = [ctypes.c_int]
     lib.dcn_oracle_set_threads.restype = None
     _lib = lib
@@ -87,9 +89,12 @@ def _np(a, dt):
 
 
 def forward(x, weight, bias, offset, mask, stride=1, padding=0, dilation=1, deformable_groups=1,
-            dtype=np.float64):
-    """y = DCNv2(x; offset, mask, weight, bias) in ``dtype`` (float64 or float32)."""
+            dtype=np.float64, coord="f32"):
+    """y = DCNv2(x; offset, mask, weight, bias) in ``dtype`` (float64 or float32).
+    ``coord="f32"`` forms sample positions in float32 as the reference does;
+    ``"f64"`` in ``dtype`` (torchvision's double kernels)."""
     lib = _load()
+    lib.dcn_oracle_set_coord_f32(1 if coord == "f32" else 0)
     sfx = "f64" if dtype == np.float64 else "f32"
     ct = ctypes.c_double if sfx == "f64" else ctypes.c_float
     x, weight, offset, mask = (_np(a, dtype) for a in (x, weight, offset, mask))
@@ -106,10 +111,12 @@ def forward(x, weight, bias, offset, mask, stride=1, padding=0, dilation=1, defo
 
 
 def backward(x, weight, offset, mask, grad_out, stride=1, padding=0, dilation=1,
-             deformable_groups=1, dtype=np.float64):
+             deformable_groups=1, dtype=np.float64, coord="f32"):
     """Returns (grad_input, grad_offset, grad_mask, grad_weight, grad_bias), the
-    order of the reference's ``dcn_v2_backward`` (com.cu:845-847)."""
+    order of the reference's ``dcn_v2_backward`` (com.cu:845-847).  ``coord`` as
+    in ``forward``."""
     lib = _load()
+    lib.dcn_oracle_set_coord_f32(1 if coord == "f32" else 0)
     sfx = "f64" if dtype == np.float64 else "f32"
     ct = ctypes.c_double if sfx == "f64" else ctypes.c_float
     x, weight, offset, mask, grad_out = (_np(a, dtype) for a in (x, weight, offset, mask, grad_out))

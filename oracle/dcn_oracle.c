@@ -28,6 +28,15 @@
  *
  * Two instantiations: _f64 (double arithmetic; the parity oracle) and _f32
  * (float arithmetic, OpenMP-parallel; the CPU baseline timed by bench.py).
+ *
+ * Sample coordinates.  The reference forms every sample position in float32:
+ * h = (h_in + i) + offset_h as one float addition (com.cu:184-185, 479-480,
+ * 587-588, 688-689), and the cell (floor) and the one-sided coordinate weights
+ * of the backward are discontinuous at integer positions, so the double oracle
+ * forms the position the same way by default (dcn_oracle_set_coord_f32(1)):
+ * a position within one float32 ulp of an integer then lands in the same cell
+ * as in the reference.  dcn_oracle_set_coord_f32(0) adds in the arithmetic type
+ * instead (how torchvision's double kernels do it; used for its fixtures).
  */
 #include <math.h>
 #include <stdlib.h>
@@ -47,6 +56,13 @@ static int out_size(int in, int k, int s, int p, int d) {
 
 int dcn_oracle_out_h(int H, int kh, int sh, int ph, int dh) { return out_size(H, kh, sh, ph, dh); }
 int dcn_oracle_out_w(int W, int kw, int sw, int pw, int dw) { return out_size(W, kw, sw, pw, dw); }
+
+static int g_coord_f32 = 1;
+void dcn_oracle_set_coord_f32(int on) { g_coord_f32 = on ? 1 : 0; }
+
+/* sample position base + off, in float32 (the reference) or in the type T */
+#define DCN_COORD(T, base, off) \
+    (g_coord_f32 ? (T)((float)(base) + (float)(off)) : (T)(base) + (off))
 
 int dcn_oracle_num_threads(void) {
 #ifdef _OPENMP
@@ -112,8 +128,8 @@ static void im2col_##SFX(const dcn_oracle_shape *s, const T *x, const T *off, co
             T *col = cols + ((size_t)c * K2 + t) * P;                                           \
             for (int p = 0; p < P; ++p) {                                                       \
                 const int ho = p / s->Wo, wo = p % s->Wo;                                       \
-                const T h = (T)(ho * s->sh - s->ph + i * s->dh) + ob[(2 * t) * P + p];          \
-                const T w = (T)(wo * s->sw - s->pw + j * s->dw) + ob[(2 * t + 1) * P + p];      \
+                const T h = DCN_COORD(T, ho * s->sh - s->ph + i * s->dh, ob[(2 * t) * P + p]);          \
+                const T w = DCN_COORD(T, wo * s->sw - s->pw + j * s->dw, ob[(2 * t + 1) * P + p]);      \
                 T v = 0;                                                                        \
                 if (h > -1 && w > -1 && h < s->H && w < s->W) v = bilinear_##SFX(im, s->H, s->W, h, w); \
                 col[p] = v * mb[t * P + p];                                                     \
@@ -187,8 +203,8 @@ void dcn_oracle_backward_##SFX(const T *x, const T *wt, const T *off, const T *m
             T *gmb = gmask + ((size_t)b * s.dg + g) * K2 * P;                                   \
             for (int p = 0; p < P; ++p) {                                                       \
                 const int ho = p / s.Wo, wo = p % s.Wo;                                         \
-                const T h = (T)(ho * s.sh - s.ph + i * s.dh) + ob[(2 * t) * P + p];             \
-                const T w = (T)(wo * s.sw - s.pw + j * s.dw) + ob[(2 * t + 1) * P + p];         \
+                const T h = DCN_COORD(T, ho * s.sh - s.ph + i * s.dh, ob[(2 * t) * P + p]);             \
+                const T w = DCN_COORD(T, wo * s.sw - s.pw + j * s.dw, ob[(2 * t + 1) * P + p]);         \
                 const T m = mb[t * P + p];                                                      \
                 const int valid = (h > -1 && w > -1 && h < s.H && w < s.W);                     \
                 T vh = 0, vw = 0, vm = 0;                                                       \
@@ -216,8 +232,8 @@ void dcn_oracle_backward_##SFX(const T *x, const T *wt, const T *off, const T *m
                 const int i = t / s.kw, j = t % s.kw;                                           \
                 for (int p = 0; p < P; ++p) {                                                   \
                     const int ho = p / s.Wo, wo = p % s.Wo;                                     \
-                    const T h = (T)(ho * s.sh - s.ph + i * s.dh) + ob[(2 * t) * P + p];         \
-                    const T w = (T)(wo * s.sw - s.pw + j * s.dw) + ob[(2 * t + 1) * P + p];     \
+                    const T h = DCN_COORD(T, ho * s.sh - s.ph + i * s.dh, ob[(2 * t) * P + p]);         \
+                    const T w = DCN_COORD(T, wo * s.sw - s.pw + j * s.dw, ob[(2 * t + 1) * P + p]);     \
                     if (!(h > -1 && w > -1 && h < s.H && w < s.W)) continue;                    \
                     const T top = gcol[((size_t)c * K2 + t) * P + p] * mb[t * P + p];           \
                     const int hl = (int)floor(h), wl = (int)floor(w);                           \

@@ -96,3 +96,47 @@ def test_dead_rank_fails_collective_instead_of_hanging():
     res = dict(_run(_failing_worker))
     assert res[1] == "left before the collective"
     assert res[0].startswith("error")
+
+
+def _overlap_worker(rank, world, port, q):
+    """Two small layers; the buckets start from the backward hooks (overlap) and
+    the averaged gradients equal the full-batch mean on every rank."""
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, root)
+    from dcnv2_b200.dp import GradBucket
+    _init(rank, world, port)
+    try:
+        torch.manual_seed(0)
+        layers = [torch.nn.Linear(6, 5).double(), torch.nn.Linear(5, 3).double()]
+        x = torch.randn(8, 6, dtype=torch.float64, generator=torch.Generator().manual_seed(1))
+        per = 8 // world
+        red = GradBucket(layers, overlap=True, average=True)
+        errs = []
+        for _step in range(2):   # hooks re-arm after every allreduce()
+            for lay in layers:
+                lay.zero_grad(set_to_none=True)
+            h = x[rank * per:(rank + 1) * per]
+            for lay in layers:
+                h = torch.tanh(lay(h))
+            h.sum().backward()
+            red.allreduce()
+            got = [p.grad.clone() for lay in layers for p in lay.parameters()]
+            for lay in layers:
+                lay.zero_grad(set_to_none=True)
+            h = x
+            for lay in layers:
+                h = torch.tanh(lay(h))
+            (h.sum() / world).backward()
+            ref = [p.grad.clone() for lay in layers for p in lay.parameters()]
+            errs.append(max(float((a - b).abs().max()) for a, b in zip(got, ref)))
+        q.put((rank, max(errs)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_overlapped_buckets_average_equals_full_batch():
+    res = _run(_overlap_worker)
+    assert len(res) == 2
+    for _, err in res:
+        assert err < 1e-6, err   # fp32 bucket

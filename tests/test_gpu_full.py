@@ -15,7 +15,13 @@ split, full 32-bit index ranges.
   (the same arithmetic; torchvision differs from the reference only in
   grad_offset at integer sample coordinates, which is not compared with it).
 * The bf16 README layer against the float64 oracle on the UNROUNDED float32
-  inputs: the north star's "bf16 within 1e-2 of the fp32 result".
+  inputs: the north star's "bf16 within 1e-2 of the fp32 result" (grad_offset
+  away from the samples that the input rounding moves into another bilinear
+  cell, where it is discontinuous).
+* Sample positions are formed in float32 in the kernels, in the reference
+  (com.cu:184, 479, 587, 688) and in the oracle; grad_offset jumps at integer
+  positions, so a position formed in another precision would land in another
+  cell for the few samples within one ulp of an integer.
 
 Tolerances (max|a-b| / max|b| per tensor, as in the other parity tests): 1e-4
 for float32, 1e-2 for float16 / bfloat16.  Every achieved error is printed in
@@ -77,14 +83,54 @@ def test_c0_readme_fp32_full():
     _compare("c0_readme_fp32", _cuda_run(case, make_inputs(case)), _oracle_fp32_inputs(case), 1e-4)
 
 
+def _cell_flips(case, off_a, off_b):
+    """Samples (b, group, tap, pixel) whose float32 sample position falls in a
+    different bilinear cell, or on the other side of the validity bound, under
+    the two offset tensors.  grad_offset is discontinuous there (the one-sided
+    coordinate weights of com.cu:388-429 switch cells), so rounding the inputs
+    to bf16 may move it by O(1) at those samples whatever the kernel does."""
+    ho_n, wo_n = case.out_hw()
+    K2 = case.kh * case.kw
+    oa = off_a.numpy().astype(np.float32).reshape(case.B, case.dg, K2, 2, ho_n, wo_n)
+    ob = off_b.float().numpy().astype(np.float32).reshape(case.B, case.dg, K2, 2, ho_n, wo_n)
+    t = np.arange(K2)
+    bh = (np.arange(ho_n)[None, :] * case.stride - case.pad + (t // case.kw)[:, None] * case.dil)
+    bw = (np.arange(wo_n)[None, :] * case.stride - case.pad + (t % case.kw)[:, None] * case.dil)
+    bh = bh.astype(np.float32)[None, None, :, :, None]
+    bw = bw.astype(np.float32)[None, None, :, None, :]
+    flips = np.zeros(oa.shape[:3] + (ho_n, wo_n), dtype=bool)
+    ha, wa = bh + oa[:, :, :, 0], bw + oa[:, :, :, 1]
+    hb, wb = bh + ob[:, :, :, 0], bw + ob[:, :, :, 1]
+
+    def valid(h, w):
+        return (h > -1) & (w > -1) & (h < case.H) & (w < case.W)
+
+    flips |= (np.floor(ha) != np.floor(hb)) | (np.floor(wa) != np.floor(wb))
+    flips |= valid(ha, wa) != valid(hb, wb)
+    return flips   # [B][dg][K2][Ho][Wo]
+
+
 @pytest.mark.gpu
 def test_c0_readme_bf16_against_fp32_result():
     """bf16 operator on bf16-rounded inputs against the float64 result of the
-    unrounded float32 inputs (the whole rounding of the inputs counts)."""
+    unrounded float32 inputs (the whole rounding of the inputs counts).
+    grad_offset is compared at the samples whose position stays in the same
+    bilinear cell under the rounding (see _cell_flips; their count is in the
+    record); every other tensor everywhere."""
     case = README
     t32 = make_inputs(case)
-    got = _cuda_run(case, [t.to(torch.bfloat16) for t in t32])
-    _compare("c0_readme_bf16_vs_fp32", got, _oracle_fp32_inputs(case), 1e-2)
+    t16 = [t.to(torch.bfloat16) for t in t32]
+    got = _cuda_run(case, t16)
+    ref = _oracle_fp32_inputs(case)
+    flips = _cell_flips(case, t32[3], t16[3])
+    keep = ~np.repeat(flips[:, :, :, None], 2, axis=3).reshape(got[2].shape)
+    errs = {n: rel_err(a, r) for n, a, r in zip(NAMES, got, ref) if n != "grad_offset"}
+    errs["grad_offset"] = float(np.abs(got[2] - ref[2])[keep].max() / np.abs(ref[2]).max())
+    errs["flipped_samples"] = int(flips.sum())
+    errs["samples"] = int(flips.size)
+    record("c0_readme_bf16_vs_fp32", errs, 1e-2)
+    bad = {k: v for k, v in errs.items() if k in NAMES and not v <= 1e-2}
+    assert not bad, f"c0_readme_bf16_vs_fp32: errors {errs} (tol 1e-2)"
 
 
 @pytest.mark.gpu
