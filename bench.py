@@ -376,6 +376,11 @@ def run_stack(args):
     gen = torch.Generator().manual_seed(100 + rank)
     x = torch.randn(Bl, C, H, W, generator=gen).to(dev, dtype)
     gy = torch.randn(Bl, C, H, W, generator=gen).to(dev, dtype)
+    if args.channels_last:
+        # channels-last activations end to end: the predictor convs and the DCN
+        # operator (DCN_NHWC layout) pass them on without layout passes
+        x = x.contiguous(memory_format=torch.channels_last)
+        gy = gy.contiguous(memory_format=torch.channels_last)
     with torch.no_grad():
         # predictor: random init scaled so the offsets have the configured std
         h = x.float()
@@ -387,6 +392,8 @@ def run_stack(args):
             h = torch.relu(torch.nn.functional.conv2d(h, lay.weight, lay.bias, padding=k // 2))
         for lay in layers:
             lay.to(dtype)
+            if args.channels_last:
+                lay.to(memory_format=torch.channels_last)
     # each layer's gradients are all-reduced as soon as its backward has produced
     # them, overlapping the backward of the layers below (not under graph capture)
     bucket = GradBucket(layers, overlap=world > 1 and not args.graph, average=True)
@@ -474,7 +481,7 @@ def run_stack(args):
                                f"{H}x{W}, global batch {G}, {Bl} per rank, fwd+bwd+all-reduce",
                    "global_batch": G, "parallelism": f"dp{world}",
                    "l2": "flushed before every step (256 MiB write)", "offset_std_px": cfg["off_std"],
-                   "cuda_graph": bool(args.graph)},
+                   "cuda_graph": bool(args.graph), "channels_last": bool(args.channels_last)},
         "fwd_bwd_gemm_tflops": world * 3 * gflop / (ms_step * 1e-3) / 1e12,
         "kernels_ms_per_step": {kk: v[1] / args.steps for kk, v in kernels.items()},
         "roofline": roofline,
@@ -552,6 +559,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-fp32", action="store_true",
                     help="skip the float32 step reported beside a 16-bit run")
+    ap.add_argument("--channels-last", action="store_true",
+                    help="stack workloads: channels-last activations (the operator's NHWC layout)")
     ap.add_argument("--graph", action="store_true",
                     help="stack workloads: capture the training step in a CUDA graph and replay it")
     ap.add_argument("--launch-only", type=int, default=0, metavar="N",

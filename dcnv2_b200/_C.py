@@ -7,6 +7,13 @@ through its C ABI; outputs and the workspace come from PyTorch's caching
 allocator on the tensors' device, and the work is queued on the current CUDA
 stream, as the reference does (com.cu:215, 748).
 
+Channels-last activations: when ``input`` is in PyTorch's ``channels_last``
+memory format, the operator runs in the library's DCN_NHWC layout: offset, mask
+(or the predictor output) and grad_output are taken channels-last (converted if
+they are not), and the output and the input / offset / mask gradients are
+returned channels-last, so stacked layers pass activations on without layout
+passes.  Otherwise everything is NCHW-contiguous, as in the reference.
+
 Errors follow the reference: a CPU tensor raises ``RuntimeError("<name> must be a
 CUDA tensor")`` (com.cu:209-213), a channel mismatch raises ``RuntimeError``
 (com.cu:760-761), and a failing library call raises ``RuntimeError`` with the
@@ -44,7 +51,20 @@ def _check_cuda(**tensors):
             raise RuntimeError(f"{name} is on {t.device}, expected {dev} (all tensors on one device)")
 
 
-def _desc(input, weight, stride_h, stride_w, pad_h, pad_w, dil_h, dil_w, dg, has_bias):
+_CL = torch.channels_last
+
+
+def _is_nhwc(t) -> bool:
+    """True for a 4-D tensor in PyTorch's channels_last memory format (and not
+    also plain contiguous, which happens when C == 1 or H == W == 1)."""
+    return t.dim() == 4 and not t.is_contiguous() and t.is_contiguous(memory_format=_CL)
+
+
+def _dense(t, nhwc):
+    return t.contiguous(memory_format=_CL) if nhwc else t.contiguous()
+
+
+def _desc(input, weight, stride_h, stride_w, pad_h, pad_w, dil_h, dil_w, dg, has_bias, nhwc=False):
     if input.dim() != 4 or weight.dim() != 4:
         raise RuntimeError("input and weight must be 4-D (NCHW / [Co, C, kh, kw])")
     B, C, H, W = input.shape
@@ -54,7 +74,8 @@ def _desc(input, weight, stride_h, stride_w, pad_h, pad_w, dil_h, dil_w, dg, has
     if input.dtype not in _DTYPES:
         raise RuntimeError(f"unsupported dtype {input.dtype}")
     d = _lib.DcnDesc(B, C, H, W, Co, kh, kw, int(stride_h), int(stride_w), int(pad_h), int(pad_w),
-                     int(dil_h), int(dil_w), int(dg), _DTYPES[input.dtype], 1 if has_bias else 0)
+                     int(dil_h), int(dil_w), int(dg), _DTYPES[input.dtype], 1 if has_bias else 0,
+                     _lib.DCN_NHWC if nhwc else _lib.DCN_NCHW)
     Ho, Wo = ctypes.c_int32(), ctypes.c_int32()
     rc = _lib.lib.dcn_output_size(ctypes.byref(d), ctypes.byref(Ho), ctypes.byref(Wo))
     if rc != _lib.DCN_OK:
@@ -62,12 +83,12 @@ def _desc(input, weight, stride_h, stride_w, pad_h, pad_w, dil_h, dil_w, dg, has
     return d, Ho.value, Wo.value
 
 
-def _prep(t, dtype, name, shape=None):
+def _prep(t, dtype, name, shape=None, nhwc=False):
     if t.dtype != dtype:
         raise RuntimeError(f"{name} must have dtype {dtype}, got {t.dtype}")
     if shape is not None and tuple(t.shape) != tuple(shape):
         raise RuntimeError(f"{name} has shape {tuple(t.shape)}, expected {tuple(shape)}")
-    return t.contiguous()
+    return _dense(t, nhwc)
 
 
 def _ptr(t):
@@ -91,18 +112,20 @@ def dcn_v2_forward(input: torch.Tensor, weight: torch.Tensor, mask: torch.Tensor
                    deformable_groups: int = 1) -> torch.Tensor:
     """Output [B, Co, Ho, Wo] of modulated deformable convolution (MyDCN_forward)."""
     _check_cuda(input=input, weight=weight, bias=bias, offset=offset, mask=mask)
+    nhwc = _is_nhwc(input)
     d, Ho, Wo = _desc(input, weight, stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w,
-                      deformable_groups, bias is not None)
+                      deformable_groups, bias is not None, nhwc)
     B, dg, K2 = input.shape[0], deformable_groups, weight.shape[2] * weight.shape[3]
     dt = input.dtype
-    input = input.contiguous()
+    input = _dense(input, nhwc)
     weight = _prep(weight, dt, "weight")
-    offset = _prep(offset, dt, "offset", (B, 2 * dg * K2, Ho, Wo))
-    mask = _prep(mask, dt, "mask", (B, dg * K2, Ho, Wo))
+    offset = _prep(offset, dt, "offset", (B, 2 * dg * K2, Ho, Wo), nhwc)
+    mask = _prep(mask, dt, "mask", (B, dg * K2, Ho, Wo), nhwc)
     if bias is not None:
         bias = _prep(bias, dt, "bias", (weight.shape[0],))
     with torch.cuda.device(input.device):
-        out = torch.empty((B, weight.shape[0], Ho, Wo), dtype=dt, device=input.device)
+        out = torch.empty((B, weight.shape[0], Ho, Wo), dtype=dt, device=input.device,
+                          memory_format=_CL if nhwc else torch.contiguous_format)
         nbytes = _lib.lib.dcn_forward_workspace_size(ctypes.byref(d))
         ws = torch.empty((max(nbytes, 256),), dtype=torch.uint8, device=input.device)
         stream = torch.cuda.current_stream(input.device).cuda_stream
@@ -122,16 +145,17 @@ def dcn_v2_backward(input: torch.Tensor, weight: torch.Tensor, mask: torch.Tenso
     _check_cuda(input=input, weight=weight, bias=bias, offset=offset, mask=mask,
                 grad_output=grad_output)
     has_bias = bias is not None
+    nhwc = _is_nhwc(input)
     d, Ho, Wo = _desc(input, weight, stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w,
-                      deformable_groups, True)
+                      deformable_groups, True, nhwc)
     B, dg, K2 = input.shape[0], deformable_groups, weight.shape[2] * weight.shape[3]
     Co = weight.shape[0]
     dt = input.dtype
-    input = input.contiguous()
+    input = _dense(input, nhwc)
     weight = _prep(weight, dt, "weight")
-    offset = _prep(offset, dt, "offset", (B, 2 * dg * K2, Ho, Wo))
-    mask = _prep(mask, dt, "mask", (B, dg * K2, Ho, Wo))
-    grad_output = _prep(grad_output, dt, "grad_output", (B, Co, Ho, Wo))
+    offset = _prep(offset, dt, "offset", (B, 2 * dg * K2, Ho, Wo), nhwc)
+    mask = _prep(mask, dt, "mask", (B, dg * K2, Ho, Wo), nhwc)
+    grad_output = _prep(grad_output, dt, "grad_output", (B, Co, Ho, Wo), nhwc)
     with torch.cuda.device(input.device):
         gi = torch.empty_like(input)
         goff = torch.empty_like(offset)
@@ -158,17 +182,19 @@ def dcn_v2_forward_om(input: torch.Tensor, weight: torch.Tensor, offset_mask: to
     the same result as ``dcn_v2_forward`` with the reference module's chunk / cat /
     sigmoid (dcn_v2_mm.py:133-137) done in the operator."""
     _check_cuda(input=input, weight=weight, bias=bias, offset_mask=offset_mask)
+    nhwc = _is_nhwc(input)
     d, Ho, Wo = _desc(input, weight, stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w,
-                      deformable_groups, bias is not None)
+                      deformable_groups, bias is not None, nhwc)
     B, dg, K2 = input.shape[0], deformable_groups, weight.shape[2] * weight.shape[3]
     dt = input.dtype
-    input = input.contiguous()
+    input = _dense(input, nhwc)
     weight = _prep(weight, dt, "weight")
-    offset_mask = _prep(offset_mask, dt, "offset_mask", (B, 3 * dg * K2, Ho, Wo))
+    offset_mask = _prep(offset_mask, dt, "offset_mask", (B, 3 * dg * K2, Ho, Wo), nhwc)
     if bias is not None:
         bias = _prep(bias, dt, "bias", (weight.shape[0],))
     with torch.cuda.device(input.device):
-        out = torch.empty((B, weight.shape[0], Ho, Wo), dtype=dt, device=input.device)
+        out = torch.empty((B, weight.shape[0], Ho, Wo), dtype=dt, device=input.device,
+                          memory_format=_CL if nhwc else torch.contiguous_format)
         nbytes = _lib.lib.dcn_forward_workspace_size(ctypes.byref(d))
         ws = torch.empty((max(nbytes, 256),), dtype=torch.uint8, device=input.device)
         stream = torch.cuda.current_stream(input.device).cuda_stream
@@ -187,15 +213,16 @@ def dcn_v2_backward_om(input: torch.Tensor, weight: torch.Tensor, offset_mask: t
     grad_offset_mask holds the offset gradients and the mask-logit gradients."""
     _check_cuda(input=input, weight=weight, bias=bias, offset_mask=offset_mask, grad_output=grad_output)
     has_bias = bias is not None
+    nhwc = _is_nhwc(input)
     d, Ho, Wo = _desc(input, weight, stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w,
-                      deformable_groups, True)
+                      deformable_groups, True, nhwc)
     B, dg, K2 = input.shape[0], deformable_groups, weight.shape[2] * weight.shape[3]
     Co = weight.shape[0]
     dt = input.dtype
-    input = input.contiguous()
+    input = _dense(input, nhwc)
     weight = _prep(weight, dt, "weight")
-    offset_mask = _prep(offset_mask, dt, "offset_mask", (B, 3 * dg * K2, Ho, Wo))
-    grad_output = _prep(grad_output, dt, "grad_output", (B, Co, Ho, Wo))
+    offset_mask = _prep(offset_mask, dt, "offset_mask", (B, 3 * dg * K2, Ho, Wo), nhwc)
+    grad_output = _prep(grad_output, dt, "grad_output", (B, Co, Ho, Wo), nhwc)
     with torch.cuda.device(input.device):
         gi = torch.empty_like(input)
         gom = torch.empty_like(offset_mask)

@@ -162,6 +162,7 @@ bool pdl_enabled() {
 bool make_gout_tmap(const Plan& P, const void* gout, TmaDesc* out) {
   static_assert(sizeof(CUtensorMap) == sizeof(TmaDesc), "tensor map size");
   EncodeTiledFn fn = encode_tiled();
+  if (P.nhwc) return false;   // channels-last grad_output goes through pack_gout_nhwc_kernel
   if (!fn || !gout || P.esz != 2 || (P.HoWo % 64) != 0) return false;
   const cuuint64_t dims[3] = {(cuuint64_t)P.HoWo, (cuuint64_t)P.Co, (cuuint64_t)P.B};
   const cuuint64_t strides[2] = {(cuuint64_t)P.HoWo * 2u, (cuuint64_t)P.Co * P.HoWo * 2u};
@@ -185,9 +186,22 @@ void set_offset_mask_strides(Plan* p, int om) {
   const int ctot_off = om ? 3 * nmsk : noff, ctot_msk = om ? 3 * nmsk : nmsk;
   p->off_bs = ctot_off * p->HoWo;
   p->msk_bs = ctot_msk * p->HoWo;
-  p->off_cs = p->msk_cs = p->HoWo;
-  p->off_ps = p->msk_ps = 1;
+  if (p->nhwc) {
+    p->off_cs = p->msk_cs = 1;
+    p->off_ps = ctot_off;
+    p->msk_ps = ctot_msk;
+  } else {
+    p->off_cs = p->msk_cs = p->HoWo;
+    p->off_ps = p->msk_ps = 1;
+  }
   p->mask_logit = om;
+}
+
+// Element offset of the mask channels inside the predictor output of the fused
+// path (channel 2*dg*K2 of pixel 0 of batch 0).
+size_t om_mask_offset(const Plan& p) {
+  const size_t c0 = (size_t)2 * p.dg * p.K2;
+  return p.nhwc ? c0 : c0 * p.HoWo;
 }
 
 int make_plan(const dcn_desc* d, Plan* p, int num_sms) {
@@ -198,9 +212,11 @@ int make_plan(const dcn_desc* d, Plan* p, int num_sms) {
       d->dw <= 0 || d->dg <= 0 || d->C % d->dg != 0)
     return DCN_E_INVALID;
   if (d->dtype != DCN_F32 && d->dtype != DCN_F16 && d->dtype != DCN_BF16) return DCN_E_INVALID;
+  if (d->layout != DCN_NCHW && d->layout != DCN_NHWC) return DCN_E_INVALID;
   p->B = d->B; p->C = d->C; p->H = d->H; p->W = d->W; p->Co = d->Co;
   p->kh = d->kh; p->kw = d->kw; p->sh = d->sh; p->sw = d->sw; p->ph = d->ph; p->pw = d->pw;
   p->dh = d->dh; p->dw = d->dw; p->dg = d->dg; p->dtype = d->dtype; p->has_bias = d->has_bias;
+  p->nhwc = d->layout == DCN_NHWC;
   const long long ho = ((long long)d->H + 2LL * d->ph - ((long long)d->dh * (d->kh - 1) + 1)) / d->sh + 1;
   const long long wo = ((long long)d->W + 2LL * d->pw - ((long long)d->dw * (d->kw - 1) + 1)) / d->sw + 1;
   if (ho <= 0 || wo <= 0) return DCN_E_INVALID;
@@ -335,7 +351,7 @@ static int forward_impl(const dcn_desc* d, const void* input, const void* weight
   if (rc != DCN_OK) return rc;
   if (om) {
     set_offset_mask_strides(&P, 1);
-    mask = offset ? static_cast<const uint8_t*>(offset) + (size_t)2 * P.dg * P.K2 * P.HoWo * P.esz : nullptr;
+    mask = offset ? static_cast<const uint8_t*>(offset) + om_mask_offset(P) * P.esz : nullptr;
   }
   if (!workspace) return DCN_E_NULLPTR;
   if (workspace_bytes < P.fwd_bytes || ((uintptr_t)workspace & (kWsAlign - 1)) != 0)
@@ -394,7 +410,7 @@ static int backward_impl(const dcn_desc* d, const void* input, const void* weigh
   int rc = make_plan(d, &P, device_sms());
   if (rc != DCN_OK) return rc;
   if (om) {
-    const size_t mofs = (size_t)2 * P.dg * P.K2 * P.HoWo * P.esz;
+    const size_t mofs = om_mask_offset(P) * P.esz;
     set_offset_mask_strides(&P, 1);
     mask = offset ? static_cast<const uint8_t*>(offset) + mofs : nullptr;
     grad_mask = grad_offset ? static_cast<uint8_t*>(grad_offset) + mofs : nullptr;

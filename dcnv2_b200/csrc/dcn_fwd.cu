@@ -366,7 +366,36 @@ __global__ void __launch_bounds__(FwdLayout<PW>::kThreads, 1)
       for (int c0 = 16 * chalf; c0 < NT; c0 += 16 * kEpiPerQuarter) {
         float v[16];
         tmem_ld16(tbase + c0, v);
-        if (vec) {
+        if (P.nhwc) {
+          // channels-last output: the lane's pixel row holds Co contiguously, so
+          // its 16 columns are one 32-byte (64 for f32) run, stored directly
+          const int co = ct * NT + c0;
+          if (!a.mma_bias) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] += sbias[co + j];
+          }
+          if (pv && !DCN_SKIP(2)) {
+            T* dst = y + (size_t)pix * P.Co + co;
+            if (a.vec_out && (P.Co % (16 / (int)sizeof(T))) == 0 && co + 16 <= P.Co) {
+              if constexpr (sizeof(T) == 4) {
+#pragma unroll
+                for (int j = 0; j < 16; j += 4)
+                  *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+              } else {
+                constexpr int kBF = OpOf<T>::kBF16;
+#pragma unroll
+                for (int j = 0; j < 16; j += 8)
+                  *reinterpret_cast<uint4*>(dst + j) =
+                      make_uint4(pack2<kBF>(v[j], v[j + 1]), pack2<kBF>(v[j + 2], v[j + 3]),
+                                 pack2<kBF>(v[j + 4], v[j + 5]), pack2<kBF>(v[j + 6], v[j + 7]));
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 16; ++j)
+                if (co + j < P.Co) dst[j] = Elem<T>::from_f(v[j]);
+            }
+          }
+        } else if (vec) {
           if constexpr (sizeof(T) == 2) {
             // stage [8 co pairs][32 px] words (co 2p in the low half, 2p+1 in the
             // high half: one packed conversion and one 32-bit store per pair), then

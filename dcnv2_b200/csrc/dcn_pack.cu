@@ -394,6 +394,176 @@ __global__ void __launch_bounds__(256) pack_input_rt_kernel(const T* __restrict_
   }
 }
 
+// ---------------------------------------------------------------------------
+// Channels-last (DCN_NHWC) activations.
+
+// Loads 4 consecutive logical channels [lc0, lc0+4) of one pixel row `src`
+// (channels of one group, Cg of them) as floats; zero past Cg.  `vec`: one 8- or
+// 16-byte load (the run lies inside the group and is 4-element aligned).
+template <typename T>
+__device__ __forceinline__ void load4_row(const T* __restrict__ src, int lc0, int Cg, bool vec, float (&v)[4]) {
+  if (vec && lc0 + 4 <= Cg) {
+    if constexpr (sizeof(T) == 4) {
+      const uint4 u = ldg_nc_v4(src + lc0);
+      v[0] = __uint_as_float(u.x); v[1] = __uint_as_float(u.y);
+      v[2] = __uint_as_float(u.z); v[3] = __uint_as_float(u.w);
+    } else {
+      const uint2 u = ldg_nc_v2(src + lc0);
+      v[0] = raw_to_f<T>(u.x & 0xffffu); v[1] = raw_to_f<T>(u.x >> 16);
+      v[2] = raw_to_f<T>(u.y & 0xffffu); v[3] = raw_to_f<T>(u.y >> 16);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[e] = lc0 + e < Cg ? ldf(src + lc0 + e) : 0.f;
+  }
+}
+
+// x [B][HW][C] -> xt [B][HW][dg][Cgp] (perm_logical order inside each 64-channel
+// block, padded channels zero).  One thread per 8-element physical slice q of a
+// block: its two runs of 4 logical channels (slice_lo / slice_hi) are read with
+// vector loads and stored as one slice; `acc` (the backward's fp32 grad_input
+// accumulator of the same layout) is zeroed alongside and `status` cleared.
+template <typename T>
+__global__ void __launch_bounds__(256) pack_input_nhwc_kernel(const T* __restrict__ x, T* __restrict__ xt,
+                                                              int C, int Cg, int Cgp, int CS, long long nslices,
+                                                              int vec, float* __restrict__ acc,
+                                                              int* __restrict__ status) {
+  pdl_wait();
+  if (status != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *status = 0;
+  const int spp = CS >> 3;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < nslices;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const long long pix = idx / spp;
+    const int sl = (int)(idx - pix * spp);
+    const int d0 = (sl >> 3) << 6, q = sl & 7;
+    const int g = d0 / Cgp, cb = d0 - g * Cgp;
+    const T* src = x + (size_t)pix * C + (size_t)g * Cg;
+    float lo[4], hi[4];
+    load4_row<T>(src, cb + slice_lo(q), Cg, vec, lo);
+    load4_row<T>(src, cb + slice_hi(q), Cg, vec, hi);
+    const size_t eo = (size_t)pix * CS + d0 + 8 * q;
+    if constexpr (sizeof(T) == 4) {
+      *reinterpret_cast<float4*>(xt + eo) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+      *reinterpret_cast<float4*>(xt + eo + 4) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+    } else {
+      constexpr int kBF = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
+      *reinterpret_cast<uint4*>(xt + eo) =
+          make_uint4(pack2<kBF>(lo[0], lo[1]), pack2<kBF>(lo[2], lo[3]), pack2<kBF>(hi[0], hi[1]),
+                     pack2<kBF>(hi[2], hi[3]));
+    }
+    if (acc != nullptr) {
+      const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+      *reinterpret_cast<float4*>(acc + eo) = z;
+      *reinterpret_cast<float4*>(acc + eo + 4) = z;
+    }
+  }
+}
+
+// fp32 [B][HW][dg][Cgp] (logical channel order) -> T [B][HW][C].  One thread per
+// run of 4 channels of a group (vector load and store when Cg % 4 == 0 and gx is
+// 16-byte aligned), else per element.
+template <typename T>
+__global__ void __launch_bounds__(256) finish_grad_input_nhwc_kernel(const float* __restrict__ gxn,
+                                                                     T* __restrict__ gx, int C, int Cg, int Cgp,
+                                                                     int CS, long long nruns, int vec) {
+  pdl_wait();
+  const int rpp = C >> 2;   // runs per pixel when vec (C % 4 == 0)
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < nruns;
+       idx += (long long)gridDim.x * blockDim.x) {
+    if (vec) {
+      const long long pix = idx / rpp;
+      const int c = (int)(idx - pix * rpp) * 4;
+      const int g = c / Cg, cc = c - g * Cg;
+      const float4 v = *reinterpret_cast<const float4*>(gxn + (size_t)pix * CS + g * Cgp + cc);
+      T* o = gx + (size_t)pix * C + c;
+      if constexpr (sizeof(T) == 4) {
+        *reinterpret_cast<float4*>(o) = v;
+      } else {
+        constexpr int kBF = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
+        *reinterpret_cast<uint2*>(o) = make_uint2(pack2<kBF>(v.x, v.y), pack2<kBF>(v.z, v.w));
+      }
+    } else {
+      const long long pix = idx / C;
+      const int c = (int)(idx - pix * C);
+      const int g = c / Cg, cc = c - g * Cg;
+      gx[idx] = Elem<T>::from_f(gxn[(size_t)pix * CS + g * Cgp + cc]);
+    }
+  }
+}
+
+// grad_output [totalP][Co] (channels-last) -> the operand blocks of
+// pack_gout_kernel (64 pixels x 64 Co, 128-byte rows with the 128-byte swizzle;
+// f32 as bf16 hi then lo).  Thread: pixel row `row` and 8-Co chunk c of a block,
+// one 16-byte load (two for f32) when Co % 8 == 0 and grad_output is aligned.
+// grad_bias partial sums go to `gb` when it is not null.
+template <typename T>
+__global__ void __launch_bounds__(256) pack_gout_nhwc_kernel(const T* __restrict__ gout,
+                                                             uint8_t* __restrict__ gpk,
+                                                             float* __restrict__ gb, const Plan P, int vec) {
+  pdl_wait();
+  const int ko = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int nPB = (int)((P.totalP + 63) / 64);
+  const size_t blk_bytes = (size_t)P.nsplit * 8192;
+  const int c = tid & 7;                 // the thread's 8-Co chunk (fixed)
+  const int co0 = ko * kChunk + c * 8;
+  float bsum[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) bsum[e] = 0.f;
+  for (int pb = blockIdx.x; pb < nPB; pb += gridDim.x) {
+    uint8_t* blk = gpk + ((size_t)pb * P.nKo + ko) * blk_bytes;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int row = (tid >> 3) + 32 * k;
+      const long long pix = (long long)pb * 64 + row;
+      float v[8];
+      if (pix < P.totalP && vec && co0 + 8 <= P.Co) {
+        const T* src = gout + (size_t)pix * P.Co + co0;
+        if constexpr (sizeof(T) == 4) {
+          const uint4 a = ldg_nc_v4(src), b = ldg_nc_v4(src + 4);
+          v[0] = __uint_as_float(a.x); v[1] = __uint_as_float(a.y);
+          v[2] = __uint_as_float(a.z); v[3] = __uint_as_float(a.w);
+          v[4] = __uint_as_float(b.x); v[5] = __uint_as_float(b.y);
+          v[6] = __uint_as_float(b.z); v[7] = __uint_as_float(b.w);
+        } else {
+          unpack8<T>(ldg_nc_v4(src), v);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          v[e] = (pix < P.totalP && co0 + e < P.Co) ? ldf(gout + (size_t)pix * P.Co + co0 + e) : 0.f;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) bsum[e] += v[e];
+      const uint32_t off = sw128_off(row, c);
+      if constexpr (OpOf<T>::kSplit) {
+        uint4 hi, lo;
+        split2(v[0], v[1], hi.x, lo.x);
+        split2(v[2], v[3], hi.y, lo.y);
+        split2(v[4], v[5], hi.z, lo.z);
+        split2(v[6], v[7], hi.w, lo.w);
+        *reinterpret_cast<uint4*>(blk + off) = hi;
+        *reinterpret_cast<uint4*>(blk + 8192 + off) = lo;
+      } else {
+        constexpr int kBF = OpOf<T>::kBF16;
+        *reinterpret_cast<uint4*>(blk + off) =
+            make_uint4(pack2<kBF>(v[0], v[1]), pack2<kBF>(v[2], v[3]), pack2<kBF>(v[4], v[5]),
+                       pack2<kBF>(v[6], v[7]));
+      }
+    }
+  }
+  if (gb != nullptr) {
+    // lanes l, l + 8, l + 16, l + 24 hold the same chunk
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      float sum = bsum[e];
+      sum += __shfl_xor_sync(0xffffffffu, sum, 8);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 16);
+      if (lane < 8 && co0 + e < P.Co) atomicAdd(gb + co0 + e, sum);
+    }
+  }
+}
+
 template <typename F>
 int dispatch(int dtype, F&& f) {
   cudaError_t e;
@@ -416,6 +586,16 @@ int grid_for(long long n, int threads) {
 int launch_pack_input(const Plan& P, const void* x, void* xt, float* zero_acc, int* status,
                       cudaStream_t s) {
   const int HW = P.H * P.W;
+  if (P.nhwc) {
+    const long long nslices = (long long)P.B * HW * (P.CS / 8);
+    const int vec = (P.C % 4 == 0) && (P.Cg % 4 == 0) && (((uintptr_t)x & 15u) == 0);
+    return dispatch(P.dtype, [&](auto tag) {
+      using T = decltype(tag);
+      return launch_k(pack_input_nhwc_kernel<T>, dim3(grid_for(nslices, 256)), dim3(256), 0, s,
+                      static_cast<const T*>(x), static_cast<T*>(xt), P.C, P.Cg, P.Cgp, P.CS, nslices, vec,
+                      zero_acc, status);
+    });
+  }
   const int vec = (HW % 8 == 0) && (((uintptr_t)x & 15u) == 0);
   const int npb = ceil_div(HW, 64), ncb = P.CS / 64;
   const long long nblocks = (long long)npb * ncb * P.B;
@@ -468,6 +648,14 @@ int launch_pack_gout(const Plan& P, const void* gout, uint8_t* gpk, float* gb, i
   if (gx < 1) gx = 1;
   if (gx > nPB) gx = nPB;
   dim3 grid(gx, P.nKo);
+  if (P.nhwc) {
+    const int v = (P.Co % 8 == 0) && (((uintptr_t)gout & 15u) == 0);
+    return dispatch(P.dtype, [&](auto tag) {
+      using T = decltype(tag);
+      return launch_k(pack_gout_nhwc_kernel<T>, dim3(grid), dim3(256), 0, s, static_cast<const T*>(gout), gpk, gb,
+                      P, v);
+    });
+  }
   return dispatch(P.dtype, [&](auto tag) {
     using T = decltype(tag);
     return launch_k(pack_gout_kernel<T>, dim3(grid), dim3(256), 0, s, static_cast<const T*>(gout), gpk, gb, P, vec);
@@ -476,6 +664,15 @@ int launch_pack_gout(const Plan& P, const void* gout, uint8_t* gpk, float* gb, i
 
 int launch_finish_grad_input(const Plan& P, const float* gxn, void* gx, cudaStream_t s) {
   const int HW = P.H * P.W;
+  if (P.nhwc) {
+    const int vec = (P.Cg % 4 == 0) && (((uintptr_t)gx & 15u) == 0);
+    const long long n = (long long)P.B * HW * P.C / (vec ? 4 : 1);
+    return dispatch(P.dtype, [&](auto tag) {
+      using T = decltype(tag);
+      return launch_k(finish_grad_input_nhwc_kernel<T>, dim3(grid_for(n, 256)), dim3(256), 0, s, gxn,
+                      static_cast<T*>(gx), P.C, P.Cg, P.Cgp, P.CS, n, vec);
+    });
+  }
   const int vec = (HW % 8 == 0) && (((uintptr_t)gx & 15u) == 0);
   dim3 grid(ceil_div(HW, 64), P.CS / 64, P.B);
   return dispatch(P.dtype, [&](auto tag) {

@@ -35,6 +35,7 @@ inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
 struct Plan {
   // problem
   int B, C, H, W, Co, kh, kw, sh, sw, ph, pw, dh, dw, dg, dtype, has_bias;
+  int nhwc;           // activations channels-last (DCN_NHWC)
   int Ho, Wo, HoWo, K2;
   long long totalP;   // B*Ho*Wo output pixels
   int Cg, Cgp, nCB;   // channels per group, padded to 64, 64-channel blocks per group

@@ -17,8 +17,11 @@
  * [B][dg*2*kh*kw][Ho][Wo] with channel 2t = dh and 2t+1 = dw of tap t = i*kw + j,
  * mask [B][dg*kh*kw][Ho][Wo], output [B][Co][Ho][Wo].  All tensors are dense,
  * contiguous device memory of one element type.  Beyond the reference: dilation
- * and deformable groups are honoured, and f16/bf16 tensors are accepted as well
- * as f32.
+ * and deformable groups are honoured, f16/bf16 tensors are accepted as well as
+ * f32, and with desc.layout = DCN_NHWC every activation tensor (input, offset,
+ * mask, output, grad_output and the gradients of input, offset and mask) is
+ * channels-last instead ([B][H][W][C], [B][Ho][Wo][2*dg*kh*kw], ...), so stacked
+ * layers pass activations on without layout passes.
  *
  * Calls are asynchronous on the given CUDA stream (NULL = legacy default stream);
  * nothing is allocated: the caller passes a device workspace of at least the
@@ -45,6 +48,13 @@ extern "C" {
 
 /* element type of every tensor argument */
 enum dcn_dtype { DCN_F32 = 0, DCN_F16 = 1, DCN_BF16 = 2 };
+
+/* memory layout of the activation tensors (input, offset, mask, output and
+ * their gradients); the weight is always [Co][C][kh][kw] */
+enum dcn_layout {
+  DCN_NCHW = 0, /* [B][C][H][W], the reference's layout */
+  DCN_NHWC = 1  /* channels-last [B][H][W][C] (PyTorch channels_last memory format) */
+};
 
 /* return codes */
 enum dcn_status_code {
@@ -73,6 +83,7 @@ typedef struct dcn_desc {
   int32_t dg;         /* deformable groups; C % dg == 0 (reference: always 1) */
   int32_t dtype;      /* enum dcn_dtype */
   int32_t has_bias;   /* 0: bias pointer ignored / grad_bias not written */
+  int32_t layout;     /* enum dcn_layout; 0 (NCHW) in a zero-initialised descriptor */
 } dcn_desc;
 
 /* Validates `d` and writes the output spatial size.  DCN_OK or DCN_E_INVALID. */

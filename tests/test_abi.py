@@ -46,7 +46,7 @@ def test_output_size_and_workspace():
 
 
 @pytest.mark.parametrize("bad", [dict(C=63, dg=2), dict(kh=0), dict(sh=0), dict(dh=0), dict(dg=0),
-                                 dict(dtype=7), dict(H=1, W=1, ph=0, pw=0), dict(Co=0)])
+                                 dict(dtype=7), dict(H=1, W=1, ph=0, pw=0), dict(Co=0), dict(layout=2)])
 def test_invalid_descriptors(bad):
     d = _desc(**bad)
     ho, wo = ctypes.c_int32(), ctypes.c_int32()
@@ -74,3 +74,12 @@ def test_strerror_and_version():
 def test_trace_collect_empty():
     _lib.trace_reset()
     assert _lib.trace_collect() == {}
+
+
+def test_descriptor_layout_field():
+    """dcn_desc ends with the layout field (17 int32); NCHW and NHWC give the
+    same output size and workspace."""
+    assert ctypes.sizeof(_lib.DcnDesc) == 17 * 4
+    a, b = _desc(layout=_lib.DCN_NCHW), _desc(layout=_lib.DCN_NHWC)
+    assert _lib.lib.dcn_forward_workspace_size(ctypes.byref(a)) == _lib.lib.dcn_forward_workspace_size(ctypes.byref(b))
+    assert _lib.lib.dcn_backward_workspace_size(ctypes.byref(a)) == _lib.lib.dcn_backward_workspace_size(ctypes.byref(b))
