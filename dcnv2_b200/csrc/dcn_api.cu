@@ -55,13 +55,23 @@ bool gout_packed_forced() {
 #endif
 }
 
+// DCN_SCATTER_TC=0 runs the plain scatter kernel even where the tile path
+// applies (both give the same results; for comparisons).
+bool scatter_tc_disabled() {
+  static bool v = [] {
+    const char* e = getenv("DCN_SCATTER_TC");
+    return e != nullptr && atoi(e) == 0;
+  }();
+  return v;
+}
+
 #ifdef DCN_STUDY
 // Study switch: DCN_DEBUG_TS prints per-stage global-timer stamps of CTA 0 of
 // a kernel to stderr.  One buffer per device (tag 0..2: forward, backward
 // data, backward weight); allocates and synchronises, so never in a normal build.
 unsigned long long* study_ts_buffer(int tag, cudaStream_t s) {
   if (!getenv("DCN_DEBUG_TS")) return nullptr;
-  static unsigned long long* bufs[64][3];
+  static unsigned long long* bufs[64][4];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
   if (!bufs[dev][tag] && cudaMalloc(&bufs[dev][tag], 1024 * sizeof(unsigned long long)) != cudaSuccess)
@@ -177,6 +187,39 @@ bool make_gout_tmap(const Plan& P, const void* gout, TmaDesc* out) {
   if (r != CUDA_SUCCESS) return false;
   memcpy(out, &m, sizeof(m));
   return true;
+}
+
+bool make_scatter_tmaps(const Plan& P, const void* xt, const void* gcol, const float* gx, TmaDesc* xmap,
+                        TmaDesc* cmap, TmaDesc* rmap) {
+  EncodeTiledFn fn = encode_tiled();
+  if (!fn || P.esz != 2) return false;
+  const CUtensorMapDataType dt =
+      P.dtype == DCN_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  auto enc = [&](CUtensorMapDataType t, const void* base, const cuuint64_t* dims, const cuuint64_t* strides,
+                 const cuuint32_t* box, TmaDesc* out) {
+    CUtensorMap m;
+    if (fn(&m, t, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return false;
+    memcpy(out, &m, sizeof(m));
+    return true;
+  };
+  // packed input [B][H][W][CS]: a 16 x 16 pixel window of one 64-channel block
+  const cuuint64_t xd[4] = {(cuuint64_t)P.CS, (cuuint64_t)P.W, (cuuint64_t)P.H, (cuuint64_t)P.B};
+  const cuuint64_t xs[3] = {(cuuint64_t)P.CS * 2u, (cuuint64_t)P.W * P.CS * 2u, (cuuint64_t)P.H * P.W * P.CS * 2u};
+  const cuuint32_t xb[4] = {64u, 16u, 16u, 1u};
+  // gcol [B][Ho][Wo][K2*dg*Cgp] (one pixel chunk): 8 x 8 pixels x 64 channels of one (tap, group)
+  const cuuint64_t row = (cuuint64_t)P.K2 * P.dg * P.Cgp;
+  const cuuint64_t cd[4] = {row, (cuuint64_t)P.Wo, (cuuint64_t)P.Ho, (cuuint64_t)P.B};
+  const cuuint64_t cs[3] = {row * 2u, (cuuint64_t)P.Wo * row * 2u, (cuuint64_t)P.HoWo * row * 2u};
+  const cuuint32_t cbx[4] = {64u, 8u, 8u, 1u};
+  // fp32 grad_input accumulator [B][H][W][CS]: 8 rows x 16 pixels x 32 channels
+  const cuuint64_t rs[3] = {(cuuint64_t)P.CS * 4u, (cuuint64_t)P.W * P.CS * 4u, (cuuint64_t)P.H * P.W * P.CS * 4u};
+  const cuuint32_t rb[4] = {32u, 16u, 8u, 1u};
+  return enc(dt, xt, xd, xs, xb, xmap) && enc(dt, gcol, cd, cs, cbx, cmap) &&
+         enc(CU_TENSOR_MAP_DATA_TYPE_FLOAT32, gx, xd, rs, rb, rmap);
 }
 
 // Strides of the offset and mask tensors (see Plan::off_bs); `om`: both are the
@@ -484,6 +527,7 @@ static int backward_impl(const dcn_desc* d, const void* input, const void* weigh
 #ifdef DCN_STUDY
   unsigned long long* const dts_d = study_ts_buffer(1, s);
   a.ts = dts_d;
+  unsigned long long* dts_s = nullptr;
 #endif
   BwdWeightArgs w;
   memset(&w, 0, sizeof(w));
@@ -501,6 +545,9 @@ static int backward_impl(const dcn_desc* d, const void* input, const void* weigh
   unsigned long long* const dts = study_ts_buffer(2, s);
   w.ts = dts;
 #endif
+  // the tile scatter (grad_input summed on the tensor cores) where it applies
+  const bool use_tc = !scatter_tc_disabled() && backward_scatter_tc_eligible(P) &&
+                      make_scatter_tmaps(P, a.xt, a.gcol, a.gx_nhwc, &a.xmap, &a.cmap, &a.rmap);
   // per pixel chunk: column gradients (tcgen05), then the scatter (grad_input,
   // grad_offset, grad_mask and the sampled columns), then the weight gradient
   for (long long p0 = 0; p0 < P.totalP; p0 += P.gcol_chunk) {
@@ -512,7 +559,12 @@ static int backward_impl(const dcn_desc* d, const void* input, const void* weigh
     }
     {
       TraceScope ts(TR_BACKWARD_SCATTER, s);
-      if ((rc = launch_backward_scatter(a, s)) != DCN_OK) return rc;
+      BwdDataArgs sa = a;
+#ifdef DCN_STUDY
+      sa.ts = a.ts ? study_ts_buffer(3, s) : nullptr;
+      dts_s = sa.ts ? sa.ts : dts_s;
+#endif
+      if ((rc = use_tc ? launch_backward_scatter_tc(sa, s) : launch_backward_scatter(sa, s)) != DCN_OK) return rc;
     }
     w.ks0 = (int)(p0 / 64);
     w.nks = (a.npix + 63) / 64;
@@ -525,6 +577,7 @@ static int backward_impl(const dcn_desc* d, const void* input, const void* weigh
   }
 #ifdef DCN_STUDY
   study_ts_print("DCN_TSD", dts_d, s);
+  study_ts_print("DCN_TSS", dts_s, s);
   study_ts_print("DCN_TSW", dts, s);
 #endif
   {

@@ -52,6 +52,10 @@ struct FwdArgs {
 
 struct BwdDataArgs {
   TmaDesc gmap;         // grad_output as [B][Co][HoWo], box 64 pixels x 64 Co, SW128 (gdirect)
+  TmaDesc xmap;         // packed input [B][H][W][CS], box 16 x 16 pixels x 64 channels, SW128 (tile scatter)
+  TmaDesc cmap;         // gcol [B][Ho][Wo][K2*dg*Cgp], box 8 x 8 pixels x 64 channels, SW128 (tile scatter)
+  TmaDesc rmap;         // fp32 grad_input accumulator [B][H][W][CS], box 8 x 16 pixels x 32 channels,
+                        // SW128 (tile scatter: TMA reductions of its windows)
   int gdirect;          // A tiles loaded from grad_output by TMA (no packed copy); 16-bit types,
                         // HoWo % 64 == 0, 16-byte aligned grad_output
   Plan plan;
@@ -134,6 +138,14 @@ int launch_finish_grad_weight(const Plan& p, const float* gw, const float* gb, v
 int launch_forward(const FwdArgs& a, cudaStream_t s);
 int launch_backward_data(const BwdDataArgs& a, cudaStream_t s);
 int launch_backward_scatter(const BwdDataArgs& a, cudaStream_t s);
+// Tile path of the scatter (dcn_bwd_scatter_tc.cu): grad_input summed on the
+// tensor cores over 16 x 16 input windows; needs a.xmap, a.cmap and a.rmap.
+bool backward_scatter_tc_eligible(const Plan& p);
+size_t backward_scatter_tc_smem(const Plan& p);
+int launch_backward_scatter_tc(const BwdDataArgs& a, cudaStream_t s);
+// Tensor maps of the tile scatter; false when the encoder rejects them.
+bool make_scatter_tmaps(const Plan& p, const void* xt, const void* gcol, const float* gx, TmaDesc* xmap,
+                        TmaDesc* cmap, TmaDesc* rmap);
 int launch_backward_weight(const BwdWeightArgs& a, cudaStream_t s);
 
 // Tensor map of grad_output [B][Co][HoWo] (16-bit) with a 64 x 64 box and the
