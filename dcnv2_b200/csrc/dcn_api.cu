@@ -17,15 +17,15 @@ namespace dcn {
 
 namespace {
 
-// Study switch (DCN_STUDY builds only): bit 0 skips the bilinear gathers, bit 1
-// output stores / scatters, bit 2 the MMAs; results are wrong when set.
+// Study switch (DCN_STUDY builds only, read at every call): bit 0 skips the
+// bilinear gathers, bit 1 output stores / scatters, bit 2 the MMAs (results are
+// wrong when set); bit 3 withholds the forward's weight-tile copies, so the
+// pipeline waits run out (the failure-detection test: the kernel must give up,
+// report DCN_DEVERR_TIMEOUT and leave the context usable).
 int debug_skip() {
 #ifdef DCN_STUDY
-  static int v = [] {
-    const char* e = getenv("DCN_DEBUG_SKIP");
-    return e ? atoi(e) : 0;
-  }();
-  return v;
+  const char* e = getenv("DCN_DEBUG_SKIP");
+  return e ? atoi(e) : 0;
 #else
   return 0;
 #endif

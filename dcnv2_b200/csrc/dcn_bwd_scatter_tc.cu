@@ -38,7 +38,7 @@
 //               per sample (16-byte slices of 8 channels)
 //   warps 16-19 epilogue: TMEM (window x 64 channels, fp32) -> staging in shared
 //               memory -> TMA reduction (add) into the grad_input accumulator
-//   warp 20     TMA: x windows (2-slot ring), gcol tiles (4-slot ring)
+//   warp 20     TMA: x windows (2-slot ring), gcol tiles (3-slot ring)
 //   warp 21     TMEM owner and tcgen05.mma issuer (M = 128 window pixels x 2,
 //               N = 64 channels, K = 64 samples per tap); warps 22-23 idle
 // Used for 16-bit types when the whole backward is one pixel chunk, the image
@@ -59,7 +59,7 @@ constexpr int kSimtWarps = 16;
 constexpr int kEpiWarp0 = 16;
 constexpr int kTmaWarp = 20, kMmaWarp = 21;
 constexpr int kThreads = 24 * 32;
-constexpr int kXS = 2, kAS = 2, kBS = 4;  // ring depths: x windows, A stages, gcol tiles
+constexpr int kXS = 2, kAS = 2, kBS = 3;  // ring depths: x windows, A stages, gcol tiles
 constexpr int kGS = 2;                    // geometry slots per lane: 4 samples x K2 <= 16 taps
 constexpr uint32_t kXBytes = kWin * 128;  // 32 KB
 constexpr uint32_t kABytes = kWin * 128;  // 32 KB: 2 M tiles x 128 rows x 128 B
@@ -99,6 +99,16 @@ __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.w
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 // named barrier of the four epilogue warps
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// {a.x * b.x + c.x, a.y * b.y + c.y} (sm_100 packed f32x2)
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  unsigned long long r;
+  asm("{\n\t.reg .b64 x, y, z;\n\tmov.b64 x, {%1, %2};\n\tmov.b64 y, {%3, %4};\n\t"
+      "mov.b64 z, {%5, %6};\n\tfma.rn.f32x2 %0, x, y, z;\n\t}"
+      : "=l"(r)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return make_float2(__uint_as_float((uint32_t)r), __uint_as_float((uint32_t)(r >> 32)));
+}
 
 template <int N>
 __device__ __forceinline__ float pick(const float (&v)[N], int i) {
@@ -157,7 +167,10 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_bwd_scatter_tc_kernel(const _
   const uint32_t aring = xring + kXS * kXBytes;
   const uint32_t bring = aring + kAS * kABytes;
   const uint32_t stg = bring + kBS * kBBytes;
-  float* sbuf = reinterpret_cast<float*>(smem_raw + (stg + kStgBytes - smem_u32(smem_raw)));
+  // per-warp sample geometry of the current unit: 4 * K2 entries of 32 bytes
+  const uint32_t geo = stg + kStgBytes;
+  const uint32_t geo_warp_bytes = (uint32_t)(4 * K2) * 32u;
+  float* sbuf = reinterpret_cast<float*>(smem_raw + (geo + kSimtWarps * geo_warp_bytes - smem_u32(smem_raw)));
   const uint32_t xfull0 = smem_u32(&bars[0]), xempty0 = xfull0 + 8 * kXS;
   const uint32_t afull0 = xempty0 + 8 * kXS, aempty0 = afull0 + 8 * kAS;
   const uint32_t bfull0 = aempty0 + 8 * kAS, bempty0 = bfull0 + 8 * kBS;
@@ -218,6 +231,26 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_bwd_scatter_tc_kernel(const _
     uint32_t xph = 0, aph = 0, bph = 0;
     bool ok = true;
     int nch = 0;                                 // K steps done (timestamps)
+    // Global writes of a K step (its sampled column and, for lane q == 0, the
+    // grad_offset / grad_mask values) are issued after the NEXT step's A
+    // entries have been fenced and published: the proxy fence before that
+    // publication would otherwise wait for them to complete.
+    uint4* dcol = nullptr;
+    uint4 vcol = make_uint4(0u, 0u, 0u, 0u);
+    T* doff = nullptr;
+    T* dmsk = nullptr;
+    int doffs = 0;
+    T vh = Elem<T>::from_f(0.f), vw = vh, vm = vh;
+    auto flush_deferred = [&]() {
+      if (dcol != nullptr) *dcol = vcol;
+      if (doff != nullptr) {
+        doff[0] = vh;
+        doff[doffs] = vw;
+        *dmsk = vm;
+      }
+      dcol = nullptr;
+      doff = nullptr;
+    };
     if (warp == 0) DCN_TS(1000);
     for (int u = blockIdx.x; u < nUnits && ok; u += gridDim.x) {
       const Unit un = unit_of(u, P, nTx, nTy);
@@ -227,10 +260,12 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_bwd_scatter_tc_kernel(const _
       const int pix = un.b * P.HoWo + p;         // flat pixel (one chunk: pix0 == 0)
       const int r0 = window_origin(un.ho0 * P.sh - P.ph, span_h, kWH, P.H);
       const int c0 = window_origin(un.wo0 * P.sw - P.pw, span_w, kWW, P.W);
-      // sampling positions and masks of the warp's 4 samples for every tap,
-      // loaded once per unit (all loads in flight together): entry e = 4 t + s
-      // (sample 4 * warp + s) lives in lane e % 32, slot e / 32
-      float gh[kGS], gw[kGS], gm[kGS];
+      // sampling geometry of the warp's 4 samples for every tap, built once per
+      // unit (all offset / mask loads in flight together; entry e = 4 t + s of
+      // sample 4 * warp + s by lane e % 32) into the warp's shared-memory table:
+      //   {window pixel of corners 0,1 (int16 x 2), of corners 2,3, corner
+      //    validity bits, image pixel of corner 0} {lh, lw, mask, -}
+      const uint32_t gtab = geo + (uint32_t)warp * geo_warp_bytes;
       {
         uint32_t rh[kGS], rw[kGS], rm[kGS];
 #pragma unroll
@@ -249,52 +284,63 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_bwd_scatter_tc_kernel(const _
 #pragma unroll
         for (int sl = 0; sl < kGS; ++sl) {
           const int e = sl * 32 + lane, te = e >> 2, ke = 4 * warp + (e & 3);
-          const int ie = te / P.kw, je = te - ie * P.kw;
-          const int hoe = un.ho0 + (ke >> 3), woe = un.wo0 + (ke & 7);
-          gh[sl] = (float)(hoe * P.sh - P.ph + ie * P.dh) + raw_to_f<T>(rh[sl]);
-          gw[sl] = (float)(woe * P.sw - P.pw + je * P.dw) + raw_to_f<T>(rw[sl]);
-          float mv = raw_to_f<T>(rm[sl]);
-          if (P.mask_logit) mv = 1.f / (1.f + __expf(-mv));   // sigmoid of a predictor logit
-          gm[sl] = mv;
+          if (te < K2) {
+            const int ie = te / P.kw, je = te - ie * P.kw;
+            const int hoe = un.ho0 + (ke >> 3), woe = un.wo0 + (ke & 7);
+            const bool pve = hoe < P.Ho && woe < P.Wo;
+            const float h = (float)(hoe * P.sh - P.ph + ie * P.dh) + raw_to_f<T>(rh[sl]);
+            const float w = (float)(woe * P.sw - P.pw + je * P.dw) + raw_to_f<T>(rw[sl]);
+            float mv = raw_to_f<T>(rm[sl]);
+            if (P.mask_logit) mv = 1.f / (1.f + __expf(-mv));   // sigmoid of a predictor logit
+            const float hf = floorf(h), wf = floorf(w);
+            const int hl = (int)hf, wl = (int)wf;
+            uint32_t cv = 0u;
+            if (pve && (h > -1.f) && (w > -1.f) && (h < (float)P.H) && (w < (float)P.W)) {
+              const bool rr0 = hl >= 0, rr1 = hl + 1 <= P.H - 1, cc0 = wl >= 0, cc1 = wl + 1 <= P.W - 1;
+              cv = (rr0 && cc0 ? 1u : 0u) | (rr0 && cc1 ? 2u : 0u) | (rr1 && cc0 ? 4u : 0u) | (rr1 && cc1 ? 8u : 0u);
+            }
+            uint32_t wpk[2] = {0u, 0u};
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const int wr = hl + (c >> 1) - r0, wc = wl + (c & 1) - c0;
+              const int wp = ((cv >> c) & 1u) && wr >= 0 && wr < kWH && wc >= 0 && wc < kWW ? wr * kWW + wc : -1;
+              wpk[c >> 1] |= ((uint32_t)wp & 0xffffu) << (16 * (c & 1));
+            }
+            const uint32_t ea = gtab + (uint32_t)e * 32u;
+            sts_v4(ea, make_uint4(wpk[0], wpk[1], cv, (uint32_t)(un.b * HW + hl * P.W + wl)));
+            sts_v4(ea + 16u, make_uint4(__float_as_uint(h - hf), __float_as_uint(w - wf),
+                                        __float_as_uint(pve ? mv : 0.f), 0u));
+          }
         }
+        __syncwarp();
       }
       for (int cb = 0; cb < nCB && ok; ++cb) {
         if (!mbar_wait_warp(xfull0 + 8 * xs, xph, a.err, &abort_flag)) { ok = false; break; }
         const uint32_t xwin = xring + xs * kXBytes;
         for (int t = 0; t < K2; ++t, ++nch) {
-          if (warp == 0 && nch < 200) DCN_TS(4 * nch);
+          if (warp == 0 && nch < 130) DCN_TS(6 * nch);
           // phase 1 (feeds the MMA): geometry and this sample's A entries
           if (!mbar_wait_warp(aempty0 + 8 * as_, aph ^ 1u, a.err, &abort_flag)) { ok = false; break; }
-          if (warp == 0 && nch < 200) DCN_TS(4 * nch + 1);
+          if (warp == 0 && nch < 130) DCN_TS(6 * nch + 1);
           const uint32_t astage = aring + as_ * kABytes, bstage = bring + bs * kBBytes;
           // clear what this lane wrote into the stage last time round
           uint32_t prev = kNoEntry;
 #pragma unroll
           for (int s2 = 0; s2 < kAS; ++s2) if (s2 == as_) prev = rem[s2];
           if (prev != kNoEntry) sts_u16(prev, 0);
-          // sampling geometry of this sample and tap (from the unit's prefetch)
-          const int gsrc = (4 * t + lp) & 31, gslot = t >> 3;
-          const float h = __shfl_sync(0xffffffffu, pick(gh, gslot), gsrc);
-          const float w = __shfl_sync(0xffffffffu, pick(gw, gslot), gsrc);
-          const float mraw = __shfl_sync(0xffffffffu, pick(gm, gslot), gsrc);
-          const float m = pv ? mraw : 0.f;
-          const float hf = floorf(h), wf = floorf(w);
-          const int hl = (int)hf, wl = (int)wf;
-          const float lh = h - hf, lw = w - wf, hh = 1.f - lh, hw = 1.f - lw;
-          uint32_t cval = 0u;
-          if (pv && (h > -1.f) && (w > -1.f) && (h < (float)P.H) && (w < (float)P.W)) {
-            const bool rr0 = hl >= 0, rr1 = hl + 1 <= P.H - 1, cc0 = wl >= 0, cc1 = wl + 1 <= P.W - 1;
-            cval = (rr0 && cc0 ? 1u : 0u) | (rr0 && cc1 ? 2u : 0u) | (rr1 && cc0 ? 4u : 0u) | (rr1 && cc1 ? 8u : 0u);
-          }
+          // sampling geometry of this sample and tap (the unit's table)
+          const uint32_t ea = gtab + (uint32_t)(4 * t + lp) * 32u;
+          const uint4 e0 = lds_v4(ea), e1 = lds_v4(ea + 16u);
+          const uint32_t cval = e0.z;
+          const int gi0 = (int)e0.w;
+          const float lh = __uint_as_float(e1.x), lw = __uint_as_float(e1.y), m = __uint_as_float(e1.z);
+          const float hh = 1.f - lh, hw = 1.f - lw;
           const float bw[4] = {(cval & 1u) ? hh * hw : 0.f, (cval & 2u) ? hh * lw : 0.f,
                                (cval & 4u) ? lh * hw : 0.f, (cval & 8u) ? lh * lw : 0.f};
-          // window position of each corner (-1: outside the window)
           int wpix[4];
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const int wr = hl + (c >> 1) - r0, wc = wl + (c & 1) - c0;
-            wpix[c] = ((cval >> c) & 1u) && wr >= 0 && wr < kWH && wc >= 0 && wc < kWW ? wr * kWW + wc : -1;
-          }
+          for (int c = 0; c < 4; ++c)
+            wpix[c] = (int)(int16_t)(((c < 2 ? e0.x : e0.y) >> (16 * (c & 1))) & 0xffffu);
           // A entry of corner q (lanes 0-3 of the sample): row = window pixel, column = sample
           uint32_t mine = kNoEntry;
           if (q < 4) {
@@ -316,13 +362,16 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_bwd_scatter_tc_kernel(const _
           }
 #pragma unroll
           for (int s2 = 0; s2 < kAS; ++s2) if (s2 == as_) rem[s2] = mine;
+          if (warp == 0 && nch < 130) DCN_TS(6 * nch + 2);
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) mbar_arrive(afull0 + 8 * as_);
           if (++as_ == kAS) { as_ = 0; aph ^= 1u; }
-          if (warp == 0 && nch < 200) DCN_TS(4 * nch + 2);
+          flush_deferred();
+          if (warp == 0 && nch < 130) DCN_TS(6 * nch + 3);
           // phase 2: corners and gcol -> S sums, sampled columns, out-of-window scatter
           if (!mbar_wait_warp(bfull0 + 8 * bs, bph, a.err, &abort_flag)) { ok = false; break; }
+          if (warp == 0 && nch < 130) DCN_TS(6 * nch + 4);
           const int cofs = un.g * P.Cgp + cb * kChunk;
           uint4 raw[4];
 #pragma unroll
@@ -330,7 +379,7 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_bwd_scatter_tc_kernel(const _
             if (wpix[c] >= 0) {
               raw[c] = lds_v4(xwin + (uint32_t)wpix[c] * 128u + (uint32_t)((q ^ (wpix[c] & 7)) << 4));
             } else if ((cval >> c) & 1u) {
-              const int gi = un.b * HW + (hl + (c >> 1)) * P.W + wl + (c & 1);
+              const int gi = gi0 + (c >> 1) * P.W + (c & 1);
               raw[c] = ldg_nc_v4(xt + (size_t)(unsigned)(gi * P.CS + cofs + q * 8));
             } else {
               raw[c] = make_uint4(0u, 0u, 0u, 0u);
@@ -338,21 +387,28 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_bwd_scatter_tc_kernel(const _
           }
           float gc[8];
           unpack8<T>(lds_v4(bstage + (uint32_t)k * 128u + (uint32_t)((q ^ (k & 7)) << 4)), gc);
+          // packed f32x2 arithmetic: two channels per instruction
           float S[4], col[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) col[e] = 0.f;
+          float2 col2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                            make_float2(0.f, 0.f)};
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             float v[8];
             unpack8<T>(raw[c], v);
-            float sc = 0.f;
             const float wcm = bw[c] * m;
+            float2 sp = make_float2(0.f, 0.f);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              sc = fmaf(gc[e], v[e], sc);
-              col[e] = fmaf(wcm, v[e], col[e]);
+            for (int e = 0; e < 8; e += 2) {
+              const float2 ve = make_float2(v[e], v[e + 1]);
+              sp = fma2(make_float2(gc[e], gc[e + 1]), ve, sp);
+              col2[e >> 1] = fma2(ve, make_float2(wcm, wcm), col2[e >> 1]);
             }
-            S[c] = sc;
+            S[c] = sp.x + sp.y;
+          }
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            col[2 * e] = col2[e].x;
+            col[2 * e + 1] = col2[e].y;
           }
           // sampled columns for the weight gradient (B tiles of dcn_bwd_weight)
           if (pv && a.cols != nullptr) {
@@ -362,15 +418,16 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_bwd_scatter_tc_kernel(const _
             uint8_t* dst = a.cols + ((size_t)(unsigned)(pix >> 6) * P.nsplit * natoms + atom) * 8192u +
                            crow * 128 + ((q ^ (crow & 7)) << 4);
             constexpr int kBF = OpOf<T>::kBF16;
-            *reinterpret_cast<uint4*>(dst) = make_uint4(pack2<kBF>(col[0], col[1]), pack2<kBF>(col[2], col[3]),
-                                                        pack2<kBF>(col[4], col[5]), pack2<kBF>(col[6], col[7]));
+            dcol = reinterpret_cast<uint4*>(dst);
+            vcol = make_uint4(pack2<kBF>(col[0], col[1]), pack2<kBF>(col[2], col[3]),
+                              pack2<kBF>(col[4], col[5]), pack2<kBF>(col[6], col[7]));
           }
           // corners outside the window: straight into the accumulator
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             if (wpix[c] < 0 && ((cval >> c) & 1u)) {
               const float sk = bw[c] * m;
-              const int gi = un.b * HW + (hl + (c >> 1)) * P.W + wl + (c & 1);
+              const int gi = gi0 + (c >> 1) * P.W + (c & 1);
               float* dst = a.gx_nhwc + (size_t)(unsigned)(gi * P.CS + cofs);
               red_add_v4(dst + slice_lo(q), gc[0] * sk, gc[1] * sk, gc[2] * sk, gc[3] * sk);
               red_add_v4(dst + slice_hi(q), gc[4] * sk, gc[5] * sk, gc[6] * sk, gc[7] * sk);
@@ -379,7 +436,7 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_bwd_scatter_tc_kernel(const _
           __syncwarp();
           if (lane == 0) mbar_arrive(bempty0 + 8 * bs);
           if (++bs == kBS) { bs = 0; bph ^= 1u; }
-          if (warp == 0 && nch < 200) DCN_TS(4 * nch + 3);
+          if (warp == 0 && nch < 130) DCN_TS(6 * nch + 5);
           // per-sample sums over the 8 lanes' channels
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
@@ -402,10 +459,12 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_bwd_scatter_tc_kernel(const _
               const float ah = hw * (S[2] - S[0]) + lw * (S[3] - S[1]);
               const float aw = hh * (S[1] - S[0]) + lh * (S[3] - S[2]);
               const int ob = un.b * P.off_bs + (un.g * 2 * K2 + 2 * t) * P.off_cs + p * P.off_ps;
-              goff[ob] = Elem<T>::from_f(ah * m);
-              goff[ob + P.off_cs] = Elem<T>::from_f(aw * m);
-              gmsk[un.b * P.msk_bs + (un.g * K2 + t) * P.msk_cs + p * P.msk_ps] =
-                  Elem<T>::from_f(P.mask_logit ? am * m * (1.f - m) : am);
+              doff = goff + ob;
+              doffs = P.off_cs;
+              dmsk = gmsk + un.b * P.msk_bs + (un.g * K2 + t) * P.msk_cs + p * P.msk_ps;
+              vh = Elem<T>::from_f(ah * m);
+              vw = Elem<T>::from_f(aw * m);
+              vm = Elem<T>::from_f(P.mask_logit ? am * m * (1.f - m) : am);
             }
           }
         }
@@ -415,6 +474,7 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_bwd_scatter_tc_kernel(const _
         if (++xs == kXS) { xs = 0; xph ^= 1u; }
       }
     }
+    flush_deferred();
   } else if (warp < kTmaWarp) {
     regs_dec<64>();
     // ------------------------------------------------ epilogue: window -> grad_input accumulator
@@ -568,7 +628,7 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_bwd_scatter_tc_kernel(const _
 
 size_t backward_scatter_tc_smem(const Plan& P) {
   return 1024 + (size_t)kXS * kXBytes + (size_t)kAS * kABytes + (size_t)kBS * kBBytes + kStgBytes +
-         (P.nCB > 1 ? (size_t)P.K2 * 64 * 4 * sizeof(float) : 0);
+         (size_t)kSimtWarps * 4 * P.K2 * 32 + (P.nCB > 1 ? (size_t)P.K2 * 64 * 4 * sizeof(float) : 0);
 }
 
 bool backward_scatter_tc_eligible(const Plan& P) {
