@@ -19,9 +19,9 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 _CHILD = r"""
 import os, sys
-sys.path.insert(0, sys.argv[1])
 sys.path.insert(0, sys.argv[2])
 sys.path.insert(0, os.path.join(sys.argv[2], "tests"))
+sys.path.insert(0, sys.argv[1])          # the study build first
 import torch
 import oracle
 from dcn_cases import Case, make_inputs, rel_err
