@@ -34,8 +34,9 @@
 //
 // CTA roles (768 threads, one CTA per SM, persistent over (tile, group) units,
 // 64-channel blocks cb inside a unit):
-//   warps 0-15  SIMT: sample k = 4 * warp + lane / 8 of each K step, 8 lanes
-//               per sample (16-byte slices of 8 channels)
+//   warps 0-15  SIMT, two groups of 8 warps taking alternate taps: sample
+//               k = 8 * (warp % 8) + lane / 4 of a K step, 4 lanes per sample
+//               (two 16-byte slices of 8 channels each)
 //   warps 16-19 epilogue: TMEM (window x 64 channels, fp32) -> staging in shared
 //               memory -> TMA reduction (add) into the grad_input accumulator
 //   warp 20     TMA: x windows (2-slot ring), gcol tiles (3-slot ring)
@@ -60,7 +61,7 @@ constexpr int kEpiWarp0 = 16;
 constexpr int kTmaWarp = 20, kMmaWarp = 21;
 constexpr int kThreads = 24 * 32;
 constexpr int kXS = 2, kAS = 2, kBS = 3;  // ring depths: x windows, A stages, gcol tiles
-constexpr int kGS = 2;                    // geometry slots per lane: 4 samples x K2 <= 16 taps
+constexpr int kGS = 2;                    // K2 <= 8 * kGS = 16 taps (geometry table size)
 constexpr uint32_t kXBytes = kWin * 128;  // 32 KB
 constexpr uint32_t kABytes = kWin * 128;  // 32 KB: 2 M tiles x 128 rows x 128 B
 constexpr uint32_t kBBytes = 64 * 128;    // 8 KB
@@ -169,7 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_bwd_scatter_tc_kernel(const _
   const uint32_t stg = bring + kBS * kBBytes;
   // per-warp sample geometry of the current unit: 4 * K2 entries of 32 bytes
   const uint32_t geo = stg + kStgBytes;
-  const uint32_t geo_warp_bytes = (uint32_t)(4 * K2) * 32u;
+  const uint32_t geo_warp_bytes = (uint32_t)(8 * ((K2 + 1) / 2)) * 32u;
   float* sbuf = reinterpret_cast<float*>(smem_raw + (geo + kSimtWarps * geo_warp_bytes - smem_u32(smem_raw)));
   const uint32_t xfull0 = smem_u32(&bars[0]), xempty0 = xfull0 + 8 * kXS;
   const uint32_t afull0 = xempty0 + 8 * kXS, aempty0 = afull0 + 8 * kAS;
@@ -183,12 +184,12 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_bwd_scatter_tc_kernel(const _
       mbar_init(xempty0 + 8 * i, kSimtWarps);
     }
     for (int i = 0; i < kAS; ++i) {
-      mbar_init(afull0 + 8 * i, kSimtWarps);
+      mbar_init(afull0 + 8 * i, kSimtWarps / 2);   // one group of 8 warps per A stage
       mbar_init(aempty0 + 8 * i, 1);
     }
     for (int i = 0; i < kBS; ++i) {
       mbar_init(bfull0 + 8 * i, 1);
-      mbar_init(bempty0 + 8 * i, kSimtWarps + 1);   // SIMT warps read it too, then the MMA commit
+      mbar_init(bempty0 + 8 * i, kSimtWarps / 2 + 1);   // the step's SIMT group reads it too, then the MMA commit
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(tfull0 + 8 * i, 1);
@@ -209,40 +210,51 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_bwd_scatter_tc_kernel(const _
   const uint32_t tmem_base = tmem_slot;
   pdl_wait();
 
-  // registers by warpgroup (launch pool 768 x 80): SIMT 4 x 128 x 96 + epilogue
-  // 128 x 64 + TMA / MMA 128 x 32 = 61440
+  // registers by warpgroup (launch pool 768 x 80): SIMT 4 x 128 x 104 +
+  // epilogue 128 x 40 + TMA / MMA 128 x 24 = 61440
   if (warp < kSimtWarps) {
-    regs_inc<96>();
+    regs_inc<104>();
     // ------------------------------------------------ SIMT: samples, A entries
+    // Two groups of 8 warps take the taps in turn: group G the taps t with
+    // (t + par) % 2 == G, par = 0, or for nCB == 1 the CTA's unit count % 2 so
+    // that an odd K2 balances over two units (with several channel blocks a tap
+    // stays with one group, whose lanes accumulate its S sums over the blocks).
+    // A stage G belongs to group G.  In a step, warp wg of the group handles
+    // samples 8 wg .. 8 wg + 7, 4 lanes per sample, each lane 16 channels
+    // (16-byte slices 2 q4 and 2 q4 + 1 of the 64-channel block).
     const T* __restrict__ xt = reinterpret_cast<const T*>(a.xt);
     const T* __restrict__ off = reinterpret_cast<const T*>(a.offset);
     const T* __restrict__ msk = reinterpret_cast<const T*>(a.mask);
     T* __restrict__ goff = reinterpret_cast<T*>(a.goffset);
     T* __restrict__ gmsk = reinterpret_cast<T*>(a.gmask);
-    const int lp = lane >> 3, q = lane & 7;
-    const int k = 4 * warp + lp;                 // sample (pixel of the tile) of this lane group
+    const int grp = warp >> 3, wg = warp & 7;
+    const int lp = lane >> 2, q4 = lane & 3;
+    const int k = 8 * wg + lp;                   // sample (pixel of the tile) of this lane group
     const int kr = k >> 3, kc = k & 7;
     const int HW = P.H * P.W;
     const int nblk = P.NC / kChunk, natoms = P.nU * nblk;
-    uint32_t rem[kAS];                           // the A entry this lane wrote in each stage
-#pragma unroll
-    for (int i = 0; i < kAS; ++i) rem[i] = kNoEntry;
-    int xs = 0, as_ = 0, bs = 0;
-    uint32_t xph = 0, aph = 0, bph = 0;
+    const uint32_t astage = aring + (uint32_t)grp * kABytes;   // this group's A stage
+    uint32_t rem = kNoEntry;                     // the A entry this lane wrote last time
+    int xs = 0;
+    uint32_t xph = 0, aph = 0;
     bool ok = true;
-    int nch = 0;                                 // K steps done (timestamps)
-    // Global writes of a K step (its sampled column and, for lane q == 0, the
-    // grad_offset / grad_mask values) are issued after the NEXT step's A
-    // entries have been fenced and published: the proxy fence before that
-    // publication would otherwise wait for them to complete.
+    int n = 0;                                   // global K step counter (both groups; B slot n % kBS)
+    int uit = 0;                                 // units done by this CTA
+    // Global writes of a K step (its sampled columns and, for lane q4 == 0, the
+    // grad_offset / grad_mask values) are issued after the group's NEXT step's A
+    // entries have been fenced and published, so the proxy fence before that
+    // publication does not wait for them.
     uint4* dcol = nullptr;
-    uint4 vcol = make_uint4(0u, 0u, 0u, 0u);
+    uint4 vcol0 = make_uint4(0u, 0u, 0u, 0u), vcol1 = vcol0;
     T* doff = nullptr;
     T* dmsk = nullptr;
     int doffs = 0;
     T vh = Elem<T>::from_f(0.f), vw = vh, vm = vh;
     auto flush_deferred = [&]() {
-      if (dcol != nullptr) *dcol = vcol;
+      if (dcol != nullptr) {
+        dcol[0] = vcol0;
+        dcol[1] = vcol1;
+      }
       if (doff != nullptr) {
         doff[0] = vh;
         doff[doffs] = vw;
@@ -251,46 +263,40 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_bwd_scatter_tc_kernel(const _
       dcol = nullptr;
       doff = nullptr;
     };
-    if (warp == 0) DCN_TS(1000);
-    for (int u = blockIdx.x; u < nUnits && ok; u += gridDim.x) {
+    // geometry table of this warp for the current unit: its 8 samples x the
+    // taps of its group, entries of 32 bytes
+    const uint32_t gtab = geo + (uint32_t)warp * geo_warp_bytes;
+    for (int u = blockIdx.x; u < nUnits && ok; u += gridDim.x, ++uit) {
       const Unit un = unit_of(u, P, nTx, nTy);
+      const int par = nCB == 1 ? (uit & 1) : 0;
+      const int t0 = (grp + par) & 1;            // first tap of this group
       const int ho = un.ho0 + kr, wo = un.wo0 + kc;
       const bool pv = ho < P.Ho && wo < P.Wo;
       const int p = ho * P.Wo + wo;
       const int pix = un.b * P.HoWo + p;         // flat pixel (one chunk: pix0 == 0)
       const int r0 = window_origin(un.ho0 * P.sh - P.ph, span_h, kWH, P.H);
       const int c0 = window_origin(un.wo0 * P.sw - P.pw, span_w, kWW, P.W);
-      // sampling geometry of the warp's 4 samples for every tap, built once per
-      // unit (all offset / mask loads in flight together; entry e = 4 t + s of
-      // sample 4 * warp + s by lane e % 32) into the warp's shared-memory table:
-      //   {window pixel of corners 0,1 (int16 x 2), of corners 2,3, corner
-      //    validity bits, image pixel of corner 0} {lh, lw, mask, -}
-      const uint32_t gtab = geo + (uint32_t)warp * geo_warp_bytes;
       {
-        uint32_t rh[kGS], rw[kGS], rm[kGS];
-#pragma unroll
-        for (int sl = 0; sl < kGS; ++sl) {
-          const int e = sl * 32 + lane, te = e >> 2, ke = 4 * warp + (e & 3);
+        // entry j = (sample 8 wg + j % 8, tap t0 + 2 (j / 8)) by lane j % 32
+        const int nE = 8 * ((K2 - t0 + 1) / 2);
+        for (int j0 = 0; j0 < nE; j0 += 32) {
+          const int j = j0 + lane;
+          const int ke = 8 * wg + (j & 7), te = t0 + 2 * (j >> 3);
           const int hoe = un.ho0 + (ke >> 3), woe = un.wo0 + (ke & 7);
-          rh[sl] = rw[sl] = rm[sl] = 0u;
-          if (te < K2 && hoe < P.Ho && woe < P.Wo) {
+          const bool pve = j < nE && hoe < P.Ho && woe < P.Wo;
+          uint32_t rh = 0u, rw = 0u, rm = 0u;
+          if (pve) {
             const int pe = hoe * P.Wo + woe;
             const int ob = un.b * P.off_bs + (un.g * 2 * K2 + 2 * te) * P.off_cs + pe * P.off_ps;
-            rh[sl] = ldg_raw<T>(off + ob);
-            rw[sl] = ldg_raw<T>(off + ob + P.off_cs);
-            rm[sl] = ldg_raw<T>(msk + un.b * P.msk_bs + (un.g * K2 + te) * P.msk_cs + pe * P.msk_ps);
+            rh = ldg_raw<T>(off + ob);
+            rw = ldg_raw<T>(off + ob + P.off_cs);
+            rm = ldg_raw<T>(msk + un.b * P.msk_bs + (un.g * K2 + te) * P.msk_cs + pe * P.msk_ps);
           }
-        }
-#pragma unroll
-        for (int sl = 0; sl < kGS; ++sl) {
-          const int e = sl * 32 + lane, te = e >> 2, ke = 4 * warp + (e & 3);
-          if (te < K2) {
+          if (j < nE) {
             const int ie = te / P.kw, je = te - ie * P.kw;
-            const int hoe = un.ho0 + (ke >> 3), woe = un.wo0 + (ke & 7);
-            const bool pve = hoe < P.Ho && woe < P.Wo;
-            const float h = (float)(hoe * P.sh - P.ph + ie * P.dh) + raw_to_f<T>(rh[sl]);
-            const float w = (float)(woe * P.sw - P.pw + je * P.dw) + raw_to_f<T>(rw[sl]);
-            float mv = raw_to_f<T>(rm[sl]);
+            const float h = (float)(hoe * P.sh - P.ph + ie * P.dh) + raw_to_f<T>(rh);
+            const float w = (float)(woe * P.sw - P.pw + je * P.dw) + raw_to_f<T>(rw);
+            float mv = raw_to_f<T>(rm);
             if (P.mask_logit) mv = 1.f / (1.f + __expf(-mv));   // sigmoid of a predictor logit
             const float hf = floorf(h), wf = floorf(w);
             const int hl = (int)hf, wl = (int)wf;
@@ -306,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_bwd_scatter_tc_kernel(const _
               const int wp = ((cv >> c) & 1u) && wr >= 0 && wr < kWH && wc >= 0 && wc < kWW ? wr * kWW + wc : -1;
               wpk[c >> 1] |= ((uint32_t)wp & 0xffffu) << (16 * (c & 1));
             }
-            const uint32_t ea = gtab + (uint32_t)e * 32u;
+            const uint32_t ea = gtab + (uint32_t)j * 32u;
             sts_v4(ea, make_uint4(wpk[0], wpk[1], cv, (uint32_t)(un.b * HW + hl * P.W + wl)));
             sts_v4(ea + 16u, make_uint4(__float_as_uint(h - hf), __float_as_uint(w - wf),
                                         __float_as_uint(pve ? mv : 0.f), 0u));
@@ -317,19 +323,16 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_bwd_scatter_tc_kernel(const _
       for (int cb = 0; cb < nCB && ok; ++cb) {
         if (!mbar_wait_warp(xfull0 + 8 * xs, xph, a.err, &abort_flag)) { ok = false; break; }
         const uint32_t xwin = xring + xs * kXBytes;
-        for (int t = 0; t < K2; ++t, ++nch) {
-          if (warp == 0 && nch < 130) DCN_TS(6 * nch);
-          // phase 1 (feeds the MMA): geometry and this sample's A entries
-          if (!mbar_wait_warp(aempty0 + 8 * as_, aph ^ 1u, a.err, &abort_flag)) { ok = false; break; }
-          if (warp == 0 && nch < 130) DCN_TS(6 * nch + 1);
-          const uint32_t astage = aring + as_ * kABytes, bstage = bring + bs * kBBytes;
-          // clear what this lane wrote into the stage last time round
-          uint32_t prev = kNoEntry;
-#pragma unroll
-          for (int s2 = 0; s2 < kAS; ++s2) if (s2 == as_) prev = rem[s2];
-          if (prev != kNoEntry) sts_u16(prev, 0);
-          // sampling geometry of this sample and tap (the unit's table)
-          const uint32_t ea = gtab + (uint32_t)(4 * t + lp) * 32u;
+        for (int t = 0; t < K2; ++t, ++n) {
+          if (((t + par) & 1) != grp) continue;
+          const int bs = n % kBS;
+          const uint32_t bph = (uint32_t)(n / kBS) & 1u;
+          const int nch = (int)((uint32_t)n >> 1);
+          if (warp == 0 && nch < 260) DCN_TS(3 * nch);
+          // phase 1 (feeds the MMA): this sample's A entries
+          if (!mbar_wait_warp(aempty0 + 8 * grp, aph ^ 1u, a.err, &abort_flag)) { ok = false; break; }
+          if (rem != kNoEntry) sts_u16(rem, 0);   // clear what this lane wrote last time round
+          const uint32_t ea = gtab + (uint32_t)(8 * ((t - t0) >> 1) + lp) * 32u;
           const uint4 e0 = lds_v4(ea), e1 = lds_v4(ea + 16u);
           const uint32_t cval = e0.z;
           const int gi0 = (int)e0.w;
@@ -341,86 +344,89 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_bwd_scatter_tc_kernel(const _
 #pragma unroll
           for (int c = 0; c < 4; ++c)
             wpix[c] = (int)(int16_t)(((c < 2 ? e0.x : e0.y) >> (16 * (c & 1))) & 0xffffu);
-          // A entry of corner q (lanes 0-3 of the sample): row = window pixel, column = sample
-          uint32_t mine = kNoEntry;
-          if (q < 4) {
+          // A entry of corner q4: row = window pixel, column = sample
+          rem = kNoEntry;
+          {
             float bq = 0.f;
             int wp = -1;
 #pragma unroll
             for (int c = 0; c < 4; ++c)
-              if (c == q) { bq = bw[c]; wp = wpix[c]; }
+              if (c == q4) { bq = bw[c]; wp = wpix[c]; }
             const float wcm = bq * m;
             if (wp >= 0 && wcm != 0.f) {
               const int mt = wp >> 7, rr = wp & 127;
-              mine = astage + (uint32_t)mt * 16384u + (uint32_t)rr * 128u +
-                     (uint32_t)(((k >> 3) ^ (rr & 7)) << 4) + (uint32_t)(k & 7) * 2u;
+              rem = astage + (uint32_t)mt * 16384u + (uint32_t)rr * 128u +
+                    (uint32_t)(((k >> 3) ^ (rr & 7)) << 4) + (uint32_t)(k & 7) * 2u;
               uint16_t hv;
               if constexpr (OpOf<T>::kBF16) hv = __bfloat16_as_ushort(__float2bfloat16_rn(wcm));
               else hv = __half_as_ushort(__float2half_rn(wcm));
-              sts_u16(mine, hv);
+              sts_u16(rem, hv);
             }
           }
-#pragma unroll
-          for (int s2 = 0; s2 < kAS; ++s2) if (s2 == as_) rem[s2] = mine;
-          if (warp == 0 && nch < 130) DCN_TS(6 * nch + 2);
           fence_proxy_async_smem();
           __syncwarp();
-          if (lane == 0) mbar_arrive(afull0 + 8 * as_);
-          if (++as_ == kAS) { as_ = 0; aph ^= 1u; }
+          if (lane == 0) mbar_arrive(afull0 + 8 * grp);
+          aph ^= 1u;
           flush_deferred();
-          if (warp == 0 && nch < 130) DCN_TS(6 * nch + 3);
+          if (warp == 0 && nch < 260) DCN_TS(3 * nch + 1);
           // phase 2: corners and gcol -> S sums, sampled columns, out-of-window scatter
           if (!mbar_wait_warp(bfull0 + 8 * bs, bph, a.err, &abort_flag)) { ok = false; break; }
-          if (warp == 0 && nch < 130) DCN_TS(6 * nch + 4);
+          const uint32_t bstage = bring + bs * kBBytes;
           const int cofs = un.g * P.Cgp + cb * kChunk;
-          uint4 raw[4];
+          // the lane's two 8-channel slices one after the other (registers)
+          float S[4] = {0.f, 0.f, 0.f, 0.f};
+          uint4 vcs[2];
+          float gcs[2][8];
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            if (wpix[c] >= 0) {
-              raw[c] = lds_v4(xwin + (uint32_t)wpix[c] * 128u + (uint32_t)((q ^ (wpix[c] & 7)) << 4));
-            } else if ((cval >> c) & 1u) {
-              const int gi = gi0 + (c >> 1) * P.W + (c & 1);
-              raw[c] = ldg_nc_v4(xt + (size_t)(unsigned)(gi * P.CS + cofs + q * 8));
-            } else {
-              raw[c] = make_uint4(0u, 0u, 0u, 0u);
+          for (int jj = 0; jj < 2; ++jj) {
+            const int sl = 2 * q4 + jj;
+            uint4 raw[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              if (wpix[c] >= 0) {
+                raw[c] = lds_v4(xwin + (uint32_t)wpix[c] * 128u + (uint32_t)((sl ^ (wpix[c] & 7)) << 4));
+              } else if ((cval >> c) & 1u) {
+                const int gi = gi0 + (c >> 1) * P.W + (c & 1);
+                raw[c] = ldg_nc_v4(xt + (size_t)(unsigned)(gi * P.CS + cofs + sl * 8));
+              } else {
+                raw[c] = make_uint4(0u, 0u, 0u, 0u);
+              }
             }
-          }
-          float gc[8];
-          unpack8<T>(lds_v4(bstage + (uint32_t)k * 128u + (uint32_t)((q ^ (k & 7)) << 4)), gc);
-          // packed f32x2 arithmetic: two channels per instruction
-          float S[4], col[8];
-          float2 col2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
-                            make_float2(0.f, 0.f)};
+            unpack8<T>(lds_v4(bstage + (uint32_t)k * 128u + (uint32_t)((sl ^ (k & 7)) << 4)), gcs[jj]);
+            // packed f32x2 arithmetic: two channels per instruction
+            float2 col2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                              make_float2(0.f, 0.f)};
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            float v[8];
-            unpack8<T>(raw[c], v);
-            const float wcm = bw[c] * m;
-            float2 sp = make_float2(0.f, 0.f);
+            for (int c = 0; c < 4; ++c) {
+              const float wcm = bw[c] * m;
+              float v[8];
+              unpack8<T>(raw[c], v);
+              float2 sp = make_float2(0.f, 0.f);
 #pragma unroll
-            for (int e = 0; e < 8; e += 2) {
-              const float2 ve = make_float2(v[e], v[e + 1]);
-              sp = fma2(make_float2(gc[e], gc[e + 1]), ve, sp);
-              col2[e >> 1] = fma2(ve, make_float2(wcm, wcm), col2[e >> 1]);
+              for (int e = 0; e < 8; e += 2) {
+                const float2 ve = make_float2(v[e], v[e + 1]);
+                sp = fma2(make_float2(gcs[jj][e], gcs[jj][e + 1]), ve, sp);
+                col2[e >> 1] = fma2(ve, make_float2(wcm, wcm), col2[e >> 1]);
+              }
+              S[c] += sp.x + sp.y;
             }
-            S[c] = sp.x + sp.y;
-          }
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            col[2 * e] = col2[e].x;
-            col[2 * e + 1] = col2[e].y;
+            constexpr int kBF = OpOf<T>::kBF16;
+            vcs[jj] = make_uint4(pack2<kBF>(col2[0].x, col2[0].y), pack2<kBF>(col2[1].x, col2[1].y),
+                                 pack2<kBF>(col2[2].x, col2[2].y), pack2<kBF>(col2[3].x, col2[3].y));
           }
           // sampled columns for the weight gradient (B tiles of dcn_bwd_weight)
           if (pv && a.cols != nullptr) {
             const int crow = pix & 63;
             const int cch = cb / nblk, cblk = cb - cch * nblk;
             const int atom = ((t * P.dg + un.g) * P.nCC + cch) * nblk + cblk;
-            uint8_t* dst = a.cols + ((size_t)(unsigned)(pix >> 6) * P.nsplit * natoms + atom) * 8192u +
-                           crow * 128 + ((q ^ (crow & 7)) << 4);
-            constexpr int kBF = OpOf<T>::kBF16;
-            dcol = reinterpret_cast<uint4*>(dst);
-            vcol = make_uint4(pack2<kBF>(col[0], col[1]), pack2<kBF>(col[2], col[3]),
-                              pack2<kBF>(col[4], col[5]), pack2<kBF>(col[6], col[7]));
+            uint8_t* rowp = a.cols + ((size_t)(unsigned)(pix >> 6) * P.nsplit * natoms + atom) * 8192u + crow * 128;
+            // slices 2 q4 and 2 q4 + 1 of the swizzled row are the two chunks of
+            // one 32-byte pair ((2 q4) ^ r and (2 q4 + 1) ^ r differ in bit 0):
+            // odd rows hold them in swapped order
+            const bool odd = (crow & 1) != 0;
+            vcol0 = odd ? vcs[1] : vcs[0];
+            vcol1 = odd ? vcs[0] : vcs[1];
+            dcol = reinterpret_cast<uint4*>(rowp + ((((2 * q4) ^ (crow & 7)) & ~1) << 4));
           }
           // corners outside the window: straight into the accumulator
 #pragma unroll
@@ -429,22 +435,26 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_bwd_scatter_tc_kernel(const _
               const float sk = bw[c] * m;
               const int gi = gi0 + (c >> 1) * P.W + (c & 1);
               float* dst = a.gx_nhwc + (size_t)(unsigned)(gi * P.CS + cofs);
-              red_add_v4(dst + slice_lo(q), gc[0] * sk, gc[1] * sk, gc[2] * sk, gc[3] * sk);
-              red_add_v4(dst + slice_hi(q), gc[4] * sk, gc[5] * sk, gc[6] * sk, gc[7] * sk);
+#pragma unroll
+              for (int jj = 0; jj < 2; ++jj) {
+                const int sl = 2 * q4 + jj;
+                red_add_v4(dst + slice_lo(sl), gcs[jj][0] * sk, gcs[jj][1] * sk, gcs[jj][2] * sk,
+                           gcs[jj][3] * sk);
+                red_add_v4(dst + slice_hi(sl), gcs[jj][4] * sk, gcs[jj][5] * sk, gcs[jj][6] * sk,
+                           gcs[jj][7] * sk);
+              }
             }
           }
           __syncwarp();
           if (lane == 0) mbar_arrive(bempty0 + 8 * bs);
-          if (++bs == kBS) { bs = 0; bph ^= 1u; }
-          if (warp == 0 && nch < 130) DCN_TS(6 * nch + 5);
-          // per-sample sums over the 8 lanes' channels
+          if (warp == 0 && nch < 260) DCN_TS(3 * nch + 2);
+          // per-sample sums over the 4 lanes' channels
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             S[c] += __shfl_xor_sync(0xffffffffu, S[c], 1);
             S[c] += __shfl_xor_sync(0xffffffffu, S[c], 2);
-            S[c] += __shfl_xor_sync(0xffffffffu, S[c], 4);
           }
-          if (q == 0 && pv) {
+          if (q4 == 0 && pv) {
             if (nCB > 1) {
               float* sb = sbuf + ((size_t)t * 64 + k) * 4;
 #pragma unroll
@@ -476,7 +486,7 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_bwd_scatter_tc_kernel(const _
     }
     flush_deferred();
   } else if (warp < kTmaWarp) {
-    regs_dec<64>();
+    regs_dec<40>();
     // ------------------------------------------------ epilogue: window -> grad_input accumulator
     const int qd = warp & 3;                     // TMEM lane quarter
     // CTA 0 first zeroes the sampled columns of the pixels past the end of the
@@ -511,12 +521,12 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_bwd_scatter_tc_kernel(const _
           const int r = qd * 32 + lane;
           const uint32_t tb = tmem_base + ((uint32_t)(qd * 32) << 16) + (uint32_t)(ab * 128 + mt * 64);
 #pragma unroll 1
-          for (int half = 0; half < 2; ++half) {
-            float v[32];
-            tmem_ld32(tb + half * 32, v);
+          for (int quarter = 0; quarter < 4; ++quarter) {
+            float v[16];
+            tmem_ld16(tb + quarter * 16, v);
 #pragma unroll
-            for (int j4 = 0; j4 < 4; ++j4) {
-              const int jq = half * 4 + j4;      // physical 8-channel slice of these columns
+            for (int j4 = 0; j4 < 2; ++j4) {
+              const int jq = quarter * 2 + j4;   // physical 8-channel slice of these columns
               const int llo = slice_lo(jq), lhi = slice_hi(jq);
               sts_v4(stg + (uint32_t)(llo >> 5) * 16384u + (uint32_t)r * 128u +
                          (uint32_t)((((llo & 31) >> 2) ^ (r & 7)) << 4),
@@ -546,7 +556,7 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_bwd_scatter_tc_kernel(const _
       }
     }
   } else {
-    regs_dec<32>();
+    regs_dec<24>();
     if (warp == kTmaWarp) {
       // ---------------------------------------------- TMA: x windows and gcol tiles
       if (lane == 0) {
@@ -577,15 +587,18 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_bwd_scatter_tc_kernel(const _
       if (lane == 0) {
         constexpr int kBF = OpOf<T>::kBF16;
         const uint32_t idesc = make_idesc(kBF, 0, 1, 128, 64);   // A K-major, B MN-major
-        int as_ = 0, bs = 0, it = 0, mch = 0;
-        uint32_t aph = 0, bph = 0;
+        int bs = 0, it = 0, mch = 0, uit = 0;
+        uint32_t aph2 = 0, bph = 0;              // bit s: phase of A stage s
         bool ok = true;
-        for (int u = blockIdx.x; u < nUnits && ok; u += gridDim.x) {
+        for (int u = blockIdx.x; u < nUnits && ok; u += gridDim.x, ++uit) {
+          const int par = nCB == 1 ? (uit & 1) : 0;
           for (int cb = 0; cb < nCB && ok; ++cb, ++it) {
             const int ab = it & 1;
             if (!mbar_wait(tempty0 + 8 * ab, ((it >> 1) & 1) ^ 1, a.err, &abort_flag)) { ok = false; break; }
             tc_fence_after();
             for (int t = 0; t < K2; ++t, ++mch) {
+              const int as_ = (t + par) & 1;       // the SIMT group (and A stage) of this tap
+              const uint32_t aph = (aph2 >> as_) & 1u;
               if (!mbar_wait(afull0 + 8 * as_, aph, a.err, &abort_flag)) { ok = false; break; }
               if (!mbar_wait(bfull0 + 8 * bs, bph, a.err, &abort_flag)) { ok = false; break; }
               if (mch < 100) DCN_TS(800 + 2 * mch);
@@ -603,7 +616,7 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_bwd_scatter_tc_kernel(const _
               umma_commit(aempty0 + 8 * as_);
               umma_commit(bempty0 + 8 * bs);
               if (mch < 100) DCN_TS(801 + 2 * mch);
-              if (++as_ == kAS) { as_ = 0; aph ^= 1u; }
+              aph2 ^= 1u << as_;
               if (++bs == kBS) { bs = 0; bph ^= 1u; }
             }
             if (!ok) break;
@@ -628,7 +641,7 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_bwd_scatter_tc_kernel(const _
 
 size_t backward_scatter_tc_smem(const Plan& P) {
   return 1024 + (size_t)kXS * kXBytes + (size_t)kAS * kABytes + (size_t)kBS * kBBytes + kStgBytes +
-         (size_t)kSimtWarps * 4 * P.K2 * 32 + (P.nCB > 1 ? (size_t)P.K2 * 64 * 4 * sizeof(float) : 0);
+         (size_t)kSimtWarps * 8 * ((P.K2 + 1) / 2) * 32 + (P.nCB > 1 ? (size_t)P.K2 * 64 * 4 * sizeof(float) : 0);
 }
 
 bool backward_scatter_tc_eligible(const Plan& P) {
