@@ -80,6 +80,10 @@ SMALL = [
     # one-pixel-high / -wide images: the clamped 2x2 corner block degenerates
     Case("thin_h1", 2, 16, 1, 9, 24, 3, 3),
     Case("thin_w1", 1, 16, 6, 1, 24, 3, 3, off_std=2.0),
+    # images large enough for the forward's input windows (Wo % 16 == 0,
+    # W >= 24, H >= 16; Ho = 20: a partial last tile row) and the tile scatter
+    Case("win_20x32", 2, 64, 20, 32, 96, 3, 3, off_std=2.0),
+    Case("win_k1", 2, 64, 16, 32, 64, 1, 1, pad=0),
 ]
 
 

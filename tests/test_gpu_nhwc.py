@@ -13,7 +13,7 @@ CL = torch.channels_last
 TOL = {torch.float32: 1e-4, torch.float16: 1e-2, torch.bfloat16: 1e-2}
 NAMES = ["output", "grad_input", "grad_offset", "grad_mask", "grad_weight", "grad_bias"]
 CASES = [c for c in SMALL if c.name in ("readme_small", "c_odd", "stride2_pad0", "dg4_bf", "edge_c4",
-                                        "k1_nopad", "nobias", "direct_co100", "co512_c512")]
+                                        "k1_nopad", "nobias", "direct_co100", "co512_c512", "win_20x32")]
 CASES.append(Case("k1_c256_co64", 2, 256, 12, 10, 64, 1, 1, pad=0))
 
 
