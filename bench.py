@@ -545,7 +545,7 @@ def config_of(args, wl):
     return {"workload": f"{args.workload}: B={B}/gpu C={C} {H}x{W} Co={Co} {k}x{k} s{s} p{p} "
                         f"d{d} dg{dg}, fwd+bwd", "global_batch": B * args.gpus,
             "parallelism": f"dp{args.gpus}", "l2": "flushed before every step (256 MiB write)",
-            "offset_std_px": off_std}
+            "offset_std_px": off_std, "channels_last": bool(getattr(args, "channels_last", False))}
 
 
 def main():
@@ -560,7 +560,7 @@ def main():
     ap.add_argument("--no-fp32", action="store_true",
                     help="skip the float32 step reported beside a 16-bit run")
     ap.add_argument("--channels-last", action="store_true",
-                    help="stack workloads: channels-last activations (the operator's NHWC layout)")
+                    help="channels-last activations (the operator's NHWC layout)")
     ap.add_argument("--graph", action="store_true",
                     help="stack workloads: capture the training step in a CUDA graph and replay it")
     ap.add_argument("--launch-only", type=int, default=0, metavar="N",
@@ -596,6 +596,9 @@ def main():
     B, C, H, W, Co, k, s, p, d, dg, _ = wl
     Ho, Wo = out_hw(H, W, k, s, p, d)
     x, w, b, off, m, gy = make_inputs(wl, dtype, dev, seed=rank)
+    if args.channels_last:
+        # the operator's NHWC layout: every activation tensor channels-last
+        x, off, m, gy = [t.contiguous(memory_format=torch.channels_last) for t in (x, off, m, gy)]
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 

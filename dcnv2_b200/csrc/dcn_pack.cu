@@ -553,14 +553,22 @@ __global__ void __launch_bounds__(256) pack_gout_nhwc_kernel(const T* __restrict
     }
   }
   if (gb != nullptr) {
-    // lanes l, l + 8, l + 16, l + 24 hold the same chunk
+    // lanes l, l + 8, l + 16, l + 24 hold the same chunk; the warps' sums meet
+    // in shared memory and the CTA adds each Co once to the accumulator (one
+    // global atomic per Co and CTA: same-address atomics from every warp took
+    // hundreds of microseconds)
+    __shared__ float sb[64];
+    if (tid < 64) sb[tid] = 0.f;
+    __syncthreads();
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       float sum = bsum[e];
       sum += __shfl_xor_sync(0xffffffffu, sum, 8);
       sum += __shfl_xor_sync(0xffffffffu, sum, 16);
-      if (lane < 8 && co0 + e < P.Co) atomicAdd(gb + co0 + e, sum);
+      if (lane < 8) atomicAdd(&sb[c * 8 + e], sum);
     }
+    __syncthreads();
+    if (tid < 64 && ko * kChunk + tid < P.Co) atomicAdd(gb + ko * kChunk + tid, sb[tid]);
   }
 }
 
