@@ -172,10 +172,27 @@ bool pdl_enabled() {
 bool make_gout_tmap(const Plan& P, const void* gout, TmaDesc* out) {
   static_assert(sizeof(CUtensorMap) == sizeof(TmaDesc), "tensor map size");
   EncodeTiledFn fn = encode_tiled();
-  if (P.nhwc) return false;   // channels-last grad_output goes through pack_gout_nhwc_kernel
-  if (!fn || !gout || P.esz != 2 || (P.HoWo % 64) != 0) return false;
-  const cuuint64_t dims[3] = {(cuuint64_t)P.HoWo, (cuuint64_t)P.Co, (cuuint64_t)P.B};
-  const cuuint64_t strides[2] = {(cuuint64_t)P.HoWo * 2u, (cuuint64_t)P.Co * P.HoWo * 2u};
+  if (!fn || !gout || P.esz != 2) return false;
+  cuuint64_t dims[3], strides[2];
+  if (P.nhwc) {
+    // channels-last grad_output is a [totalP][Co] matrix: a box of 64 Co x 64
+    // pixels lands in shared memory as the packed block (pixel rows of 128 B,
+    // SW128), so the GEMMs keep the packed operand layouts; blocks may straddle
+    // images and rows past totalP read zeros
+    if ((P.Co % 8) != 0) return false;
+    dims[0] = (cuuint64_t)P.Co;
+    dims[1] = (cuuint64_t)P.totalP;
+    dims[2] = 1;
+    strides[0] = (cuuint64_t)P.Co * 2u;
+    strides[1] = (cuuint64_t)P.totalP * P.Co * 2u;
+  } else {
+    if ((P.HoWo % 64) != 0) return false;
+    dims[0] = (cuuint64_t)P.HoWo;
+    dims[1] = (cuuint64_t)P.Co;
+    dims[2] = (cuuint64_t)P.B;
+    strides[0] = (cuuint64_t)P.HoWo * 2u;
+    strides[1] = (cuuint64_t)P.Co * P.HoWo * 2u;
+  }
   const cuuint32_t box[3] = {64u, 64u, 1u};
   const cuuint32_t estr[3] = {1u, 1u, 1u};
   const CUtensorMapDataType dt =
@@ -494,13 +511,16 @@ static int backward_impl(const dcn_desc* d, const void* input, const void* weigh
     if ((rc = launch_pack_weight_bwd(P, weight, ws + P.off_wd, gw, P.bwd_bytes - P.off_gw, s)) != DCN_OK)
       return rc;
   }
-  // 16-bit grad_output whose 64-pixel blocks never straddle two images is read
-  // by the GEMMs directly (TMA tiles of 64 pixels x 64 Co); otherwise it is
-  // packed into swizzled blocks first (and f32 is split into bf16 hi/lo).
+  // 16-bit grad_output is read by the GEMMs directly (TMA tiles of 64 pixels x
+  // 64 Co) when NCHW with 64-pixel blocks that never straddle two images, or
+  // channels-last with Co % 8 == 0; otherwise it is packed into swizzled
+  // blocks first (and f32 is split into bf16 hi/lo).
   BwdDataArgs a;
   memset(&a, 0, sizeof(a));
-  a.gdirect = P.esz == 2 && aligned16(grad_output) && !gout_packed_forced() &&
-              make_gout_tmap(P, grad_output, &a.gmap);
+  a.gdirect = (P.esz == 2 && aligned16(grad_output) && !gout_packed_forced() &&
+               make_gout_tmap(P, grad_output, &a.gmap))
+                  ? (P.nhwc ? kGoutNhwc : kGoutNchw)
+                  : 0;
   if (!a.gdirect) {
     TraceScope ts(TR_PACK_GRAD_OUTPUT, s);
     const int vec = aligned16(grad_output) && (P.HoWo % 8 == 0);

@@ -204,14 +204,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     regs_dec<56>();
     if (warp < kAWarps) {
       // ---------------------------------------------- grad_out chunk loader
-      // One thread bulk-copies the two pre-packed 64-pixel blocks of each Co
-      // chunk (K-major, 128-byte swizzle; f32: hi and lo) into the A ring.
+      // One thread copies the two 64-pixel blocks of each Co chunk into the A
+      // ring: pre-packed blocks (K-major, 128-byte swizzle; f32: hi and lo) by
+      // bulk copy, or TMA boxes of 16-bit grad_output.
       if (warp == 0 && lane == 0) {
         int r = 0;                                  // A ring slot and its phase
         uint32_t ph = 0;
         bool ok = true;
         const uint32_t blk = NS * 8192u;
-        const bool gdirect = NS == 1 && a.gdirect;
+        const bool gdirect = NS == 1 && a.gdirect == kGoutNchw;
+        const bool gnhwc = NS == 1 && a.gdirect == kGoutNhwc;
         const int nPBi = P.HoWo / 64;              // 64-pixel blocks per image (gdirect)
         for (int tile = r0; tile < nTiles && ok; tile += cpu) {
           for (int ko = 0; ko < P.nKo; ++ko, (++r == RA ? (r = 0, ph ^= 1u) : 0u)) {
@@ -226,6 +228,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // pixels contiguous, so the tile is MN-major; Co past the end reads zeros
                 const int pbi = pb0 + h, b = pbi / nPBi;
                 tma_load_3d(at + h * 8192u, &a.gmap, (pbi - b * nPBi) * 64, ko * 64, b, afull0 + 8 * r);
+              } else if (gnhwc) {
+                // channels-last: 64 Co of 64 consecutive pixels, the packed block's layout
+                tma_load_3d(at + h * 8192u, &a.gmap, ko * 64, (pb0 + h) * 64, 0, afull0 + 8 * r);
               } else {
                 const uint8_t* src = a.gpk + ((size_t)(pb0 + h) * P.nKo + ko) * blk;
                 bulk_g2s(at + h * 8192u, src, 8192u, afull0 + 8 * r);
@@ -262,7 +267,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // A: packed grad_out chunks are K-major (Co contiguous per pixel row);
         // tiles read from grad_output directly are MN-major (pixels contiguous
         // per Co row, the two 64-pixel halves 8 KB apart)
-        const bool gdirect = NS == 1 && a.gdirect;
+        const bool gdirect = NS == 1 && a.gdirect == kGoutNchw;
         const uint32_t idesc = make_idesc(OpOf<T>::kBF16, gdirect ? 1 : 0, 0, kTileM, NC);
         uint32_t it = 0;
         int ar = 0, ms = 0;                         // A slot / W^T stage and their phases

@@ -71,8 +71,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int ntot = ucount * NC;
   // grad_output read directly (16-bit): A tiles are K-major (pixels contiguous
   // per Co row), and the CTAs of unit set 0 also sum grad_bias from them
-  const bool gdirect = NS == 1 && a.gdirect;
-  const bool bias = gdirect && a.gb != nullptr && set == 0;
+  const bool gdirect = NS == 1 && a.gdirect == kGoutNchw;
+  const bool gnhwc = NS == 1 && a.gdirect == kGoutNhwc;
+  const bool bias = (gdirect || gnhwc) && a.gb != nullptr && set == 0;
 
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bars[2 * kMaxStages + 2];
@@ -143,6 +144,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                           full0 + 8 * s);
               continue;
             }
+            if (gnhwc) {
+              // channels-last: the packed block's layout straight from grad_output
+              tma_load_3d(at + m * kATile + h * 8192u, &a.gmap, ko * 64, ks * 64, 0, full0 + 8 * s);
+              continue;
+            }
             const uint8_t* src = a.gpk + ((size_t)ks * P.nKo + ko) * blk;
             bulk_g2s(at + m * kATile + h * 8192u, src, 8192u, full0 + 8 * s);
             if constexpr (NS == 2)
@@ -204,9 +210,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Thread tid owns Co row tid of every M tile: per stage it adds the 64
       // pixels of its 128-byte row (chunk order is irrelevant to the sum; lane
       // i starts at chunk i % 8 so that eight rows hit eight bank groups).
-      float bsum[kMaxMT];
+      // Channels-last tiles hold 64 pixel rows of 64 Co per half: thread tid
+      // sums the Co pair 2 * (tid & 31) of half (tid >> 5) & 1 over rows
+      // 32 * (tid >> 6) .. +31 (a warp reads one 128-byte row per load).
+      float bsum[kMaxMT], bsum1[kMaxMT];
 #pragma unroll
-      for (int m = 0; m < kMaxMT; ++m) bsum[m] = 0.f;
+      for (int m = 0; m < kMaxMT; ++m) bsum[m] = bsum1[m] = 0.f;
+      const int nh = (tid >> 5) & 1, np = tid & 31, nr0 = 32 * (tid >> 6);
+      const uint32_t ncol = (uint32_t)((2 * np) & 7) * 2u;
+      const int nchunk = (2 * np) >> 3;
       int bs = 0;
       uint32_t bph = 0;
       bool ok = true;
@@ -216,6 +228,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (++bs == S) { bs = 0; bph ^= 1u; }
         if (!mbar_wait_warp(full0 + 8 * s, ph, a.err, &abort_flag)) { ok = false; break; }
         const uint32_t at = sbase + s * stageBytes;
+        if (gnhwc) {
+#pragma unroll
+          for (int m = 0; m < kMaxMT; ++m) {
+            if (m < mcount) {
+              const uint32_t hb = at + m * kATile + (uint32_t)nh * 8192u + ncol;
+              float a0 = 0.f, a1 = 0.f;
+#pragma unroll 8
+              for (int rr = 0; rr < 32; ++rr) {
+                const int r = nr0 + rr;
+                const uint32_t w = lds_u32(hb + (uint32_t)r * 128u + (uint32_t)((nchunk ^ (r & 7)) << 4));
+                a0 += raw_to_f<T>(w & 0xffffu);
+                a1 += raw_to_f<T>(w >> 16);
+              }
+              bsum[m] += a0;
+              bsum1[m] += a1;
+            }
+          }
+        } else {
 #pragma unroll
         for (int m = 0; m < kMaxMT; ++m) {
           if (m < mcount) {
@@ -228,13 +258,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             bsum[m] += acc;
           }
         }
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(empty0 + 8 * s);
       }
       if (ok) {
         for (int m = 0; m < mcount; ++m) {
-          const int co = (mt0 + m) * 128 + tid;
-          if (co < P.Co) atomicAdd(a.gb + co, bsum[m]);
+          if (gnhwc) {
+            const int co = (mt0 + m) * 128 + nh * 64 + 2 * np;
+            if (co < P.Co) atomicAdd(a.gb + co, bsum[m]);
+            if (co + 1 < P.Co) atomicAdd(a.gb + co + 1, bsum1[m]);
+          } else {
+            const int co = (mt0 + m) * 128 + tid;
+            if (co < P.Co) atomicAdd(a.gb + co, bsum[m]);
+          }
         }
       }
     }

@@ -50,14 +50,23 @@ struct FwdArgs {
   int dbg;              // experiment switches (DCN_DEBUG_SKIP); 0 in normal use
 };
 
+// BwdDataArgs::gdirect / BwdWeightArgs::gdirect: where the GEMMs' grad_output
+// tiles come from.  0: packed blocks (pack_grad_output); kGoutNchw: TMA boxes
+// of NCHW grad_output (64 pixels contiguous per Co row, MN-major for the
+// data GEMM, K-major for the weight GEMM); kGoutNhwc: TMA boxes of
+// channels-last grad_output (64 Co contiguous per pixel row: the packed
+// block's layout, so the packed operand descriptors apply).
+enum : int { kGoutNchw = 1, kGoutNhwc = 2 };
+
 struct BwdDataArgs {
-  TmaDesc gmap;         // grad_output as [B][Co][HoWo], box 64 pixels x 64 Co, SW128 (gdirect)
+  TmaDesc gmap;         // grad_output box 64 x 64, SW128: NCHW as [B][Co][HoWo], channels-last
+                        // as [1][totalP][Co] (gdirect)
   TmaDesc xmap;         // packed input [B][H][W][CS], box 16 x 16 pixels x 64 channels, SW128 (tile scatter)
   TmaDesc cmap;         // gcol [B][Ho][Wo][K2*dg*Cgp], box 8 x 8 pixels x 64 channels, SW128 (tile scatter)
   TmaDesc rmap;         // fp32 grad_input accumulator [B][H][W][CS], box 8 x 16 pixels x 32 channels,
                         // SW128 (tile scatter: TMA reductions of its windows)
-  int gdirect;          // A tiles loaded from grad_output by TMA (no packed copy); 16-bit types,
-                        // HoWo % 64 == 0, 16-byte aligned grad_output
+  int gdirect;          // 0, kGoutNchw or kGoutNhwc: A tiles loaded from grad_output by TMA
+                        // (no packed copy); 16-bit types, 16-byte aligned grad_output
   Plan plan;
   unsigned long long* ts;  // optional pipeline timestamps of CTA 0 (DCN_DEBUG_TS), else null
   const void* xt;       // packed NHWC input
@@ -84,7 +93,7 @@ struct BwdDataArgs {
 
 struct BwdWeightArgs {
   TmaDesc gmap;         // as BwdDataArgs::gmap
-  int gdirect;          // A tiles from grad_output by TMA; grad_bias then summed here
+  int gdirect;          // as BwdDataArgs::gdirect; grad_bias then summed here
   float* gb;            // fp32 [Co] grad_bias accumulator (gdirect and bias), else null
   Plan plan;
   unsigned long long* ts;  // optional pipeline timestamps of CTA 0 (DCN_DEBUG_TS), else null
