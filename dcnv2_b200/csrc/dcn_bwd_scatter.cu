@@ -35,25 +35,13 @@ namespace {
 
 constexpr int kThreads = 256;
 
-// {a.x * b.x + c.x, a.y * b.y + c.y} (sm_100 packed f32x2)
-__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
-  unsigned long long r;
-  asm("{\n\t.reg .b64 x, y, z;\n\tmov.b64 x, {%1, %2};\n\tmov.b64 y, {%3, %4};\n\t"
-      "mov.b64 z, {%5, %6};\n\tfma.rn.f32x2 %0, x, y, z;\n\t}"
-      : "=l"(r)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-  return make_float2(__uint_as_float((uint32_t)r), __uint_as_float((uint32_t)(r >> 32)));
-}
+// {a.x * b.x + c.x, a.y * b.y + c.y}: the sm_100 packed f32x2 FMA through the
+// CUDA builtin (operands stay in register pairs; inline PTX packing them with
+// mov.b64 cost extra moves)
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
 
 // 2 x f32 packed multiply (sm_100): {a.x * s, a.y * s}
-__device__ __forceinline__ float2 mul2(float2 a, float s) {
-  unsigned long long r;
-  asm("{\n\t.reg .b64 x, y;\n\tmov.b64 x, {%1, %2};\n\tmov.b64 y, {%3, %3};\n\t"
-      "mul.rn.f32x2 %0, x, y;\n\t}"
-      : "=l"(r)
-      : "f"(a.x), "f"(a.y), "f"(s));
-  return make_float2(__uint_as_float((uint32_t)r), __uint_as_float((uint32_t)(r >> 32)));
-}
+__device__ __forceinline__ float2 mul2(float2 a, float s) { return __fmul2_rn(a, make_float2(s, s)); }
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 3) dcn_bwd_scatter_kernel(const __grid_constant__ BwdDataArgs a) {

@@ -101,15 +101,10 @@ __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wa
 // named barrier of the four epilogue warps
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
-// {a.x * b.x + c.x, a.y * b.y + c.y} (sm_100 packed f32x2)
-__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
-  unsigned long long r;
-  asm("{\n\t.reg .b64 x, y, z;\n\tmov.b64 x, {%1, %2};\n\tmov.b64 y, {%3, %4};\n\t"
-      "mov.b64 z, {%5, %6};\n\tfma.rn.f32x2 %0, x, y, z;\n\t}"
-      : "=l"(r)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-  return make_float2(__uint_as_float((uint32_t)r), __uint_as_float((uint32_t)(r >> 32)));
-}
+// {a.x * b.x + c.x, a.y * b.y + c.y}: the sm_100 packed f32x2 FMA through the
+// CUDA builtin (operands stay in register pairs; inline PTX packing them with
+// mov.b64 cost extra moves)
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
 
 template <int N>
 __device__ __forceinline__ float pick(const float (&v)[N], int i) {

@@ -413,10 +413,9 @@ __device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
       f[2 * i] = x.x;
       f[2 * i + 1] = x.y;
     } else {
-      __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[i]);
-      float2 x = __bfloat1622float2(h);
-      f[2 * i] = x.x;
-      f[2 * i + 1] = x.y;
+      // bf16 is the top half of an f32: two bit operations, no conversion
+      f[2 * i] = __uint_as_float(w[i] << 16);
+      f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
     }
   }
 }
