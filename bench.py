@@ -545,7 +545,8 @@ def config_of(args, wl):
     return {"workload": f"{args.workload}: B={B}/gpu C={C} {H}x{W} Co={Co} {k}x{k} s{s} p{p} "
                         f"d{d} dg{dg}, fwd+bwd", "global_batch": B * args.gpus,
             "parallelism": f"dp{args.gpus}", "l2": "flushed before every step (256 MiB write)",
-            "offset_std_px": off_std, "channels_last": bool(getattr(args, "channels_last", False))}
+            "offset_std_px": off_std, "channels_last": bool(getattr(args, "channels_last", False)),
+            "backward_reuses_packed_input": not getattr(args, "no_reuse", False)}
 
 
 def main():
@@ -557,6 +558,8 @@ def main():
     ap.add_argument("--dtype", default="bf16", choices=list(DTYPES))
     ap.add_argument("--workload", default="readme", choices=list(WORKLOADS) + list(STACKS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reuse", action="store_true",
+                    help="the backward packs the input again instead of reusing the forward's")
     ap.add_argument("--no-fp32", action="store_true",
                     help="skip the float32 step reported beside a 16-bit run")
     ap.add_argument("--channels-last", action="store_true",
@@ -602,9 +605,15 @@ def main():
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
+    reuse = not args.no_reuse
+
     def step(x, off, m, gy):
-        y = _C.dcn_v2_forward(x, w, m, off, b, s, s, p, p, d, d, dg)
-        gi, goff, gm, gw, gb = _C.dcn_v2_backward(x, w, m, off, b, gy, s, s, p, p, d, d, dg)
+        # one workspace for the pair, so the backward reuses the input the forward
+        # packed (what the autograd modules do); --no-reuse packs it twice
+        ws = _C.backward_workspace(x, w, s, s, p, p, d, d, dg) if reuse else None
+        y = _C.dcn_v2_forward(x, w, m, off, b, s, s, p, p, d, d, dg, workspace=ws)
+        gi, goff, gm, gw, gb = _C.dcn_v2_backward(x, w, m, off, b, gy, s, s, p, p, d, d, dg,
+                                                  workspace=ws, input_packed=reuse)
         if world > 1:  # the data-parallel exchange: one bucketed all-reduce
             gw, gb = allreduce_tensors([gw, gb])
         return y, gw, gb
@@ -731,8 +740,10 @@ def main():
         x32, w32, b32, off32, m32, gy32 = make_inputs(wl, torch.float32, dev, seed=rank)
 
         def step32():
-            _C.dcn_v2_forward(x32, w32, m32, off32, b32, s, s, p, p, d, d, dg)
-            gi_, go_, gm_, gw_, gb_ = _C.dcn_v2_backward(x32, w32, m32, off32, b32, gy32, s, s, p, p, d, d, dg)
+            ws = _C.backward_workspace(x32, w32, s, s, p, p, d, d, dg) if reuse else None
+            _C.dcn_v2_forward(x32, w32, m32, off32, b32, s, s, p, p, d, d, dg, workspace=ws)
+            gi_, go_, gm_, gw_, gb_ = _C.dcn_v2_backward(x32, w32, m32, off32, b32, gy32, s, s, p, p, d, d, dg,
+                                                         workspace=ws, input_packed=reuse)
             if world > 1:
                 allreduce_tensors([gw_, gb_])
 

@@ -14,6 +14,18 @@ they are not), and the output and the input / offset / mask gradients are
 returned channels-last, so stacked layers pass activations on without layout
 passes.  Otherwise everything is NCHW-contiguous, as in the reference.
 
+Workspace reuse (no counterpart in the reference): the functions take an
+optional keyword ``workspace`` (a uint8 CUDA tensor).  ``dcn_v2_backward(...,
+workspace=ws, input_packed=True)`` reuses the packed input that the forward
+left in ``ws`` (allocate it with ``backward_workspace``, pass it to the forward,
+keep it until the backward); the autograd functions in ``modules`` do this when
+``REUSE_PACKED_INPUT`` is true (the default), holding the backward workspace
+from the forward to the backward.  For inference, ``enable_weight_cache(True)``
+keeps the packed weight of each (weight, version, shape, stream) in a small
+cache and skips its repacking; it keys on ``weight._version``, so in-place
+changes made through ``weight.data`` (which do not bump the version) must be
+followed by ``clear_weight_cache()``.
+
 Errors follow the reference: a CPU tensor raises ``RuntimeError("<name> must be a
 CUDA tensor")`` (com.cu:209-213), a channel mismatch raises ``RuntimeError``
 (com.cu:760-761), and a failing library call raises ``RuntimeError`` with the
@@ -21,6 +33,7 @@ library's message (com.cu:266-270).
 """
 from __future__ import annotations
 
+import collections
 import ctypes
 import os
 from typing import List, Optional
@@ -64,7 +77,7 @@ def _dense(t, nhwc):
     return t.contiguous(memory_format=_CL) if nhwc else t.contiguous()
 
 
-def _desc(input, weight, stride_h, stride_w, pad_h, pad_w, dil_h, dil_w, dg, has_bias, nhwc=False):
+def _desc(input, weight, stride_h, stride_w, pad_h, pad_w, dil_h, dil_w, dg, has_bias, nhwc=False, flags=0):
     if input.dim() != 4 or weight.dim() != 4:
         raise RuntimeError("input and weight must be 4-D (NCHW / [Co, C, kh, kw])")
     B, C, H, W = input.shape
@@ -75,7 +88,7 @@ def _desc(input, weight, stride_h, stride_w, pad_h, pad_w, dil_h, dil_w, dg, has
         raise RuntimeError(f"unsupported dtype {input.dtype}")
     d = _lib.DcnDesc(B, C, H, W, Co, kh, kw, int(stride_h), int(stride_w), int(pad_h), int(pad_w),
                      int(dil_h), int(dil_w), int(dg), _DTYPES[input.dtype], 1 if has_bias else 0,
-                     _lib.DCN_NHWC if nhwc else _lib.DCN_NCHW)
+                     _lib.DCN_NHWC if nhwc else _lib.DCN_NCHW, int(flags))
     Ho, Wo = ctypes.c_int32(), ctypes.c_int32()
     rc = _lib.lib.dcn_output_size(ctypes.byref(d), ctypes.byref(Ho), ctypes.byref(Wo))
     if rc != _lib.DCN_OK:
@@ -106,11 +119,84 @@ def _check(rc):
         raise RuntimeError(f"dcn: {_lib.strerror(rc)}")
 
 
+# backward workspace allocated by the autograd forward and handed to the backward
+REUSE_PACKED_INPUT = os.environ.get("DCN_REUSE_PACKED_INPUT", "1") not in ("", "0")
+
+
+def _workspace(d, backward, device, given):
+    nbytes = (_lib.lib.dcn_backward_workspace_size if backward else _lib.lib.dcn_forward_workspace_size)(
+        ctypes.byref(d))
+    if given is None:
+        return torch.empty((max(nbytes, 256),), dtype=torch.uint8, device=device)
+    if given.dtype != torch.uint8 or not given.is_cuda or given.device != device or not given.is_contiguous():
+        raise RuntimeError(f"workspace must be a contiguous uint8 tensor on {device}")
+    if given.numel() < nbytes:
+        raise RuntimeError(f"workspace has {given.numel()} bytes, {nbytes} needed")
+    return given
+
+
+def backward_workspace(input: torch.Tensor, weight: torch.Tensor, stride_h: int, stride_w: int,
+                       pad_h: int, pad_w: int, dilation_h: int = 1, dilation_w: int = 1,
+                       deformable_groups: int = 1) -> torch.Tensor:
+    """A workspace that serves both the forward and the backward of this problem
+    (dcn_backward_workspace_size bytes): pass it to the forward and, with
+    ``input_packed=True``, to the backward."""
+    d, _, _ = _desc(input, weight, stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w,
+                    deformable_groups, True, _is_nhwc(input))
+    with torch.cuda.device(input.device):
+        return _workspace(d, True, input.device, None)
+
+
+# packed-weight cache for inference (off unless enabled)
+_WCACHE_ON = os.environ.get("DCN_WEIGHT_CACHE", "0") not in ("", "0")
+_WCACHE: "collections.OrderedDict" = collections.OrderedDict()
+_WCACHE_MAX = 16
+
+
+def enable_weight_cache(on: bool = True) -> None:
+    """Turns the inference packed-weight cache on or off (and empties it)."""
+    global _WCACHE_ON
+    _WCACHE_ON = bool(on)
+    _WCACHE.clear()
+
+
+def clear_weight_cache() -> None:
+    _WCACHE.clear()
+
+
+def _cached_forward_ws(d, weight, stream):
+    """(workspace, weight already packed in it) for an inference forward."""
+    key = (weight.device.index, stream, bytes(d), weight.data_ptr(), weight._version)
+    ws = _WCACHE.get(key)
+    if ws is not None:
+        _WCACHE.move_to_end(key)
+        return ws, True
+    ws = _workspace(d, False, weight.device, None)
+    _WCACHE[key] = ws
+    while len(_WCACHE) > _WCACHE_MAX:
+        _WCACHE.popitem(last=False)
+    return ws, False
+
+
+def _forward_ws(d, weight, stream, given, cache_weight):
+    if given is not None:
+        return _workspace(d, False, weight.device, given)
+    if cache_weight and _WCACHE_ON:
+        ws, packed = _cached_forward_ws(d, weight, stream)
+        if packed:
+            d.flags |= _lib.DCN_FLAG_WEIGHT_PACKED
+        return ws
+    return _workspace(d, False, weight.device, None)
+
+
 def dcn_v2_forward(input: torch.Tensor, weight: torch.Tensor, mask: torch.Tensor,
                    offset: torch.Tensor, bias: Optional[torch.Tensor], stride_h: int, stride_w: int,
                    pad_h: int, pad_w: int, dilation_h: int = 1, dilation_w: int = 1,
-                   deformable_groups: int = 1) -> torch.Tensor:
-    """Output [B, Co, Ho, Wo] of modulated deformable convolution (MyDCN_forward)."""
+                   deformable_groups: int = 1, *, workspace: Optional[torch.Tensor] = None,
+                   cache_weight: bool = False) -> torch.Tensor:
+    """Output [B, Co, Ho, Wo] of modulated deformable convolution (MyDCN_forward).
+    ``workspace``: optional caller-owned workspace (see ``backward_workspace``);
+    ``cache_weight``: use the inference packed-weight cache when it is enabled."""
     _check_cuda(input=input, weight=weight, bias=bias, offset=offset, mask=mask)
     nhwc = _is_nhwc(input)
     d, Ho, Wo = _desc(input, weight, stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w,
@@ -126,9 +212,8 @@ def dcn_v2_forward(input: torch.Tensor, weight: torch.Tensor, mask: torch.Tensor
     with torch.cuda.device(input.device):
         out = torch.empty((B, weight.shape[0], Ho, Wo), dtype=dt, device=input.device,
                           memory_format=_CL if nhwc else torch.contiguous_format)
-        nbytes = _lib.lib.dcn_forward_workspace_size(ctypes.byref(d))
-        ws = torch.empty((max(nbytes, 256),), dtype=torch.uint8, device=input.device)
         stream = torch.cuda.current_stream(input.device).cuda_stream
+        ws = _forward_ws(d, weight, stream, workspace, cache_weight)
         _check(_lib.lib.dcn_forward(ctypes.byref(d), _ptr(input), _ptr(weight), _ptr(mask),
                                     _ptr(offset), _ptr(bias), _ptr(out), _ptr(ws), ws.numel(),
                                     ctypes.c_void_p(stream)))
@@ -140,14 +225,18 @@ def dcn_v2_forward(input: torch.Tensor, weight: torch.Tensor, mask: torch.Tensor
 def dcn_v2_backward(input: torch.Tensor, weight: torch.Tensor, mask: torch.Tensor,
                     offset: torch.Tensor, bias: Optional[torch.Tensor], grad_output: torch.Tensor,
                     stride_h: int, stride_w: int, pad_h: int, pad_w: int, dilation_h: int = 1,
-                    dilation_w: int = 1, deformable_groups: int = 1) -> List[torch.Tensor]:
-    """[grad_input, grad_offset, grad_mask, grad_weight, grad_bias] (MyDCN_backward order)."""
+                    dilation_w: int = 1, deformable_groups: int = 1, *,
+                    workspace: Optional[torch.Tensor] = None, input_packed: bool = False) -> List[torch.Tensor]:
+    """[grad_input, grad_offset, grad_mask, grad_weight, grad_bias] (MyDCN_backward order).
+    ``input_packed``: ``workspace`` went through the forward of this input and
+    still holds its packed copy (DCN_FLAG_INPUT_PACKED)."""
     _check_cuda(input=input, weight=weight, bias=bias, offset=offset, mask=mask,
                 grad_output=grad_output)
     has_bias = bias is not None
     nhwc = _is_nhwc(input)
     d, Ho, Wo = _desc(input, weight, stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w,
-                      deformable_groups, True, nhwc)
+                      deformable_groups, True, nhwc,
+                      _lib.DCN_FLAG_INPUT_PACKED if input_packed else 0)
     B, dg, K2 = input.shape[0], deformable_groups, weight.shape[2] * weight.shape[3]
     Co = weight.shape[0]
     dt = input.dtype
@@ -162,8 +251,9 @@ def dcn_v2_backward(input: torch.Tensor, weight: torch.Tensor, mask: torch.Tenso
         gm = torch.empty_like(mask)
         gw = torch.empty_like(weight)
         gb = torch.empty((Co,), dtype=dt, device=input.device)
-        nbytes = _lib.lib.dcn_backward_workspace_size(ctypes.byref(d))
-        ws = torch.empty((max(nbytes, 256),), dtype=torch.uint8, device=input.device)
+        if input_packed and workspace is None:
+            raise RuntimeError("input_packed=True needs the workspace the forward used")
+        ws = _workspace(d, True, input.device, workspace)
         stream = torch.cuda.current_stream(input.device).cuda_stream
         _check(_lib.lib.dcn_backward(ctypes.byref(d), _ptr(input), _ptr(weight), _ptr(mask),
                                      _ptr(offset), _ptr(bias), _ptr(grad_output), _ptr(gi),
@@ -176,7 +266,8 @@ def dcn_v2_backward(input: torch.Tensor, weight: torch.Tensor, mask: torch.Tenso
 
 def dcn_v2_forward_om(input: torch.Tensor, weight: torch.Tensor, offset_mask: torch.Tensor,
                       bias: Optional[torch.Tensor], stride_h: int, stride_w: int, pad_h: int, pad_w: int,
-                      dilation_h: int = 1, dilation_w: int = 1, deformable_groups: int = 1) -> torch.Tensor:
+                      dilation_h: int = 1, dilation_w: int = 1, deformable_groups: int = 1, *,
+                      workspace: Optional[torch.Tensor] = None, cache_weight: bool = False) -> torch.Tensor:
     """Forward fed by the raw predictor output [B, 3*dg*K2, Ho, Wo]: offsets in the
     first 2*dg*K2 channels, mask logits (sigmoid applied in the kernel) in the rest;
     the same result as ``dcn_v2_forward`` with the reference module's chunk / cat /
@@ -195,9 +286,8 @@ def dcn_v2_forward_om(input: torch.Tensor, weight: torch.Tensor, offset_mask: to
     with torch.cuda.device(input.device):
         out = torch.empty((B, weight.shape[0], Ho, Wo), dtype=dt, device=input.device,
                           memory_format=_CL if nhwc else torch.contiguous_format)
-        nbytes = _lib.lib.dcn_forward_workspace_size(ctypes.byref(d))
-        ws = torch.empty((max(nbytes, 256),), dtype=torch.uint8, device=input.device)
         stream = torch.cuda.current_stream(input.device).cuda_stream
+        ws = _forward_ws(d, weight, stream, workspace, cache_weight)
         _check(_lib.lib.dcn_forward_om(ctypes.byref(d), _ptr(input), _ptr(weight), _ptr(offset_mask),
                                        _ptr(bias), _ptr(out), _ptr(ws), ws.numel(), ctypes.c_void_p(stream)))
         if _CHECK:
@@ -208,14 +298,16 @@ def dcn_v2_forward_om(input: torch.Tensor, weight: torch.Tensor, offset_mask: to
 def dcn_v2_backward_om(input: torch.Tensor, weight: torch.Tensor, offset_mask: torch.Tensor,
                        bias: Optional[torch.Tensor], grad_output: torch.Tensor, stride_h: int,
                        stride_w: int, pad_h: int, pad_w: int, dilation_h: int = 1, dilation_w: int = 1,
-                       deformable_groups: int = 1) -> List[torch.Tensor]:
+                       deformable_groups: int = 1, *, workspace: Optional[torch.Tensor] = None,
+                       input_packed: bool = False) -> List[torch.Tensor]:
     """[grad_input, grad_offset_mask, grad_weight, grad_bias] of ``dcn_v2_forward_om``;
     grad_offset_mask holds the offset gradients and the mask-logit gradients."""
     _check_cuda(input=input, weight=weight, bias=bias, offset_mask=offset_mask, grad_output=grad_output)
     has_bias = bias is not None
     nhwc = _is_nhwc(input)
     d, Ho, Wo = _desc(input, weight, stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w,
-                      deformable_groups, True, nhwc)
+                      deformable_groups, True, nhwc,
+                      _lib.DCN_FLAG_INPUT_PACKED if input_packed else 0)
     B, dg, K2 = input.shape[0], deformable_groups, weight.shape[2] * weight.shape[3]
     Co = weight.shape[0]
     dt = input.dtype
@@ -228,8 +320,9 @@ def dcn_v2_backward_om(input: torch.Tensor, weight: torch.Tensor, offset_mask: t
         gom = torch.empty_like(offset_mask)
         gw = torch.empty_like(weight)
         gb = torch.empty((Co,), dtype=dt, device=input.device)
-        nbytes = _lib.lib.dcn_backward_workspace_size(ctypes.byref(d))
-        ws = torch.empty((max(nbytes, 256),), dtype=torch.uint8, device=input.device)
+        if input_packed and workspace is None:
+            raise RuntimeError("input_packed=True needs the workspace the forward used")
+        ws = _workspace(d, True, input.device, workspace)
         stream = torch.cuda.current_stream(input.device).cuda_stream
         _check(_lib.lib.dcn_backward_om(ctypes.byref(d), _ptr(input), _ptr(weight), _ptr(offset_mask),
                                         _ptr(bias), _ptr(grad_output), _ptr(gi), _ptr(gom), _ptr(gw),

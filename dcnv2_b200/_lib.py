@@ -13,6 +13,8 @@ LIB_PATH = os.path.join(_HERE, "libdcn_b200.so")
 
 DCN_F32, DCN_F16, DCN_BF16 = 0, 1, 2
 DCN_NCHW, DCN_NHWC = 0, 1
+# dcn_desc.flags bits
+DCN_FLAG_INPUT_PACKED, DCN_FLAG_WEIGHT_PACKED = 1, 2
 DCN_OK = 0
 DCN_E_SCRATCH_LIMIT = -7
 NOALLOC_SCRATCH_BYTES = 48 << 20
@@ -42,7 +44,7 @@ class DcnDesc(ctypes.Structure):
 
     _fields_ = [(n, ctypes.c_int32) for n in (
         "B", "C", "H", "W", "Co", "kh", "kw", "sh", "sw", "ph", "pw", "dh", "dw", "dg",
-        "dtype", "has_bias", "layout")]
+        "dtype", "has_bias", "layout", "flags")]
 
 
 class TraceEntry(ctypes.Structure):

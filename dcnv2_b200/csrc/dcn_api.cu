@@ -273,6 +273,7 @@ int make_plan(const dcn_desc* d, Plan* p, int num_sms) {
     return DCN_E_INVALID;
   if (d->dtype != DCN_F32 && d->dtype != DCN_F16 && d->dtype != DCN_BF16) return DCN_E_INVALID;
   if (d->layout != DCN_NCHW && d->layout != DCN_NHWC) return DCN_E_INVALID;
+  if ((d->flags & ~(DCN_FLAG_INPUT_PACKED | DCN_FLAG_WEIGHT_PACKED)) != 0) return DCN_E_INVALID;
   p->B = d->B; p->C = d->C; p->H = d->H; p->W = d->W; p->Co = d->Co;
   p->kh = d->kh; p->kw = d->kw; p->sh = d->sh; p->sw = d->sw; p->ph = d->ph; p->pw = d->pw;
   p->dh = d->dh; p->dw = d->dw; p->dg = d->dg; p->dtype = d->dtype; p->has_bias = d->has_bias;
@@ -428,7 +429,7 @@ static int forward_impl(const dcn_desc* d, const void* input, const void* weight
     TraceScope ts(TR_PACK_INPUT, s);
     if ((rc = launch_pack_input(P, input, ws + P.off_x, nullptr, status, s)) != DCN_OK) return rc;
   }
-  {
+  if (!(d->flags & DCN_FLAG_WEIGHT_PACKED)) {
     TraceScope ts(TR_PACK_WEIGHT_FWD, s);
     if ((rc = launch_pack_weight_fwd(P, weight, ws + P.off_wf, s)) != DCN_OK) return rc;
   }
@@ -500,15 +501,20 @@ static int backward_impl(const dcn_desc* d, const void* input, const void* weigh
       return launch_finish_grad_input(P, gxn, grad_input, s);
     return DCN_OK;
   }
-  {
+  const bool packed = (d->flags & DCN_FLAG_INPUT_PACKED) != 0;
+  if (!packed) {
     // the input pack also clears the status word and the grad_input accumulator
     TraceScope ts(TR_PACK_INPUT, s);
     if ((rc = launch_pack_input(P, input, ws + P.off_x, gxn, status, s)) != DCN_OK) return rc;
   }
   {
     TraceScope ts(TR_PACK_WEIGHT_BWD, s);
-    // ... and the weight pack the gw and gb accumulators (contiguous)
-    if ((rc = launch_pack_weight_bwd(P, weight, ws + P.off_wd, gw, P.bwd_bytes - P.off_gw, s)) != DCN_OK)
+    // ... and the weight pack the gw and gb accumulators (contiguous); with the
+    // forward's packed input reused it clears the grad_input accumulator (just
+    // before gw) and the status word too
+    uint8_t* z0 = ws + (packed ? P.off_gx : P.off_gw);
+    if ((rc = launch_pack_weight_bwd(P, weight, ws + P.off_wd, reinterpret_cast<float*>(z0),
+                                     P.bwd_bytes - (size_t)(z0 - ws), packed ? status : nullptr, s)) != DCN_OK)
       return rc;
   }
   // 16-bit grad_output is read by the GEMMs directly (TMA tiles of 64 pixels x

@@ -134,9 +134,9 @@ int launch_pack_input(const Plan& p, const void* x, void* xt, float* zero_acc, i
                       cudaStream_t s);
 int launch_pack_weight_fwd(const Plan& p, const void* w, uint8_t* wpk, cudaStream_t s);
 // W -> backward-data B tiles; also zeroes `zero_bytes` (a multiple of 16) at
-// `zero_acc` when it is not null.
+// `zero_acc` when it is not null, and the status word when `status` is not null.
 int launch_pack_weight_bwd(const Plan& p, const void* w, uint8_t* wpk, float* zero_acc, size_t zero_bytes,
-                           cudaStream_t s);
+                           int* status, cudaStream_t s);
 int launch_pack_gout(const Plan& p, const void* gout, uint8_t* gpk, float* gb, int vec,
                      cudaStream_t s);
 int launch_finish_grad_input(const Plan& p, const float* gx_nhwc, void* gx, cudaStream_t s);

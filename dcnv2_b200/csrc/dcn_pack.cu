@@ -146,8 +146,10 @@ __global__ void pack_weight_fwd_kernel(const T* __restrict__ w, uint8_t* __restr
 // accumulators.
 template <typename T>
 __global__ void pack_weight_bwd_kernel(const T* __restrict__ w, uint8_t* __restrict__ wpk,
-                                       const Plan P, float4* __restrict__ zacc, long long nz4) {
+                                       const Plan P, float4* __restrict__ zacc, long long nz4,
+                                       int* __restrict__ status) {
   pdl_wait();
+  if (status != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *status = 0;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < nz4;
        i += (long long)gridDim.x * blockDim.x)
     zacc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -639,13 +641,13 @@ int launch_pack_weight_fwd(const Plan& P, const void* w, uint8_t* wpk, cudaStrea
 }
 
 int launch_pack_weight_bwd(const Plan& P, const void* w, uint8_t* wpk, float* zero_acc, size_t zero_bytes,
-                           cudaStream_t s) {
+                           int* status, cudaStream_t s) {
   const long long n = (long long)P.gnU * P.nKo * P.gNC * 8;
   if (zero_bytes % 16 != 0 || ((uintptr_t)zero_acc & 15u) != 0) return DCN_E_UNSUPPORTED;
   const long long nz4 = zero_acc ? (long long)(zero_bytes / 16) : 0;
   return dispatch(P.dtype, [&](auto tag) {
     using T = decltype(tag);
-    return launch_k(pack_weight_bwd_kernel<T>, dim3(grid_for(n > nz4 ? n : nz4, 256)), dim3(256), 0, s, static_cast<const T*>(w), wpk, P, reinterpret_cast<float4*>(zero_acc), nz4);
+    return launch_k(pack_weight_bwd_kernel<T>, dim3(grid_for(n > nz4 ? n : nz4, 256)), dim3(256), 0, s, static_cast<const T*>(w), wpk, P, reinterpret_cast<float4*>(zero_acc), nz4, status);
   });
 }
 

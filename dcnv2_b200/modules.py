@@ -19,6 +19,18 @@ from torch.nn.modules.utils import _pair
 from . import _C
 
 
+def _forward_workspace(ctx, input, weight):
+    """Workspace for an autograd forward: the backward's, allocated now and kept
+    on ctx, so that the backward reuses the input the forward packed into it
+    (DCN_FLAG_INPUT_PACKED); None (a fresh forward-only workspace per call) when
+    the reuse is switched off."""
+    if _C.REUSE_PACKED_INPUT:
+        return _C.backward_workspace(input, weight, ctx.stride[0], ctx.stride[1], ctx.padding[0],
+                                     ctx.padding[1], ctx.dilation[0], ctx.dilation[1],
+                                     ctx.deformable_groups)
+    return None
+
+
 class _DCNv2(Function):
     """Autograd glue (dcn_v2_mm.py:15-53); argument order input, weight, mask, offset, bias."""
 
@@ -29,9 +41,11 @@ class _DCNv2(Function):
         ctx.padding = _pair(padding)
         ctx.dilation = _pair(dilation)
         ctx.deformable_groups = int(deformable_groups)
+        ws = _forward_workspace(ctx, input, weight)
         output = _C.dcn_v2_forward(input, weight, mask, offset, bias, ctx.stride[0], ctx.stride[1],
                                    ctx.padding[0], ctx.padding[1], ctx.dilation[0],
-                                   ctx.dilation[1], ctx.deformable_groups)
+                                   ctx.dilation[1], ctx.deformable_groups, workspace=ws)
+        ctx.ws = ws
         ctx.save_for_backward(input, weight, mask, offset, bias)
         return output
 
@@ -39,10 +53,11 @@ class _DCNv2(Function):
     @once_differentiable
     def backward(ctx, grad_output):
         input, weight, mask, offset, bias = ctx.saved_tensors
+        ws, ctx.ws = ctx.ws, None
         grad_input, grad_offset, grad_mask, grad_weight, grad_bias = _C.dcn_v2_backward(
             input, weight, mask, offset, bias, grad_output, ctx.stride[0], ctx.stride[1],
             ctx.padding[0], ctx.padding[1], ctx.dilation[0], ctx.dilation[1],
-            ctx.deformable_groups)
+            ctx.deformable_groups, workspace=ws, input_packed=ws is not None)
         return (grad_input, grad_weight, grad_mask, grad_offset, grad_bias, None, None, None, None)
 
 
@@ -61,9 +76,11 @@ class _DCNv2OM(Function):
         ctx.padding = _pair(padding)
         ctx.dilation = _pair(dilation)
         ctx.deformable_groups = int(deformable_groups)
+        ws = _forward_workspace(ctx, input, weight)
         output = _C.dcn_v2_forward_om(input, weight, offset_mask, bias, ctx.stride[0], ctx.stride[1],
                                       ctx.padding[0], ctx.padding[1], ctx.dilation[0], ctx.dilation[1],
-                                      ctx.deformable_groups)
+                                      ctx.deformable_groups, workspace=ws)
+        ctx.ws = ws
         ctx.save_for_backward(input, weight, offset_mask, bias)
         return output
 
@@ -71,9 +88,11 @@ class _DCNv2OM(Function):
     @once_differentiable
     def backward(ctx, grad_output):
         input, weight, offset_mask, bias = ctx.saved_tensors
+        ws, ctx.ws = ctx.ws, None
         grad_input, grad_om, grad_weight, grad_bias = _C.dcn_v2_backward_om(
             input, weight, offset_mask, bias, grad_output, ctx.stride[0], ctx.stride[1],
-            ctx.padding[0], ctx.padding[1], ctx.dilation[0], ctx.dilation[1], ctx.deformable_groups)
+            ctx.padding[0], ctx.padding[1], ctx.dilation[0], ctx.dilation[1], ctx.deformable_groups,
+            workspace=ws, input_packed=ws is not None)
         return (grad_input, grad_weight, grad_om, grad_bias, None, None, None, None)
 
 
@@ -109,6 +128,11 @@ class DCNv2(nn.Module):
         k2 = self.kernel_size[0] * self.kernel_size[1]
         assert 2 * self.deformable_groups * k2 == offset.shape[1]
         assert self.deformable_groups * k2 == mask.shape[1]
+        if not torch.is_grad_enabled():
+            # inference: no autograd record, and the packed-weight cache when enabled
+            return _C.dcn_v2_forward(input, self.weight, mask, offset, self.bias, self.stride[0],
+                                     self.stride[1], self.padding[0], self.padding[1], self.dilation[0],
+                                     self.dilation[1], self.deformable_groups, cache_weight=True)
         return dcn_v2_conv(input, self.weight, mask, offset, self.bias, self.stride, self.padding,
                            self.dilation, self.deformable_groups)
 
@@ -134,5 +158,9 @@ class DCN(DCNv2):
         # the predictor's output goes to the operator as it is: the reference's
         # chunk / cat / sigmoid (dcn_v2_mm.py:133-137) happen inside the kernels
         out = self.conv_offset_mask(input)
+        if not torch.is_grad_enabled():
+            return _C.dcn_v2_forward_om(input, self.weight, out, self.bias, self.stride[0], self.stride[1],
+                                        self.padding[0], self.padding[1], self.dilation[0],
+                                        self.dilation[1], self.deformable_groups, cache_weight=True)
         return dcn_v2_conv_om(input, self.weight, out, self.bias, self.stride, self.padding,
                               self.dilation, self.deformable_groups)

@@ -84,7 +84,24 @@ typedef struct dcn_desc {
   int32_t dtype;      /* enum dcn_dtype */
   int32_t has_bias;   /* 0: bias pointer ignored / grad_bias not written */
   int32_t layout;     /* enum dcn_layout; 0 (NCHW) in a zero-initialised descriptor */
+  int32_t flags;      /* DCN_FLAG_* bits; 0 in a zero-initialised descriptor */
 } dcn_desc;
+
+/* dcn_desc.flags.  Both let a caller that keeps one workspace across calls skip
+ * a packing pass whose result is already in it (no counterpart in the
+ * reference, which re-derives everything per call).
+ *
+ * DCN_FLAG_INPUT_PACKED (dcn_backward, dcn_backward_om): `workspace` was passed,
+ *   with the same descriptor and `input`, to the dcn_forward / dcn_forward_om
+ *   call that this backward follows, and nothing has written to it since: the
+ *   packed input it holds is reused instead of packing `input` again.  The
+ *   workspace must then have dcn_backward_workspace_size bytes for both calls
+ *   (the two layouts share the packed-input region).
+ * DCN_FLAG_WEIGHT_PACKED (dcn_forward, dcn_forward_om): `workspace` holds the
+ *   packed weight of an earlier forward call with the same descriptor and the
+ *   same `weight` contents: the weight pack is skipped. */
+#define DCN_FLAG_INPUT_PACKED 1
+#define DCN_FLAG_WEIGHT_PACKED 2
 
 /* Validates `d` and writes the output spatial size.  DCN_OK or DCN_E_INVALID. */
 DCN_API int dcn_output_size(const dcn_desc* d, int32_t* Ho, int32_t* Wo);

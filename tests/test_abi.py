@@ -46,7 +46,8 @@ def test_output_size_and_workspace():
 
 
 @pytest.mark.parametrize("bad", [dict(C=63, dg=2), dict(kh=0), dict(sh=0), dict(dh=0), dict(dg=0),
-                                 dict(dtype=7), dict(H=1, W=1, ph=0, pw=0), dict(Co=0), dict(layout=2)])
+                                 dict(dtype=7), dict(H=1, W=1, ph=0, pw=0), dict(Co=0), dict(layout=2),
+                                 dict(flags=4), dict(flags=-1)])
 def test_invalid_descriptors(bad):
     d = _desc(**bad)
     ho, wo = ctypes.c_int32(), ctypes.c_int32()
@@ -77,9 +78,9 @@ def test_trace_collect_empty():
 
 
 def test_descriptor_layout_field():
-    """dcn_desc ends with the layout field (17 int32); NCHW and NHWC give the
-    same output size and workspace."""
-    assert ctypes.sizeof(_lib.DcnDesc) == 17 * 4
+    """dcn_desc ends with the layout and flags fields (18 int32); NCHW and NHWC
+    give the same output size and workspace."""
+    assert ctypes.sizeof(_lib.DcnDesc) == 18 * 4
     a, b = _desc(layout=_lib.DCN_NCHW), _desc(layout=_lib.DCN_NHWC)
     assert _lib.lib.dcn_forward_workspace_size(ctypes.byref(a)) == _lib.lib.dcn_forward_workspace_size(ctypes.byref(b))
     assert _lib.lib.dcn_backward_workspace_size(ctypes.byref(a)) == _lib.lib.dcn_backward_workspace_size(ctypes.byref(b))
