@@ -320,7 +320,8 @@ int launch_backward_weight(const BwdWeightArgs& a, cudaStream_t stream) {
   const size_t stageBytes =
       (size_t)P.nsplit * ((size_t)P.wg_mt_per_cta * 128 * 128 +
                           (size_t)P.wg_units_per_set * P.NC * 128);
-  int S = (int)((kBwdSmemBudget - 1024) / stageBytes);
+  // as many stages as the shared memory holds (the work split needs two)
+  int S = (int)((kBwdSmemLimit - 1024) / stageBytes);
   if (S > kMaxStages) S = kMaxStages;
   if (S < 2) return DCN_E_UNSUPPORTED;
   BwdWeightArgs args = a;
