@@ -341,7 +341,7 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_bwd_scatter_tc_kernel(const _
             wpix[c] = (int)(int16_t)(((c < 2 ? e0.x : e0.y) >> (16 * (c & 1))) & 0xffffu);
           // A entry of corner q4: row = window pixel, column = sample
           rem = kNoEntry;
-          {
+          if (!DCN_SKIP(1 << 17)) {
             float bq = 0.f;
             int wp = -1;
 #pragma unroll
@@ -374,6 +374,7 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_bwd_scatter_tc_kernel(const _
           float gcs[2][8];
 #pragma unroll
           for (int jj = 0; jj < 2; ++jj) {
+            if (DCN_SKIP(1 << 16)) { vcs[jj] = make_uint4(0u, 0u, 0u, 0u); continue; }
             const int sl = 2 * q4 + jj;
             uint4 raw[4];
 #pragma unroll
@@ -410,7 +411,7 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_bwd_scatter_tc_kernel(const _
                                  pack2<kBF>(col2[2].x, col2[2].y), pack2<kBF>(col2[3].x, col2[3].y));
           }
           // sampled columns for the weight gradient (B tiles of dcn_bwd_weight)
-          if (pv && a.cols != nullptr) {
+          if (pv && a.cols != nullptr && !DCN_SKIP(1 << 18)) {
             const int crow = pix & 63;
             const int cch = cb / nblk, cblk = cb - cch * nblk;
             const int atom = ((t * P.dg + un.g) * P.nCC + cch) * nblk + cblk;
@@ -444,6 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_bwd_scatter_tc_kernel(const _
           if (lane == 0) mbar_arrive(bempty0 + 8 * bs);
           if (warp == 0 && nch < 260) DCN_TS(3 * nch + 2);
           // per-sample sums over the 4 lanes' channels
+          if (DCN_SKIP(1 << 19)) continue;
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             S[c] += __shfl_xor_sync(0xffffffffu, S[c], 1);

@@ -65,6 +65,31 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread is suspended (issuing nothing)
+// until the phase completes or about `ns` nanoseconds have passed.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint32_t bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Suspend-time hint of the bounded waits below (ns); 0 selects polling with a
+// growing __nanosleep between polls instead.  Measured on the README layer:
+// the same instruction count either way (waiting warps issue little), the tile
+// scatter 183.3 -> 181.5 us with a 20 us hint (the warp resumes as soon as the
+// phase completes instead of at the end of its sleep); the clock and the abort
+// flag are checked after every suspended poll.
+#ifndef DCN_MBAR_SUSPEND_NS
+#define DCN_MBAR_SUSPEND_NS 20000
+#endif
+constexpr uint32_t kMbarSuspendNs = DCN_MBAR_SUSPEND_NS;
+
 // Longest sleep between two failed polls of an mbarrier (ns).  Waiting warps
 // that spin without sleeping took most of the issue slots of the tile scatter
 // (ncu: 142 warp instructions per sample, issue 66% active).
@@ -87,10 +112,14 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
   uint64_t t0 = 0;
   uint32_t ns = 32;
   for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    __nanosleep(ns);
-    if (ns < kMbarMaxSleepNs) ns <<= 1;
-    if ((i & 255u) == 0u) {
+    if (kMbarSuspendNs) {
+      if (mbar_try_wait_suspend(bar, parity, kMbarSuspendNs)) return true;
+    } else {
+      if (mbar_try_wait(bar, parity)) return true;
+      __nanosleep(ns);
+      if (ns < kMbarMaxSleepNs) ns <<= 1;
+    }
+    if (kMbarSuspendNs || (i & 255u) == 0u) {
       if (*abort_flag) return false;
       const uint64_t now = globaltimer();
       if (t0 == 0) {
@@ -117,10 +146,14 @@ __device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, in
   uint64_t t0 = 0;
   uint32_t ns = 32;
   for (uint32_t i = 1;; ++i) {
-    if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
-    __nanosleep(ns);
-    if (ns < kMbarMaxSleepNs) ns <<= 1;
-    if ((i & 255u) == 0u) {
+    if (kMbarSuspendNs) {
+      if (__all_sync(0xffffffffu, mbar_try_wait_suspend(bar, parity, kMbarSuspendNs))) return true;
+    } else {
+      if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+      __nanosleep(ns);
+      if (ns < kMbarMaxSleepNs) ns <<= 1;
+    }
+    if (kMbarSuspendNs || (i & 255u) == 0u) {
       int give_up = 0;
       if (lane == 0) {
         if (*abort_flag) {
