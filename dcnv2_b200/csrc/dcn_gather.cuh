@@ -217,31 +217,33 @@ __device__ __forceinline__ void load_corners_px(const T* __restrict__ xt, const 
   }
 }
 
-// Packed blend for 16-bit inputs: 8 channels, two per FMA (bf16x2 / half2),
-// result already in the operand format.
+// Blend for 16-bit inputs: 8 channels of the four corners, each sample formed
+// in fp32 (two channels per packed f32x2 FMA, weights x mask in fp32) and
+// rounded once to the operand format, as the reference forms the sample in
+// float and rounds it once (com.cu:83-87, 119-148).
 template <typename T>
 __device__ __forceinline__ uint4 blend_packed(const uint4 (&v)[4][1], const float (&w)[4]) {
-  using H2 = typename std::conditional<std::is_same<T, __half>::value, __half2, __nv_bfloat162>::type;
-  H2 w2[4];
+  float2 acc[4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) acc[c] = make_float2(0.f, 0.f);
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    if constexpr (std::is_same<T, __half>::value) w2[i] = __float2half2_rn(w[i]);
-    else w2[i] = __float2bfloat162_rn(w[i]);
-  }
-  uint32_t in[4][4];
+    const uint32_t in[4] = {v[i][0].x, v[i][0].y, v[i][0].z, v[i][0].w};
+    const float2 wi = make_float2(w[i], w[i]);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    in[i][0] = v[i][0].x; in[i][1] = v[i][0].y; in[i][2] = v[i][0].z; in[i][3] = v[i][0].w;
+    for (int c = 0; c < 4; ++c) {
+      float2 x;
+      if constexpr (std::is_same<T, __half>::value) {
+        x = __half22float2(*reinterpret_cast<const __half2*>(&in[c]));
+      } else {
+        x = make_float2(__uint_as_float(in[c] << 16), __uint_as_float(in[c] & 0xffff0000u));
+      }
+      acc[c] = __ffma2_rn(x, wi, acc[c]);
+    }
   }
-  uint32_t out[4];
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    H2 acc = __hmul2(w2[0], *reinterpret_cast<const H2*>(&in[0][c]));
-#pragma unroll
-    for (int i = 1; i < 4; ++i) acc = __hfma2(w2[i], *reinterpret_cast<const H2*>(&in[i][c]), acc);
-    out[c] = *reinterpret_cast<uint32_t*>(&acc);
-  }
-  return make_uint4(out[0], out[1], out[2], out[3]);
+  constexpr int kBF = std::is_same<T, __half>::value ? 0 : 1;
+  return make_uint4(pack2<kBF>(acc[0].x, acc[0].y), pack2<kBF>(acc[1].x, acc[1].y),
+                    pack2<kBF>(acc[2].x, acc[2].y), pack2<kBF>(acc[3].x, acc[3].y));
 }
 
 // Blends and stores one lane's slice (packed math for 16-bit inputs, f32 math
