@@ -424,14 +424,23 @@ static int forward_impl(const dcn_desc* d, const void* input, const void* weight
     return cudaMemsetAsync(status, 0, sizeof(int), s) == cudaSuccess ? DCN_OK : DCN_E_CUDA;
   if (!input || !weight || !mask || !offset || !output) return DCN_E_NULLPTR;
   if (d->has_bias && !bias) return DCN_E_NULLPTR;
-  {
+  const bool wpacked = (d->flags & DCN_FLAG_WEIGHT_PACKED) != 0;
+  const bool fused = !wpacked && !P.nhwc && P.esz == 2 && (P.H * P.W) % 8 == 0 && aligned16(input);
+  if (fused) {
+    // 16-bit NCHW: input and weight packs in one launch (traced as pack_input);
     // the input pack also clears the status word
     TraceScope ts(TR_PACK_INPUT, s);
-    if ((rc = launch_pack_input(P, input, ws + P.off_x, nullptr, status, s)) != DCN_OK) return rc;
-  }
-  if (!(d->flags & DCN_FLAG_WEIGHT_PACKED)) {
-    TraceScope ts(TR_PACK_WEIGHT_FWD, s);
-    if ((rc = launch_pack_weight_fwd(P, weight, ws + P.off_wf, s)) != DCN_OK) return rc;
+    if ((rc = launch_pack_forward(P, input, ws + P.off_x, status, weight, ws + P.off_wf, s)) != DCN_OK) return rc;
+  } else {
+    {
+      // the input pack also clears the status word
+      TraceScope ts(TR_PACK_INPUT, s);
+      if ((rc = launch_pack_input(P, input, ws + P.off_x, nullptr, status, s)) != DCN_OK) return rc;
+    }
+    if (!wpacked) {
+      TraceScope ts(TR_PACK_WEIGHT_FWD, s);
+      if ((rc = launch_pack_weight_fwd(P, weight, ws + P.off_wf, s)) != DCN_OK) return rc;
+    }
   }
   FwdArgs a;
   memset(&a, 0, sizeof(a));
@@ -606,6 +615,11 @@ static int backward_impl(const dcn_desc* d, const void* input, const void* weigh
   study_ts_print("DCN_TSS", dts_s, s);
   study_ts_print("DCN_TSW", dts, s);
 #endif
+  if (!P.nhwc) {
+    // NCHW: both finishing passes in one launch (traced as finish_grad_input)
+    TraceScope ts(TR_FINISH_GRAD_INPUT, s);
+    return launch_finish_grads(P, gxn, grad_input, gw, gb, grad_weight, d->has_bias ? grad_bias : nullptr, s);
+  }
   {
     TraceScope ts(TR_FINISH_GRAD_INPUT, s);
     if ((rc = launch_finish_grad_input(P, gxn, grad_input, s)) != DCN_OK) return rc;

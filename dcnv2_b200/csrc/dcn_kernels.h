@@ -133,6 +133,10 @@ cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
 int launch_pack_input(const Plan& p, const void* x, void* xt, float* zero_acc, int* status,
                       cudaStream_t s);
 int launch_pack_weight_fwd(const Plan& p, const void* w, uint8_t* wpk, cudaStream_t s);
+// 16-bit NCHW input (H*W % 8 == 0, 16-byte aligned) and the forward weight
+// tiles packed by one launch; clears the status word
+int launch_pack_forward(const Plan& p, const void* x, void* xt, int* status, const void* w, uint8_t* wpk,
+                        cudaStream_t s);
 // W -> backward-data B tiles; also zeroes `zero_bytes` (a multiple of 16) at
 // `zero_acc` when it is not null, and the status word when `status` is not null.
 int launch_pack_weight_bwd(const Plan& p, const void* w, uint8_t* wpk, float* zero_acc, size_t zero_bytes,
@@ -140,6 +144,9 @@ int launch_pack_weight_bwd(const Plan& p, const void* w, uint8_t* wpk, float* ze
 int launch_pack_gout(const Plan& p, const void* gout, uint8_t* gpk, float* gb, int vec,
                      cudaStream_t s);
 int launch_finish_grad_input(const Plan& p, const float* gx_nhwc, void* gx, cudaStream_t s);
+// NCHW grad_input and grad_weight / grad_bias finished by one launch
+int launch_finish_grads(const Plan& p, const float* gx_nhwc, void* gx, const float* gw, const float* gb,
+                        void* gw_out, void* gb_out, cudaStream_t s);
 int launch_finish_grad_weight(const Plan& p, const float* gw, const float* gb, void* gw_out,
                               void* gb_out, cudaStream_t s);
 

@@ -109,12 +109,11 @@ __device__ __forceinline__ void write_chunk(uint8_t* tile, size_t lo_ofs, int ro
 // Forward B operand: tile (ct, kc) holds rows co = ct*NT + r, K elements
 // (t, g, cb*64 + e) of W[co][g*Cg + cb*64 + e][t].  One thread per 16-byte chunk.
 template <typename T>
-__global__ void pack_weight_fwd_kernel(const T* __restrict__ w, uint8_t* __restrict__ wpk,
-                                       const Plan P) {
-  pdl_wait();
+__device__ __forceinline__ void pack_weight_fwd_part(const T* __restrict__ w, uint8_t* __restrict__ wpk,
+                                                     const Plan& P, int vb, int vg) {
   const long long nchunks = (long long)P.nCoT * P.nK * P.NT * 8;
-  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < nchunks;
-       idx += (long long)gridDim.x * blockDim.x) {
+  for (long long idx = vb * (long long)blockDim.x + threadIdx.x; idx < nchunks;
+       idx += (long long)vg * blockDim.x) {
     const int chunk = (int)(idx & 7);
     const long long rt = idx >> 3;
     const int r = (int)(rt % P.NT);
@@ -136,6 +135,13 @@ __global__ void pack_weight_fwd_kernel(const T* __restrict__ w, uint8_t* __restr
     uint8_t* tile = wpk + (size_t)(ct * P.nK + kc) * P.wf_tile_bytes;
     write_chunk<T>(tile, (size_t)P.NT * 128, r, chunk, v);
   }
+}
+
+template <typename T>
+__global__ void pack_weight_fwd_kernel(const T* __restrict__ w, uint8_t* __restrict__ wpk,
+                                       const Plan P) {
+  pdl_wait();
+  pack_weight_fwd_part<T>(w, wpk, P, blockIdx.x, gridDim.x);
 }
 
 // Backward-data B operand (W transposed): tile (u, ko) of unit u = (set, cch)
@@ -274,15 +280,13 @@ __global__ void __launch_bounds__(256) pack_gout_kernel(const T* __restrict__ go
 // channels of one group block: 16-byte loads along channels, 16-byte stores
 // along pixels (when `vec`: H*W % 8 == 0 and gx 16-byte aligned).
 template <typename T>
-__global__ void __launch_bounds__(256) finish_grad_input_kernel(const float* __restrict__ gxn,
-                                                                T* __restrict__ gx, int C, int HW,
-                                                                int Cg, int Cgp, int CS, int vec) {
-  pdl_wait();
+__device__ __forceinline__ void finish_grad_input_block(const float* __restrict__ gxn, T* __restrict__ gx, int C,
+                                                        int HW, int Cg, int Cgp, int CS, int vec, int bx, int by,
+                                                        int bz, float (&tile)[64][65]) {
   constexpr int EPV = 16 / (int)sizeof(T);
-  __shared__ float tile[64][65];                      // [pixel][channel]
-  const int b = blockIdx.z;
-  const int d0 = blockIdx.y * 64;
-  const int p0 = blockIdx.x * 64;
+  const int b = bz;
+  const int d0 = by * 64;
+  const int p0 = bx * 64;
   const int g = d0 / Cgp, cb = d0 - g * Cgp;
   const float* src = gxn + (size_t)b * HW * CS + d0;
   const int tid = threadIdx.x;
@@ -315,14 +319,22 @@ __global__ void __launch_bounds__(256) finish_grad_input_kernel(const float* __r
   }
 }
 
-// fp32 [Co][K2][dg][Cgp] -> T [Co][C][K2]; fp32 [Co] -> T [Co]
 template <typename T>
-__global__ void finish_grad_weight_kernel(const float* __restrict__ gw, const float* __restrict__ gb,
-                                          T* __restrict__ gwo, T* __restrict__ gbo, const Plan P) {
+__global__ void __launch_bounds__(256) finish_grad_input_kernel(const float* __restrict__ gxn,
+                                                                T* __restrict__ gx, int C, int HW,
+                                                                int Cg, int Cgp, int CS, int vec) {
   pdl_wait();
+  __shared__ float tile[64][65];                      // [pixel][channel]
+  finish_grad_input_block<T>(gxn, gx, C, HW, Cg, Cgp, CS, vec, blockIdx.x, blockIdx.y, blockIdx.z, tile);
+}
+
+// fp32 [Co][K2][dg][Cgp] -> T [Co][C][K2]; fp32 [Co] -> T [Co]; block vb of vg
+template <typename T>
+__device__ __forceinline__ void finish_grad_weight_part(const float* __restrict__ gw, const float* __restrict__ gb,
+                                                        T* __restrict__ gwo, T* __restrict__ gbo, const Plan& P,
+                                                        int vb, int vg) {
   const long long n = (long long)P.Co * P.C * P.K2;
-  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < n;
-       idx += (long long)gridDim.x * blockDim.x) {
+  for (long long idx = vb * (long long)blockDim.x + threadIdx.x; idx < n; idx += (long long)vg * blockDim.x) {
     const int t = (int)(idx % P.K2);
     const long long r = idx / P.K2;
     const int c = (int)(r % P.C);
@@ -330,6 +342,33 @@ __global__ void finish_grad_weight_kernel(const float* __restrict__ gw, const fl
     const int g = c / P.Cg, cc = c - g * P.Cg;
     gwo[idx] = Elem<T>::from_f(gw[((size_t)co * P.K2 + t) * P.CS + g * P.Cgp + cc]);
     if (gbo != nullptr && idx < P.Co) gbo[idx] = Elem<T>::from_f(gb[idx]);
+  }
+}
+
+template <typename T>
+__global__ void finish_grad_weight_kernel(const float* __restrict__ gw, const float* __restrict__ gb,
+                                          T* __restrict__ gwo, T* __restrict__ gbo, const Plan P) {
+  pdl_wait();
+  finish_grad_weight_part<T>(gw, gb, gwo, gbo, P, blockIdx.x, gridDim.x);
+}
+
+// Both finishing passes in one launch (NCHW): blocks 0 .. nA-1 transpose
+// grad_input tiles (block b = (x, y, z) of the separate kernel's grid
+// (nx, ny, B), x fastest), the rest convert grad_weight / grad_bias.
+template <typename T>
+__global__ void __launch_bounds__(256) finish_grads_kernel(const float* __restrict__ gxn, T* __restrict__ gx,
+                                                           int vec, int nx, int ny, int nA,
+                                                           const float* __restrict__ gw,
+                                                           const float* __restrict__ gb, T* __restrict__ gwo,
+                                                           T* __restrict__ gbo, const Plan P) {
+  pdl_wait();
+  __shared__ float tile[64][65];
+  const int bid = blockIdx.x;
+  if (bid < nA) {
+    const int bx = bid % nx, r = bid / nx;
+    finish_grad_input_block<T>(gxn, gx, P.C, P.H * P.W, P.Cg, P.Cgp, P.CS, vec, bx, r % ny, r / ny, tile);
+  } else {
+    finish_grad_weight_part<T>(gw, gb, gwo, gbo, P, bid - nA, (int)gridDim.x - nA);
   }
 }
 
@@ -358,15 +397,13 @@ __device__ __forceinline__ void transpose8x8_b16(const uint4 (&row)[8], uint4 (&
 // When `acc` is not null the fp32 accumulator of the same layout (the backward's
 // grad_input sums) is zeroed alongside, and `status` (if not null) is cleared.
 template <typename T>
-__global__ void __launch_bounds__(256) pack_input_rt_kernel(const T* __restrict__ x, T* __restrict__ xt,
-                                                            int C, int HW, int Cg, int Cgp, int CS,
-                                                            long long nthr, float* __restrict__ acc,
-                                                            int* __restrict__ status) {
-  pdl_wait();
+__device__ __forceinline__ void pack_input_rt_part(const T* __restrict__ x, T* __restrict__ xt, int C, int HW,
+                                                   int Cg, int Cgp, int CS, long long nthr,
+                                                   float* __restrict__ acc, int* __restrict__ status, int vb,
+                                                   int vg) {
   const int np8 = HW >> 3, nblk = CS >> 6;
-  if (status != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *status = 0;
-  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < nthr;
-       idx += (long long)gridDim.x * blockDim.x) {
+  if (status != nullptr && vb == 0 && threadIdx.x == 0) *status = 0;
+  for (long long idx = vb * (long long)blockDim.x + threadIdx.x; idx < nthr; idx += (long long)vg * blockDim.x) {
     const int q = (int)(idx & 7);
     const long long r1 = idx >> 3;
     const int p8 = (int)(r1 % np8);
@@ -394,6 +431,29 @@ __global__ void __launch_bounds__(256) pack_input_rt_kernel(const T* __restrict_
       }
     }
   }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) pack_input_rt_kernel(const T* __restrict__ x, T* __restrict__ xt,
+                                                            int C, int HW, int Cg, int Cgp, int CS,
+                                                            long long nthr, float* __restrict__ acc,
+                                                            int* __restrict__ status) {
+  pdl_wait();
+  pack_input_rt_part<T>(x, xt, C, HW, Cg, Cgp, CS, nthr, acc, status, blockIdx.x, gridDim.x);
+}
+
+// The forward's input pack (register transpose) and weight pack in one launch:
+// blocks 0 .. nA-1 pack the input, the rest the weight tiles.
+template <typename T>
+__global__ void __launch_bounds__(256) pack_forward_kernel(const T* __restrict__ x, T* __restrict__ xt, int HW,
+                                                           long long nthr, int* __restrict__ status, int nA,
+                                                           const T* __restrict__ w, uint8_t* __restrict__ wpk,
+                                                           const Plan P) {
+  pdl_wait();
+  if ((int)blockIdx.x < nA)
+    pack_input_rt_part<T>(x, xt, P.C, HW, P.Cg, P.Cgp, P.CS, nthr, nullptr, status, blockIdx.x, nA);
+  else
+    pack_weight_fwd_part<T>(w, wpk, P, blockIdx.x - nA, (int)gridDim.x - nA);
 }
 
 // ---------------------------------------------------------------------------
@@ -632,6 +692,25 @@ int launch_pack_input(const Plan& P, const void* x, void* xt, float* zero_acc, i
   });
 }
 
+int launch_pack_forward(const Plan& P, const void* x, void* xt, int* status, const void* w, uint8_t* wpk,
+                        cudaStream_t s) {
+  const int HW = P.H * P.W;
+  const bool rt = !P.nhwc && P.esz == 2 && (HW % 8 == 0) && (((uintptr_t)x & 15u) == 0);
+  if (!rt) return DCN_E_UNSUPPORTED;
+  const long long nthr = (long long)P.B * (HW / 8) * (P.CS / 64) * 8;
+  const long long nA = grid_for(nthr, 256);
+  const long long nw = (long long)P.nCoT * P.nK * P.NT * 8;
+  long long nW = (nw + 255) / 256;
+  if (nW > 148) nW = 148;
+  return dispatch(P.dtype, [&](auto tag) {
+    using T = decltype(tag);
+    if constexpr (sizeof(T) != 2) return cudaErrorInvalidValue;
+    else
+      return launch_k(pack_forward_kernel<T>, dim3((unsigned)(nA + nW)), dim3(256), 0, s, static_cast<const T*>(x),
+                      static_cast<T*>(xt), HW, nthr, status, (int)nA, static_cast<const T*>(w), wpk, P);
+  });
+}
+
 int launch_pack_weight_fwd(const Plan& P, const void* w, uint8_t* wpk, cudaStream_t s) {
   const long long n = (long long)P.nCoT * P.nK * P.NT * 8;
   return dispatch(P.dtype, [&](auto tag) {
@@ -689,6 +768,24 @@ int launch_finish_grad_input(const Plan& P, const float* gxn, void* gx, cudaStre
     using T = decltype(tag);
     return launch_k(finish_grad_input_kernel<T>, dim3(grid), dim3(256), 0, s, gxn, static_cast<T*>(gx), P.C, HW, P.Cg,
                                                      P.Cgp, P.CS, vec);
+  });
+}
+
+int launch_finish_grads(const Plan& P, const float* gxn, void* gx, const float* gw, const float* gb, void* gwo,
+                        void* gbo, cudaStream_t s) {
+  const int HW = P.H * P.W;
+  if (P.nhwc) return DCN_E_UNSUPPORTED;
+  const int vec = (HW % 8 == 0) && (((uintptr_t)gx & 15u) == 0);
+  const long long nx = ceil_div(HW, 64), ny = P.CS / 64;
+  const long long nA = nx * ny * P.B;
+  const long long n = (long long)P.Co * P.C * P.K2;
+  long long nW = (n + 255) / 256;
+  if (nW > 148) nW = 148;
+  if (nA + nW >= (1LL << 31)) return DCN_E_UNSUPPORTED;
+  return dispatch(P.dtype, [&](auto tag) {
+    using T = decltype(tag);
+    return launch_k(finish_grads_kernel<T>, dim3((unsigned)(nA + nW)), dim3(256), 0, s, gxn, static_cast<T*>(gx),
+                    vec, (int)nx, (int)ny, (int)nA, gw, gb, static_cast<T*>(gwo), static_cast<T*>(gbo), P);
   });
 }
 
