@@ -61,8 +61,11 @@ int dcn_forward_noalloc(const dcn_desc* d, const void* input, const void* weight
   const int rc = scratch_address(&scratch);
   if (rc != DCN_OK) return rc;
   // dcn_forward clears the status word and overwrites every byte of packed
-  // input and weight it reads, so nothing left by an earlier call is used.
-  return dcn_forward(d, input, weight, mask, offset, bias, output, scratch,
+  // input and weight it reads, so nothing left by an earlier call is used; the
+  // reuse flags do not apply to the shared scratch and are ignored.
+  dcn_desc dd = *d;
+  dd.flags = 0;
+  return dcn_forward(&dd, input, weight, mask, offset, bias, output, scratch,
                      (size_t)DCN_NOALLOC_SCRATCH_BYTES, stream);
 }
 

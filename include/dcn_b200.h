@@ -99,7 +99,8 @@ typedef struct dcn_desc {
  *   (the two layouts share the packed-input region).
  * DCN_FLAG_WEIGHT_PACKED (dcn_forward, dcn_forward_om): `workspace` holds the
  *   packed weight of an earlier forward call with the same descriptor and the
- *   same `weight` contents: the weight pack is skipped. */
+ *   same `weight` contents: the weight pack is skipped.
+ * dcn_forward_noalloc ignores both flags. */
 #define DCN_FLAG_INPUT_PACKED 1
 #define DCN_FLAG_WEIGHT_PACKED 2
 
