@@ -276,8 +276,8 @@ __global__ void __launch_bounds__(256) pack_gout_kernel(const T* __restrict__ go
   }
 }
 
-// fp32 [B][H*W][dg][Cgp] -> T [B][C][H*W].  One CTA moves 64 pixels x 64
-// channels of one group block: 16-byte loads along channels, 16-byte stores
+// fp32 [B][H*W][dg][Cgp] -> T [B][C][H*W].  One CTA of 256 threads moves 64
+// pixels x 64 channels of one group block: 16-byte loads along channels, 16-byte stores
 // along pixels (when `vec`: H*W % 8 == 0 and gx 16-byte aligned).
 template <typename T>
 __device__ __forceinline__ void finish_grad_input_block(const float* __restrict__ gxn, T* __restrict__ gx, int C,
@@ -290,15 +290,24 @@ __device__ __forceinline__ void finish_grad_input_block(const float* __restrict_
   const int g = d0 / Cgp, cb = d0 - g * Cgp;
   const float* src = gxn + (size_t)b * HW * CS + d0;
   const int tid = threadIdx.x;
-  for (int item = tid; item < 64 * 16; item += 256) {
+  // 256 threads: each loads its four 16-byte pieces before storing any, so the
+  // four loads are in flight together
+  float4 v[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int item = tid + 256 * k;
+    const int p = p0 + (item >> 4);
+    v[k] = p < HW ? *reinterpret_cast<const float4*>(src + (size_t)p * CS + (item & 15) * 4)
+                  : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int item = tid + 256 * k;
     const int pl = item >> 4, cv = item & 15;
-    const int p = p0 + pl;
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (p < HW) v = *reinterpret_cast<const float4*>(src + (size_t)p * CS + cv * 4);
-    tile[pl][cv * 4 + 0] = v.x;
-    tile[pl][cv * 4 + 1] = v.y;
-    tile[pl][cv * 4 + 2] = v.z;
-    tile[pl][cv * 4 + 3] = v.w;
+    tile[pl][cv * 4 + 0] = v[k].x;
+    tile[pl][cv * 4 + 1] = v[k].y;
+    tile[pl][cv * 4 + 2] = v[k].z;
+    tile[pl][cv * 4 + 3] = v[k].w;
   }
   __syncthreads();
   T* dst = gx + (size_t)b * C * HW;
